@@ -1,0 +1,330 @@
+// capi.cu - extern "C" entry points of libftb.so (declared in include/ftb.h).
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "moe_kernels.cuh"
+
+namespace ftb {
+
+int launch_route_topk(const float* logits, int64_t T, int E, int top_k, int mode,
+                      const float* bias, float scaling, int renorm, float* w, int32_t* ids,
+                      cudaStream_t stream);
+int launch_router_gemv(const uint16_t* x, const float* G, int64_t T, int H, int E, float* logits,
+                       cudaStream_t stream);
+
+namespace {
+thread_local char g_last_error[256] = "";
+
+// Carves 256-byte aligned sub-buffers out of a workspace.
+struct Carver {
+  char* base;
+  size_t off = 0;
+  explicit Carver(void* p) : base(static_cast<char*>(p)) {}
+  template <typename T>
+  T* take(int64_t n) {
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off += (size_t)ceil_div((int64_t)(n * (int64_t)sizeof(T)), 256) * 256;
+    return p;
+  }
+};
+
+struct DecodeWs {
+  int32_t* status;
+  __half* x16;
+  float* xscale;
+  int32_t* offsets;
+  int32_t* sorted;
+  int32_t* seg_expert;
+  int32_t* seg_off;
+  int32_t* seg_cnt;
+  int32_t* n_seg;
+  __half* h16;
+  uint16_t* ic3;
+  uint16_t* ic3s;
+  size_t bytes;
+};
+
+DecodeWs carve_decode(void* ws, int64_t T, int H, int I, int64_t E, int top_k, int has_shared) {
+  const int64_t R = T * top_k;
+  const int64_t Rs = R + (has_shared ? T : 0);
+  Carver c(ws);
+  DecodeWs w;
+  w.status = c.take<int32_t>(1);
+  w.x16 = c.take<__half>(T * H);
+  w.xscale = c.take<float>(T);
+  w.offsets = c.take<int32_t>(E + 1);
+  w.sorted = c.take<int32_t>(Rs);
+  w.seg_expert = c.take<int32_t>(E + 1);
+  w.seg_off = c.take<int32_t>(E + 1);
+  w.seg_cnt = c.take<int32_t>(E + 1);
+  w.n_seg = c.take<int32_t>(1);
+  w.h16 = c.take<__half>(Rs * I);
+  w.ic3 = c.take<uint16_t>(R * H);
+  w.ic3s = c.take<uint16_t>(has_shared ? T * H : 1);
+  w.bytes = c.off;
+  return w;
+}
+
+struct AlignWs {
+  int32_t* status;
+  int32_t* offsets;
+  int32_t* sorted;
+  int32_t* padded_off;
+  int32_t* padded_cnt;
+  size_t bytes;
+};
+
+AlignWs carve_align(void* ws, int64_t T, int top_k, int E) {
+  Carver c(ws);
+  AlignWs w;
+  w.status = c.take<int32_t>(1);
+  w.offsets = c.take<int32_t>(E + 1);
+  w.sorted = c.take<int32_t>(T * top_k);
+  w.padded_off = c.take<int32_t>(E);
+  w.padded_cnt = c.take<int32_t>(E);
+  w.bytes = c.off;
+  return w;
+}
+
+bool bank_ok(const ftb_nvfp4_bank* b) {
+  return b && b->gate_up_packed && b->gate_up_scale && b->gate_up_global && b->down_packed &&
+         b->down_scale && b->down_global && aligned16(b->gate_up_packed) &&
+         aligned16(b->down_packed);
+}
+
+BankView view_gu(const ftb_nvfp4_bank* b, const ftb_nvfp4_bank* s) {
+  return BankView{b->gate_up_packed, b->gate_up_scale, b->gate_up_global,
+                  s ? s->gate_up_packed : nullptr, s ? s->gate_up_scale : nullptr,
+                  s ? s->gate_up_global : nullptr};
+}
+BankView view_dn(const ftb_nvfp4_bank* b, const ftb_nvfp4_bank* s) {
+  return BankView{b->down_packed, b->down_scale, b->down_global, s ? s->down_packed : nullptr,
+                  s ? s->down_scale : nullptr, s ? s->down_global : nullptr};
+}
+
+}  // namespace
+
+int cuda_status(cudaError_t err) {
+  if (err == cudaSuccess) return FTB_OK;
+  std::snprintf(g_last_error, sizeof(g_last_error), "%s: %s", cudaGetErrorName(err),
+                cudaGetErrorString(err));
+  return FTB_ERR_CUDA;
+}
+
+int sm_count() {
+  static std::mutex mu;
+  static std::vector<int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  std::lock_guard<std::mutex> lock(mu);
+  if ((int)cache.size() <= dev) cache.resize(dev + 1, 0);
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+static int decode_impl(const uint16_t* x, const ftb_nvfp4_bank* bank, const ftb_nvfp4_bank* shared,
+                       const float* topk_w, const int32_t* topk_ids, int64_t T, int H, int I,
+                       int top_k, float act_limit, uint16_t* out, void* workspace,
+                       size_t workspace_bytes, uint16_t* dbg_ic1, uint16_t* dbg_h,
+                       uint16_t* dbg_ic3, uint16_t* dbg_sic1, uint16_t* dbg_sh,
+                       uint16_t* dbg_sout, cudaStream_t stream) {
+  if (T < 0 || H <= 0 || I <= 0 || top_k < 1) return FTB_ERR_SHAPE;
+  if (H % 128 || I % 128) return FTB_ERR_SHAPE;
+  if (!bank_ok(bank) || (shared && !bank_ok(shared))) return FTB_ERR_ARG;
+  const int64_t E = bank->num_experts;
+  if (E < 1 || E > 1024 || (shared && shared->num_experts < 1)) return FTB_ERR_SHAPE;
+  if (T == 0) return FTB_OK;
+  if (!x || !topk_w || !topk_ids || !out) return FTB_ERR_ARG;
+  if (!aligned16(x) || !aligned16(out)) return FTB_ERR_ALIGN;
+  const int has_shared = shared ? 1 : 0;
+  const DecodeWs need = carve_decode(nullptr, T, H, I, E, top_k, has_shared);
+  if (!workspace || workspace_bytes < need.bytes) return FTB_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return FTB_ERR_ALIGN;
+  const DecodeWs w = carve_decode(workspace, T, H, I, E, top_k, has_shared);
+  const int64_t R = T * top_k;
+
+  int st = cuda_status(cudaMemsetAsync(w.status, 0, sizeof(int32_t), stream));
+  if (st) return st;
+
+  SortParams sp{};
+  sp.ids = topk_ids;
+  sp.R = R;
+  sp.T = T;
+  sp.E = (int)E;
+  sp.top_k = top_k;
+  sp.has_shared = has_shared;
+  sp.block_m = 0;
+  sp.offsets = w.offsets;
+  sp.sorted = w.sorted;
+  sp.seg_expert = w.seg_expert;
+  sp.seg_off = w.seg_off;
+  sp.seg_cnt = w.seg_cnt;
+  sp.n_seg = w.n_seg;
+  sp.status = w.status;
+  sp.x = x;
+  sp.x16 = w.x16;
+  sp.xscale = w.xscale;
+  sp.H = H;
+  st = launch_sort_stage(sp, stream);
+  if (st) return st;
+
+  DecodeParams dp{};
+  dp.gu = view_gu(bank, shared);
+  dp.dn = view_dn(bank, shared);
+  dp.H = H;
+  dp.I = I;
+  dp.E = (int)E;
+  dp.top_k = top_k;
+  dp.T = T;
+  dp.R = R;
+  dp.limit = act_limit;
+  dp.topk_w = topk_w;
+  dp.topk_ids = topk_ids;
+  dp.sorted = w.sorted;
+  dp.seg_expert = w.seg_expert;
+  dp.seg_off = w.seg_off;
+  dp.seg_cnt = w.seg_cnt;
+  dp.n_seg = w.n_seg;
+  dp.x16 = w.x16;
+  dp.xscale = w.xscale;
+  dp.h16 = w.h16;
+  dp.ic3 = w.ic3;
+  dp.ic3s = w.ic3s;
+  dp.out = out;
+  dp.status = w.status;
+  dp.dbg_ic1 = dbg_ic1;
+  dp.dbg_h = dbg_h;
+  dp.dbg_sic1 = dbg_sic1;
+  dp.dbg_sh = dbg_sh;
+  dp.has_shared = has_shared;
+  st = launch_decode_gemvs(dp, stream);
+  if (st) return st;
+  if (dbg_ic3) {
+    st = cuda_status(cudaMemcpyAsync(dbg_ic3, w.ic3, (size_t)R * H * 2, cudaMemcpyDeviceToDevice,
+                                     stream));
+    if (st) return st;
+  }
+  if (dbg_sout && has_shared) {
+    st = cuda_status(cudaMemcpyAsync(dbg_sout, w.ic3s, (size_t)T * H * 2,
+                                     cudaMemcpyDeviceToDevice, stream));
+    if (st) return st;
+  }
+  return FTB_OK;
+}
+
+}  // namespace ftb
+
+using namespace ftb;
+
+extern "C" {
+
+const char* ftb_status_string(int status) {
+  switch (status) {
+    case FTB_OK: return "ok";
+    case FTB_ERR_SHAPE: return "unsupported or inconsistent shape";
+    case FTB_ERR_ALIGN: return "pointer not aligned (16 B for banks/activations, 256 B workspace)";
+    case FTB_ERR_WORKSPACE: return "workspace missing or too small";
+    case FTB_ERR_CUDA: return "CUDA error";
+    case FTB_ERR_ARG: return "null pointer or bad argument";
+    case FTB_ERR_TIMEOUT: return "device-side wait timed out";
+    case FTB_ERR_NOT_BUILT: return "path not built into this library";
+    default: return "unknown status";
+  }
+}
+
+int ftb_version(void) { return 1; }
+
+const char* ftb_last_cuda_error(void) { return g_last_error; }
+
+int ftb_route_topk(const float* logits, int64_t T, int E, int top_k, int mode, const float* bias,
+                   float scaling, int renorm, float* topk_w, int32_t* topk_ids,
+                   ftb_stream_t stream) {
+  if (T < 0 || E < 1 || E > 1024 || top_k < 1 || top_k > 32 || top_k > E) return FTB_ERR_SHAPE;
+  if (mode != FTB_ROUTE_SOFTMAX && mode != FTB_ROUTE_SIGMOID) return FTB_ERR_ARG;
+  if (T == 0) return FTB_OK;
+  if (!logits || !topk_w || !topk_ids) return FTB_ERR_ARG;
+  return launch_route_topk(logits, T, E, top_k, mode, bias, scaling, renorm, topk_w, topk_ids,
+                           (cudaStream_t)stream);
+}
+
+int ftb_router_gemv(const uint16_t* x, const float* gate_w, int64_t T, int H, int E,
+                    float* logits, ftb_stream_t stream) {
+  if (T < 0 || T > 65535 || H <= 0 || E < 1 || H % 4) return FTB_ERR_SHAPE;
+  if (T == 0) return FTB_OK;
+  if (!x || !gate_w || !logits) return FTB_ERR_ARG;
+  if (!aligned16(gate_w) || (reinterpret_cast<uintptr_t>(x) & 7u)) return FTB_ERR_ALIGN;
+  return launch_router_gemv(x, gate_w, T, H, E, logits, (cudaStream_t)stream);
+}
+
+size_t ftb_moe_align_workspace_bytes(int64_t T, int top_k, int E) {
+  return carve_align(nullptr, T, top_k, E).bytes;
+}
+
+int ftb_moe_align(const int32_t* topk_ids, int64_t T, int top_k, int E, int block_m,
+                  int32_t* sorted_ids, int32_t* expert_ids, int32_t* num_tokens_post_padded,
+                  int32_t* expert_offsets, void* workspace, size_t workspace_bytes,
+                  ftb_stream_t stream) {
+  if (T < 0 || top_k < 1 || E < 1 || E > 1024 || block_m < 1) return FTB_ERR_SHAPE;
+  if (!topk_ids || !sorted_ids || !expert_ids || !num_tokens_post_padded) return FTB_ERR_ARG;
+  const AlignWs need = carve_align(nullptr, T, top_k, E);
+  if (!workspace || workspace_bytes < need.bytes) return FTB_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return FTB_ERR_ALIGN;
+  const AlignWs w = carve_align(workspace, T, top_k, E);
+  cudaStream_t s = (cudaStream_t)stream;
+  int st = cuda_status(cudaMemsetAsync(w.status, 0, sizeof(int32_t), s));
+  if (st) return st;
+  SortParams sp{};
+  sp.ids = topk_ids;
+  sp.R = T * top_k;
+  sp.T = T;
+  sp.E = E;
+  sp.top_k = top_k;
+  sp.block_m = block_m;
+  sp.offsets = w.offsets;
+  sp.sorted = w.sorted;
+  sp.sorted_ids = sorted_ids;
+  sp.expert_ids = expert_ids;
+  sp.ntpp = num_tokens_post_padded;
+  sp.padded_off = w.padded_off;
+  sp.padded_cnt = w.padded_cnt;
+  sp.status = w.status;
+  st = launch_sort_stage(sp, s);
+  if (st) return st;
+  if (expert_offsets)
+    st = cuda_status(cudaMemcpyAsync(expert_offsets, w.offsets, sizeof(int32_t) * (E + 1),
+                                     cudaMemcpyDeviceToDevice, s));
+  return st;
+}
+
+size_t ftb_moe_decode_workspace_bytes(int64_t T, int H, int I, int E, int top_k, int has_shared) {
+  return carve_decode(nullptr, T, H, I, E, top_k, has_shared).bytes;
+}
+
+int ftb_moe_decode(const uint16_t* x, const ftb_nvfp4_bank* bank, const ftb_nvfp4_bank* shared,
+                   const float* topk_w, const int32_t* topk_ids, int64_t T, int H, int I,
+                   int top_k, float act_limit, uint16_t* out, void* workspace,
+                   size_t workspace_bytes, ftb_stream_t stream) {
+  return decode_impl(x, bank, shared, topk_w, topk_ids, T, H, I, top_k, act_limit, out, workspace,
+                     workspace_bytes, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+                     (cudaStream_t)stream);
+}
+
+int ftb_moe_decode_debug(const uint16_t* x, const ftb_nvfp4_bank* bank,
+                         const ftb_nvfp4_bank* shared, const float* topk_w,
+                         const int32_t* topk_ids, int64_t T, int H, int I, int top_k,
+                         float act_limit, uint16_t* out, void* workspace, size_t workspace_bytes,
+                         uint16_t* ic1, uint16_t* h, uint16_t* ic3, uint16_t* shared_ic1,
+                         uint16_t* shared_h, uint16_t* shared_out, ftb_stream_t stream) {
+  return decode_impl(x, bank, shared, topk_w, topk_ids, T, H, I, top_k, act_limit, out, workspace,
+                     workspace_bytes, ic1, h, ic3, shared_ic1, shared_h, shared_out,
+                     (cudaStream_t)stream);
+}
+
+}  // extern "C"

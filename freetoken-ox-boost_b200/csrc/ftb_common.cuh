@@ -1,0 +1,106 @@
+// ftb_common.cuh - shared helpers for the sm_100a NVFP4 MoE kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/ftb.h"
+
+namespace ftb {
+
+constexpr int kWarp = 32;
+
+// Records the CUDA error text for ftb_last_cuda_error() and maps it to a status.
+int cuda_status(cudaError_t err);
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+__host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---------------------------------------------------------------------------------------
+// bf16 / f16 helpers. bf16 values travel as raw uint16_t bits.
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) {
+  return __uint_as_float(static_cast<uint32_t>(b) << 16);
+}
+
+// fp32 -> bf16 bits, round to nearest even (NaN preserved).
+__device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+
+__device__ __forceinline__ float bf16_round(float f) { return bf16_bits_to_f32(f32_to_bf16_bits(f)); }
+
+// ---------------------------------------------------------------------------------------
+// NVFP4 dequantisation in registers.
+// cvt.rn.f16x2.e2m1x2: one byte holding two E2M1 codes -> f16x2 (low nibble -> low half).
+// Both E2M1 values and E2M1 x E4M3 products are exact in f16 (<= 6 significant bits,
+// magnitudes 2^-10 .. 2688).
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ void e2m1x8_to_f16x2x4(uint32_t w, uint32_t (&h)[4]) {
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
+      : "r"(w));
+}
+
+// Two E4M3 bytes (low byte first) -> f16x2.
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint16_t s) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(s));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// Broadcast half 0 (sel=0) or half 1 (sel=1) of an f16x2 to both halves.
+__device__ __forceinline__ uint32_t f16x2_bcast_lo(uint32_t v) { return __byte_perm(v, v, 0x1010); }
+__device__ __forceinline__ uint32_t f16x2_bcast_hi(uint32_t v) { return __byte_perm(v, v, 0x3232); }
+
+// D(16x8 f32) += A(16x16 f16, row) * B(16x8 f16, col).
+__device__ __forceinline__ void mma_16816_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                              uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// 128-bit read-only streaming load (weights are read once per launch).
+__device__ __forceinline__ uint4 ldg_stream_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ uint4 ldg_v4(const void* p) {
+  return __ldg(reinterpret_cast<const uint4*>(p));
+}
+
+// SwiGLU of the reference: bf16((g * sigmoid(g)) * u), clamps when limit > 0.
+__device__ __forceinline__ float swiglu_f32(float g, float u, float limit) {
+  if (limit > 0.f) {
+    g = fminf(g, limit);
+    u = fminf(fmaxf(u, -limit), limit);
+  }
+  const float sg = 1.0f / (1.0f + expf(-g));
+  return (g * sg) * u;
+}
+
+}  // namespace ftb

@@ -1,0 +1,86 @@
+// moe_kernels.cuh - parameter blocks and launchers shared by the NVFP4 MoE kernels.
+#pragma once
+
+#include "ftb_common.cuh"
+
+namespace ftb {
+
+// Bits of the device status word (workspace), OR-ed by kernels.
+constexpr int kStatusBadId = 1;         // a top-k id outside [0, E): route skipped
+constexpr int kStatusF16Overflow = 2;   // |activation| >= 65504 met on the f16 MMA operand
+
+struct SortParams {
+  const int32_t* ids;  // [R] flat topk ids
+  int64_t R;           // T * top_k
+  int64_t T;
+  int E;
+  int top_k;
+  int has_shared;
+  int block_m;         // > 0: also emit the padded (moe_align) outputs
+  // outputs (decode segment table); seg_expert may be null
+  int32_t* offsets;    // [E+1] unpadded, required
+  int32_t* sorted;     // [R (+T)] route ids sorted by expert; shared routes appended as R+t
+  int32_t* seg_expert; // [E+1] active experts ascending, shared marker E last
+  int32_t* seg_off;    // [E+1]
+  int32_t* seg_cnt;    // [E+1]
+  int32_t* n_seg;      // [1]
+  // align outputs (block_m > 0)
+  int32_t* sorted_ids;
+  int32_t* expert_ids;
+  int32_t* ntpp;
+  int32_t* padded_off;  // [E] scratch
+  int32_t* padded_cnt;  // [E] scratch
+  int32_t* status;
+  // activation staging (x16 == null: no staging blocks)
+  const uint16_t* x;    // [T, H] bf16
+  __half* x16;          // [T, H]
+  float* xscale;        // [T] 2^s
+  int H;
+};
+
+size_t sort_smem_bytes(int E);
+int launch_sort_stage(const SortParams& P, cudaStream_t stream);
+
+// One NVFP4 matrix family (gate_up or down) of the routed bank plus the shared expert.
+struct BankView {
+  const uint8_t* packed;
+  const uint8_t* scale;
+  const uint16_t* global;
+  const uint8_t* s_packed;   // shared expert (may be null)
+  const uint8_t* s_scale;
+  const uint16_t* s_global;
+};
+
+struct DecodeParams {
+  BankView gu, dn;
+  int H, I, E, top_k;
+  int64_t T, R;
+  float limit;
+  const float* topk_w;     // [R]
+  const int32_t* topk_ids; // [R]
+  // sort results
+  const int32_t* sorted;
+  const int32_t* seg_expert;
+  const int32_t* seg_off;
+  const int32_t* seg_cnt;
+  const int32_t* n_seg;
+  // staged activations
+  const __half* x16;
+  const float* xscale;
+  // intermediates
+  __half* h16;             // [(R+T), I] sorted order
+  uint16_t* ic3;           // [R, H] route order
+  uint16_t* ic3s;          // [T, H] shared expert output
+  uint16_t* out;           // [T, H]
+  int32_t* status;
+  // optional debug copies (route order)
+  uint16_t* dbg_ic1;       // [R, 2I]
+  uint16_t* dbg_h;         // [R, I]
+  uint16_t* dbg_sic1;      // [T, 2I]
+  uint16_t* dbg_sh;        // [T, I]
+  int has_shared;
+};
+
+int launch_decode_gemvs(const DecodeParams& P, cudaStream_t stream);
+
+}  // namespace ftb

@@ -1,0 +1,255 @@
+// moe_sort.cu - deterministic token->expert permutation and activation staging.
+//
+// One launch does both jobs of the layer's "front":
+//   block 0      stable counting sort of the T*top_k routes by expert (ties by route index),
+//                the per-expert segment table the GEMV kernels walk, and (align mode) the
+//                BLOCK_M-padded sorted_ids / expert_ids of moe_align_block_size;
+//   blocks 1..T  one token each: bf16 row -> f16 row scaled by 2^-s (s from the row's max
+//                exponent so that max|x|*2^-s lies in [2^14, 2^15): the f16 tensor-core
+//                operand is then exact for every element within 2^-31 of the row max).
+//
+// The sort is single-CTA: 32 warps each own a contiguous chunk of routes; __match_any_sync
+// ranks equal experts inside a 32-route group, so the result is the same on every run
+// (no atomics decide positions).
+#include "ftb_common.cuh"
+#include "moe_kernels.cuh"
+
+namespace ftb {
+
+namespace {
+
+constexpr int kSortThreads = 1024;
+constexpr int kSortWarps = kSortThreads / kWarp;
+
+// Exclusive block-wide scan of one value per thread (blockDim.x == 1024). Returns the
+// exclusive prefix; *total receives the sum over the block.
+__device__ int block_exclusive_scan(int v, int* sm_warp, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += n;
+  }
+  if (lane == 31) sm_warp[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int w = sm_warp[lane];
+    int wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += n;
+    }
+    sm_warp[lane] = wi - w;  // exclusive prefix of warp sums
+    if (lane == 31) sm_warp[32] = wi;
+  }
+  __syncthreads();
+  const int r = sm_warp[warp] + incl - v;
+  *total = sm_warp[32];
+  __syncthreads();
+  return r;
+}
+
+__device__ void sort_block(const SortParams& P, int* hist /* [32][E] */) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int E = P.E;
+  const int64_t R = P.R;
+  __shared__ int sm_scan[33];
+  __shared__ int sm_total;
+
+  for (int i = tid; i < kSortWarps * E; i += kSortThreads) hist[i] = 0;
+  __syncthreads();
+
+  const int64_t chunk = ceil_div(ceil_div(R, kSortWarps), 32) * 32;
+  const int64_t beg = warp * chunk;
+  const int64_t end = (beg + chunk < R) ? beg + chunk : R;
+  const unsigned lt_mask = (1u << lane) - 1u;
+
+  // pass 1: per-warp histograms
+  for (int64_t base = beg; base < end; base += 32) {
+    const int64_t r = base + lane;
+    int e = -1;
+    if (r < end) {
+      e = P.ids[r];
+      if (e < 0 || e >= E) {
+        atomicOr(P.status, kStatusBadId);
+        e = -1;
+      }
+    }
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    if (e >= 0 && lane == __ffs(peers) - 1) hist[warp * E + e] += __popc(peers);
+  }
+  __syncthreads();
+
+  // per-expert totals, unpadded and padded offsets, active-expert compaction
+  const int nchunks = (int)ceil_div(E, kSortThreads);
+  int run_off = 0, run_pad = 0, run_act = 0;
+  for (int c = 0; c < nchunks; ++c) {
+    const int e = c * kSortThreads + tid;
+    int cnt = 0;
+    if (e < E)
+      for (int w = 0; w < kSortWarps; ++w) cnt += hist[w * E + e];
+    const int bm = P.block_m > 0 ? P.block_m : 1;
+    const int pad = (int)ceil_div(cnt, bm) * bm;
+    int tot;
+    const int off = run_off + block_exclusive_scan(cnt, sm_scan, &tot);
+    run_off += tot;
+    const int poff = run_pad + block_exclusive_scan(P.block_m > 0 ? pad : 0, sm_scan, &tot);
+    run_pad += tot;
+    const int aidx = run_act + block_exclusive_scan(cnt > 0 ? 1 : 0, sm_scan, &tot);
+    run_act += tot;
+    if (e < E) {
+      P.offsets[e] = off;
+      if (cnt > 0 && P.seg_expert) {
+        P.seg_expert[aidx] = e;
+        P.seg_off[aidx] = off;
+        P.seg_cnt[aidx] = cnt;
+      }
+      // turn hist[w][e] into the base position of warp w's first route of expert e
+      int run = off;
+      for (int w = 0; w < kSortWarps; ++w) {
+        const int h = hist[w * E + e];
+        hist[w * E + e] = run;
+        run += h;
+      }
+      if (P.block_m > 0) {
+        // the padded copy is written after pass 2 from these
+        P.padded_off[e] = poff;
+        P.padded_cnt[e] = cnt;
+        const int nb = pad / P.block_m;
+        for (int b = 0; b < nb; ++b) P.expert_ids[poff / P.block_m + b] = e;
+      }
+    }
+  }
+  if (tid == 0) {
+    P.offsets[E] = run_off;
+    if (P.ntpp) *P.ntpp = run_pad;
+    if (P.seg_expert) {
+      int n = run_act;
+      if (P.has_shared && P.T > 0) {
+        P.seg_expert[n] = E;  // marker: the shared expert
+        P.seg_off[n] = (int)R;
+        P.seg_cnt[n] = (int)P.T;
+        ++n;
+      }
+      *P.n_seg = n;
+    }
+    sm_total = run_pad;
+  }
+  __syncthreads();
+
+  // pass 2: stable scatter
+  for (int64_t base = beg; base < end; base += 32) {
+    const int64_t r = base + lane;
+    int e = -1;
+    if (r < end) {
+      e = P.ids[r];
+      if (e < 0 || e >= E) e = -1;
+    }
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    int pos = 0;
+    if (e >= 0) pos = hist[warp * E + e] + __popc(peers & lt_mask);
+    __syncwarp();
+    if (e >= 0) {
+      P.sorted[pos] = (int)r;
+      if (lane == __ffs(peers) - 1) hist[warp * E + e] += __popc(peers);
+    }
+    __syncwarp();
+  }
+  if (P.has_shared && P.sorted)
+    for (int64_t t = tid; t < P.T; t += kSortThreads) P.sorted[R + t] = (int)(R + t);
+
+  if (P.block_m > 0) {
+    __syncthreads();
+    // padded sorted_ids: the expert's routes in order, then the sentinel R
+    for (int e = warp; e < E; e += kSortWarps) {
+      const int poff = P.padded_off[e], cnt = P.padded_cnt[e], off = P.offsets[e];
+      const int pad = (int)ceil_div(cnt, P.block_m) * P.block_m;
+      for (int i = lane; i < pad; i += 32) P.sorted_ids[poff + i] = (i < cnt) ? P.sorted[off + i] : (int)R;
+    }
+    // tails up to capacity: sentinel ids, expert -1
+    const int64_t cap = R + (int64_t)E * (P.block_m - 1);
+    for (int64_t i = sm_total + tid; i < cap; i += kSortThreads) P.sorted_ids[i] = (int)R;
+    for (int64_t b = sm_total / P.block_m + tid; b < ceil_div(cap, P.block_m); b += kSortThreads)
+      P.expert_ids[b] = -1;
+  }
+}
+
+__device__ void stage_token(const SortParams& P, int64_t t) {
+  __shared__ float sm_max[32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint4* xr = reinterpret_cast<const uint4*>(P.x + t * P.H);
+  const int nv = P.H / 8;
+  float m = 0.f;
+  for (int i = tid; i < nv; i += blockDim.x) {
+    const uint4 v = xr[i];
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      m = fmaxf(m, fabsf(__uint_as_float(w[j] << 16)));
+      m = fmaxf(m, fabsf(__uint_as_float(w[j] & 0xffff0000u)));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) sm_max[warp] = m;
+  __syncthreads();
+  if (warp == 0) {
+    m = (lane < (int)(blockDim.x >> 5)) ? sm_max[lane] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) sm_max[0] = m;
+  }
+  __syncthreads();
+  m = sm_max[0];
+  int s = 0;
+  if (m > 0.f && m <= 3.0e38f) {
+    int ex;
+    frexpf(m, &ex);  // m = f * 2^ex, f in [0.5, 1)
+    s = ex - 1 - 14;
+    s = s < -100 ? -100 : (s > 100 ? 100 : s);
+  }
+  const float down = exp2f((float)-s);
+  if (tid == 0) P.xscale[t] = exp2f((float)s);
+  uint4* yr = reinterpret_cast<uint4*>(P.x16 + t * P.H);
+  for (int i = tid; i < nv; i += blockDim.x) {
+    const uint4 v = xr[i];
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const __half2 h = __floats2half2_rn(__uint_as_float(w[j] << 16) * down,
+                                          __uint_as_float(w[j] & 0xffff0000u) * down);
+      o[j] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    yr[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+__global__ void __launch_bounds__(kSortThreads) k_sort_stage(SortParams P) {
+  extern __shared__ int hist[];
+  if (blockIdx.x == 0) {
+    sort_block(P, hist);
+  } else {
+    stage_token(P, (int64_t)blockIdx.x - 1);
+  }
+}
+
+}  // namespace
+
+size_t sort_smem_bytes(int E) { return (size_t)kSortWarps * E * sizeof(int); }
+
+int launch_sort_stage(const SortParams& P, cudaStream_t stream) {
+  const size_t smem = sort_smem_bytes(P.E);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(k_sort_stage, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return cuda_status(e);
+  }
+  const int64_t blocks = 1 + (P.x16 ? P.T : 0);
+  k_sort_stage<<<(unsigned)blocks, kSortThreads, smem, stream>>>(P);
+  return cuda_status(cudaGetLastError());
+}
+
+}  // namespace ftb

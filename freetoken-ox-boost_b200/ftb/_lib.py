@@ -1,0 +1,110 @@
+"""ctypes binding of ``libftb.so`` (the sm_100a CUDA library; C ABI in ``include/ftb.h``).
+
+The library is loaded from this package directory only. There is no fallback: if it is
+missing or fails to load, every op raises ``FtbLibraryError``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libftb.so")
+
+FTB_OK = 0
+FTB_ERR_SHAPE = 1
+FTB_ERR_ALIGN = 2
+FTB_ERR_WORKSPACE = 3
+FTB_ERR_CUDA = 4
+FTB_ERR_ARG = 5
+FTB_ERR_TIMEOUT = 6
+FTB_ERR_NOT_BUILT = 7
+
+FTB_ROUTE_SOFTMAX = 0
+FTB_ROUTE_SIGMOID = 1
+
+STATUS_BAD_ID = 1
+STATUS_F16_OVERFLOW = 2
+
+# Every symbol include/ftb.h declares, with (restype, argtypes).
+_vp, _i32, _i64, _f32, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
+
+
+class Nvfp4BankStruct(ctypes.Structure):
+    """``ftb_nvfp4_bank``: device pointers of the six banks + the expert count."""
+    _fields_ = [
+        ("gate_up_packed", _vp),
+        ("gate_up_scale", _vp),
+        ("gate_up_global", _vp),
+        ("down_packed", _vp),
+        ("down_scale", _vp),
+        ("down_global", _vp),
+        ("num_experts", _i64),
+    ]
+
+
+_BP = ctypes.POINTER(Nvfp4BankStruct)
+
+SIGNATURES = {
+    "ftb_status_string": (ctypes.c_char_p, [_i32]),
+    "ftb_version": (_i32, []),
+    "ftb_last_cuda_error": (ctypes.c_char_p, []),
+    "ftb_route_topk": (_i32, [_vp, _i64, _i32, _i32, _i32, _vp, _f32, _i32, _vp, _vp, _vp]),
+    "ftb_router_gemv": (_i32, [_vp, _vp, _i64, _i32, _i32, _vp, _vp]),
+    "ftb_moe_align_workspace_bytes": (_sz, [_i64, _i32, _i32]),
+    "ftb_moe_align": (_i32, [_vp, _i64, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "ftb_moe_decode_workspace_bytes": (_sz, [_i64, _i32, _i32, _i32, _i32, _i32]),
+    "ftb_moe_decode": (_i32, [_vp, _BP, _BP, _vp, _vp, _i64, _i32, _i32, _i32, _f32, _vp, _vp,
+                              _sz, _vp]),
+    "ftb_moe_decode_debug": (_i32, [_vp, _BP, _BP, _vp, _vp, _i64, _i32, _i32, _i32, _f32, _vp,
+                                    _vp, _sz, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+}
+
+
+class FtbLibraryError(RuntimeError):
+    pass
+
+
+class FtbError(RuntimeError):
+    def __init__(self, fn: str, status: int, detail: str = ""):
+        self.status = status
+        super().__init__(f"{fn} failed: status {status} ({status_string(status)}){detail}")
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def load(path: str = LIB_PATH):
+    """Load libftb.so once; raise if it is absent (no CPU or Python fallback exists)."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(path):
+            raise FtbLibraryError(
+                f"{path} is not built; build it with `make -C freetoken-ox-boost_b200/csrc` "
+                "or `python -c 'import __graft_entry__ as g; g.build()'`")
+        lib = ctypes.CDLL(path)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+        return lib
+
+
+def status_string(status: int) -> str:
+    try:
+        return load().ftb_status_string(int(status)).decode()
+    except FtbLibraryError:
+        return "?"
+
+
+def check(fn: str, status: int) -> None:
+    if status != FTB_OK:
+        detail = ""
+        if status == FTB_ERR_CUDA:
+            detail = ": " + load().ftb_last_cuda_error().decode()
+        raise FtbError(fn, status, detail)

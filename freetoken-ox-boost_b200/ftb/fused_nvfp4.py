@@ -1,0 +1,188 @@
+"""NVFP4 fused-MoE entry points on libftb (B200, sm_100a).
+
+Mirrors ``freetoken.moe.fused_nvfp4`` (patches/moe_fused_nvfp4.patch):
+  * ``fused_experts_decode_nvfp4_marlin(x, gu_p, gu_s, gu_g, dn_p, dn_s, dn_g, topk_weights,
+    topk_ids, activation, apply_router_weight_on_input, act_alpha, act_limit)``
+    (decode driver, :136-152) - expert-major HBM-streaming GEMVs;
+  * ``fused_experts_nvfp4(..., num_experts, ...)`` (prefill driver, called at
+    overlay/freetoken/models/glm5_next/experts_resident.py:71-75);
+  * ``moe_align_block_size(topk_ids, block_size, num_experts)`` (:155-156).
+Extension: keyword ``shared=`` adds one always-on NVFP4 shared expert exactly as the model
+block does after ``routed_forward`` (``out + shared_experts(x)``, routed first, bf16;
+patches/models_glm_moe_dsa_moe.patch:203-206).
+
+Activations: ``"silu"`` (plain, act_limit ignored like the reference's silu path) and
+``"swiglu_clamp"`` (silu(min(g, L)) * clamp(u, +-L) with L = act_limit). Errors mirror the
+reference's setup checks: ``ValueError`` for bad shapes/dtypes, ``NotImplementedError`` for
+activations/modes this build does not implement.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from ._runtime import ptr, read_status, require, require_cuda, stream_handle, workspace
+from .banks import Nvfp4Bank
+
+_ACTS = ("silu", "swiglu_clamp")
+
+
+def _act_limit(activation: str, act_limit: float) -> float:
+    if activation not in _ACTS:
+        raise NotImplementedError(f"activation {activation!r} is not built (have {_ACTS})")
+    if activation == "silu":
+        return float("inf")
+    L = float("inf") if act_limit is None else float(act_limit)
+    return L
+
+
+def _check_inputs(x, bank: Nvfp4Bank, topk_weights, topk_ids, shared):
+    dev = require_cuda(x, bank.gate_up_packed, topk_weights, topk_ids)
+    bank.validate()
+    require(x, "hidden_states", torch.bfloat16)
+    T, H = x.shape
+    if H != bank.hidden:
+        raise ValueError(f"hidden {H} != bank hidden {bank.hidden}")
+    require(topk_weights, "topk_weights", torch.float32)
+    require(topk_ids, "topk_ids", torch.int32)
+    if topk_ids.shape != topk_weights.shape or topk_ids.shape[0] != T:
+        raise ValueError("topk_weights/topk_ids must both be [T, top_k]")
+    if shared is not None:
+        shared.validate()
+        if shared.device != dev or shared.hidden != H or shared.inter != bank.inter:
+            raise ValueError("shared expert must match the routed bank's device and shape")
+    return dev
+
+
+def decode_workspace_bytes(T: int, bank: Nvfp4Bank, top_k: int, has_shared: bool) -> int:
+    return int(_lib.load().ftb_moe_decode_workspace_bytes(
+        T, bank.hidden, bank.inter, bank.num_experts, top_k, 1 if has_shared else 0))
+
+
+def moe_decode(x: torch.Tensor, bank: Nvfp4Bank, topk_weights: torch.Tensor,
+               topk_ids: torch.Tensor, *, activation: str = "silu", act_limit: float = 7.0,
+               shared: Nvfp4Bank | None = None, out: torch.Tensor | None = None,
+               debug: bool = False, check_status: bool = False):
+    """Decode layer on a bank object. ``debug=True`` returns (out, intermediates dict)."""
+    dev = _check_inputs(x, bank, topk_weights, topk_ids, shared)
+    limit = _act_limit(activation, act_limit)
+    T, H = x.shape
+    K = topk_ids.shape[1]
+    I = bank.inter
+    if out is None:
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    nbytes = decode_workspace_bytes(T, bank, K, shared is not None)
+    ws = workspace(nbytes, dev)
+    b = bank.struct()
+    s = shared.struct() if shared is not None else None
+    lib = _lib.load()
+    sp = ctypes.byref(s) if s is not None else None
+    if not debug:
+        st = lib.ftb_moe_decode(ptr(x), ctypes.byref(b), sp, ptr(topk_weights), ptr(topk_ids),
+                                T, H, I, K, limit, ptr(out), ptr(ws), ws.numel(),
+                                stream_handle(dev))
+        _lib.check("ftb_moe_decode", st)
+        inter = None
+    else:
+        bf = torch.bfloat16
+        inter = dict(ic1=torch.zeros(T, K, 2 * I, dtype=bf, device=dev),
+                     h=torch.zeros(T, K, I, dtype=bf, device=dev),
+                     ic3=torch.zeros(T, K, H, dtype=bf, device=dev))
+        if shared is not None:
+            inter.update(shared_ic1=torch.zeros(T, 2 * I, dtype=bf, device=dev),
+                         shared_h=torch.zeros(T, I, dtype=bf, device=dev),
+                         shared_out=torch.zeros(T, H, dtype=bf, device=dev))
+        g = inter.get
+        st = lib.ftb_moe_decode_debug(ptr(x), ctypes.byref(b), sp, ptr(topk_weights),
+                                      ptr(topk_ids), T, H, I, K, limit, ptr(out), ptr(ws),
+                                      ws.numel(), ptr(g("ic1")), ptr(g("h")), ptr(g("ic3")),
+                                      ptr(g("shared_ic1")), ptr(g("shared_h")),
+                                      ptr(g("shared_out")), stream_handle(dev))
+        _lib.check("ftb_moe_decode_debug", st)
+    if check_status or debug:
+        status = read_status(ws)
+        if inter is not None:
+            inter["status"] = status
+        if check_status and status & _lib.STATUS_BAD_ID:
+            raise ValueError("topk_ids holds ids outside [0, num_experts)")
+        if check_status and status & _lib.STATUS_F16_OVERFLOW:
+            raise OverflowError("an expert activation exceeded the f16 operand range")
+    return (out, inter) if debug else out
+
+
+def fused_experts_decode_nvfp4_marlin(
+    hidden_states: torch.Tensor,
+    gate_up_packed: torch.Tensor,
+    gate_up_scale: torch.Tensor,
+    gate_up_global: torch.Tensor,
+    down_packed: torch.Tensor,
+    down_scale: torch.Tensor,
+    down_global: torch.Tensor,
+    topk_weights: torch.Tensor,
+    topk_ids: torch.Tensor,
+    activation: str = "silu",
+    apply_router_weight_on_input: bool = False,
+    act_alpha: float = 1.702,
+    act_limit: float = 7.0,
+    *,
+    shared: Nvfp4Bank | None = None,
+) -> torch.Tensor:
+    """Drop-in for the reference decode driver (CUDA-graph safe after one eager call)."""
+    del act_alpha  # only the swigluoai activation uses it; not built
+    if apply_router_weight_on_input:
+        raise NotImplementedError("apply_router_weight_on_input=True is not built")
+    bank = Nvfp4Bank(gate_up_packed, gate_up_scale, gate_up_global, down_packed, down_scale,
+                     down_global)
+    return moe_decode(hidden_states, bank, topk_weights, topk_ids, activation=activation,
+                      act_limit=act_limit, shared=shared)
+
+
+def fused_experts_nvfp4(
+    hidden_states: torch.Tensor,
+    gate_up_packed: torch.Tensor,
+    gate_up_scale: torch.Tensor,
+    gate_up_global: torch.Tensor,
+    down_packed: torch.Tensor,
+    down_scale: torch.Tensor,
+    down_global: torch.Tensor,
+    topk_weights: torch.Tensor,
+    topk_ids: torch.Tensor,
+    num_experts: int,
+    activation: str = "silu",
+    apply_router_weight_on_input: bool = False,
+    act_alpha: float = 1.702,
+    act_limit: float = 7.0,
+    *,
+    shared: Nvfp4Bank | None = None,
+) -> torch.Tensor:
+    """Prefill driver. Same contract and result as the decode driver."""
+    bank = Nvfp4Bank(gate_up_packed, gate_up_scale, gate_up_global, down_packed, down_scale,
+                     down_global)
+    if num_experts != bank.num_experts:
+        raise ValueError(f"num_experts {num_experts} != bank experts {bank.num_experts}")
+    if apply_router_weight_on_input:
+        raise NotImplementedError("apply_router_weight_on_input=True is not built")
+    del act_alpha
+    return moe_decode(hidden_states, bank, topk_weights, topk_ids, activation=activation,
+                      act_limit=act_limit, shared=shared)
+
+
+def moe_align_block_size(topk_ids: torch.Tensor, block_size: int, num_experts: int):
+    """Stable, deterministic permutation: (sorted_ids [cap], expert_ids [cap/bm],
+    num_tokens_post_padded int32 [1]); cap = T*top_k + E*(block_size-1)."""
+    dev = require_cuda(topk_ids)
+    require(topk_ids, "topk_ids", torch.int32)
+    T, K = topk_ids.shape
+    cap = T * K + num_experts * (block_size - 1)
+    sorted_ids = torch.empty(cap, dtype=torch.int32, device=dev)
+    expert_ids = torch.empty((cap + block_size - 1) // block_size, dtype=torch.int32, device=dev)
+    ntpp = torch.empty(1, dtype=torch.int32, device=dev)
+    lib = _lib.load()
+    ws = workspace(lib.ftb_moe_align_workspace_bytes(T, K, num_experts), dev)
+    st = lib.ftb_moe_align(ptr(topk_ids), T, K, num_experts, block_size, ptr(sorted_ids),
+                           ptr(expert_ids), ptr(ntpp), None, ptr(ws), ws.numel(),
+                           stream_handle(dev))
+    _lib.check("ftb_moe_align", st)
+    return sorted_ids, expert_ids, ntpp

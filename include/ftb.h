@@ -1,0 +1,141 @@
+/*
+ * ftb.h - C ABI of the B200 (sm_100a) NVFP4 fused-MoE layer (libftb.so).
+ *
+ * Plain pointers, sizes and a cudaStream_t; every entry point returns an int status
+ * (FTB_OK = 0). No exception crosses the ABI. Device pointers must be on the current device.
+ * Bank layout (the six "native" banks of a resident NVFP4 MoE layer, position == expert id;
+ * overlay/freetoken/models/glm5_next/experts_resident.py:36-41), all C-contiguous:
+ *   gate_up_packed [E, 2I, H/2] u8   byte b of a row = k 2b (low nibble), 2b+1 (high nibble)
+ *   gate_up_scale  [E, 2I, H/16] u8  FP8-E4M3 bits, one per 16 k
+ *   gate_up_global [E, 2I]       fp16 (per-row copy of the expert's global scale)
+ *   down_packed    [E, H, I/2]   u8
+ *   down_scale     [E, H, I/16]  u8 (E4M3)
+ *   down_global    [E, H]        fp16
+ * Rows 0..I-1 of gate_up are the gate projection, rows I..2I-1 the up projection.
+ * Activations and outputs are bf16 bit patterns (uint16_t).
+ */
+#ifndef FTB_H_
+#define FTB_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define FTB_API __attribute__((visibility("default")))
+#else
+#define FTB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* ftb_stream_t; /* == cudaStream_t; NULL = legacy default stream */
+
+enum {
+  FTB_OK = 0,
+  FTB_ERR_SHAPE = 1,      /* unsupported or inconsistent shape */
+  FTB_ERR_ALIGN = 2,      /* a pointer is not aligned as required (16 B for banks/activations) */
+  FTB_ERR_WORKSPACE = 3,  /* workspace NULL or smaller than *_workspace_bytes() */
+  FTB_ERR_CUDA = 4,       /* a CUDA launch or query failed */
+  FTB_ERR_ARG = 5,        /* NULL pointer or bad enum value */
+  FTB_ERR_TIMEOUT = 6,    /* a bounded device-side wait gave up */
+  FTB_ERR_NOT_BUILT = 7   /* this path is not compiled into the library */
+};
+
+/* Router modes of ftb_route_topk. */
+enum {
+  FTB_ROUTE_SOFTMAX = 0, /* fused_topk(..., renormalize): softmax, top-k, renormalise */
+  FTB_ROUTE_SIGMOID = 1  /* fused_route(): sigmoid + bias, top-k, renorm /(sum+1e-20), scale */
+};
+
+typedef struct ftb_nvfp4_bank {
+  const uint8_t* gate_up_packed;
+  const uint8_t* gate_up_scale;
+  const uint16_t* gate_up_global;
+  const uint8_t* down_packed;
+  const uint8_t* down_scale;
+  const uint16_t* down_global;
+  int64_t num_experts;
+} ftb_nvfp4_bank;
+
+FTB_API const char* ftb_status_string(int status);
+FTB_API int ftb_version(void);
+/* Last CUDA error text seen by the library on this thread ("" if none). */
+FTB_API const char* ftb_last_cuda_error(void);
+
+/*
+ * Router top-k over fp32 logits [T, E] -> topk_w fp32 [T, top_k], topk_ids int32 [T, top_k].
+ * SOFTMAX replaces the generic fused_topk(hidden, gating_output, topk, renormalize)
+ *   of OffloadMoELayer.decode_forward (patches/layers_moe.patch:100-113): ids by descending
+ *   logit (lowest index on ties), weights = softmax probabilities, divided by their sum when
+ *   renorm != 0. bias and scaling are ignored.
+ * SIGMOID replaces fused_route(logits, bias, top_k, renorm, scaling)
+ *   (overlay/freetoken/kernel/triton/fused_route.py:65-82): NaN scores -> -FLT_MAX, ids clamped.
+ * Requires 1 <= top_k <= 32, top_k <= E <= 1024.
+ */
+FTB_API int ftb_route_topk(const float* logits, int64_t T, int E, int top_k, int mode,
+                   const float* bias, float scaling, int renorm,
+                   float* topk_w, int32_t* topk_ids, ftb_stream_t stream);
+
+/*
+ * fp32 router GEMV logits[T, E] = float(x[T, H]) . gate_w[E, H]^T, replacing
+ * F.linear(x.float(), gate.float()) (patches/models_glm_moe_dsa_moe.patch:129).
+ */
+FTB_API int ftb_router_gemv(const uint16_t* x, const float* gate_w, int64_t T, int H, int E,
+                    float* logits, ftb_stream_t stream);
+
+/*
+ * Stable token->expert permutation, replacing moe_align_block_size(topk_ids, BLOCK_M,
+ * num_experts) -> (sorted_ids, expert_ids, num_tokens_post_padded)
+ * (call sites patches/moe_fused_ds_fp4.patch:72, patches/moe_fused_nvfp4.patch:155-156).
+ * Routes r = t*top_k + k sorted by expert, ties by r; each expert's run padded to a multiple
+ * of block_m with the sentinel T*top_k. Capacities: sorted_ids >= T*top_k + E*(block_m-1),
+ * expert_ids >= that / block_m (slots past the padded total: sentinel ids, expert -1).
+ * expert_offsets [E+1] (unpadded starts) may be NULL. Out-of-range ids are skipped and set
+ * bit 0 of the device status word (workspace bytes [0, 4)).
+ */
+FTB_API size_t ftb_moe_align_workspace_bytes(int64_t T, int top_k, int E);
+FTB_API int ftb_moe_align(const int32_t* topk_ids, int64_t T, int top_k, int E, int block_m,
+                  int32_t* sorted_ids, int32_t* expert_ids, int32_t* num_tokens_post_padded,
+                  int32_t* expert_offsets, void* workspace, size_t workspace_bytes,
+                  ftb_stream_t stream);
+
+/*
+ * Decode (small T) fused MoE: gate_up GEMV + SwiGLU, down GEMV with routed weight,
+ * fixed-order combine, optional shared-expert add. Replaces
+ * fused_experts_decode_nvfp4_marlin(x, gu_p, gu_s, gu_g, dn_p, dn_s, dn_g, w, ids, activation,
+ * apply_router_weight_on_input=False, act_alpha, act_limit)
+ * (patches/moe_fused_nvfp4.patch:136-152; caller overlay/.../experts_resident.py:79-83),
+ * followed by "out + shared_experts(x)" (patches/models_glm_moe_dsa_moe.patch:203-206)
+ * when shared != NULL (one expert, weight 1.0).
+ * act_limit: +inf = silu(g)*u; finite L > 0 = swiglu_clamp silu(min(g,L))*clamp(u,+-L).
+ * Requires H % 128 == 0, I % 128 == 0, 16-byte aligned pointers.
+ * Workspace: ftb_moe_decode_workspace_bytes() bytes of device memory, 256-byte aligned.
+ * Bytes [0, 4) of every workspace hold the device status word, cleared at each call:
+ * bit 0 = a top-k id outside [0, E) was skipped (its route contributes 0);
+ * bit 1 = an activation reached |v| >= 65504 on the f16 tensor-core operand.
+ */
+FTB_API size_t ftb_moe_decode_workspace_bytes(int64_t T, int H, int I, int E, int top_k, int has_shared);
+FTB_API int ftb_moe_decode(const uint16_t* x, const ftb_nvfp4_bank* bank, const ftb_nvfp4_bank* shared,
+                   const float* topk_w, const int32_t* topk_ids,
+                   int64_t T, int H, int I, int top_k, float act_limit,
+                   uint16_t* out, void* workspace, size_t workspace_bytes, ftb_stream_t stream);
+
+/*
+ * Same layer with its intermediates exposed (parity tests): ic1 bf16 [T, top_k, 2I] (gate_up
+ * outputs x global, before the activation), h bf16 [T, top_k, I] (activation), ic3 bf16
+ * [T, top_k, H] (down outputs x global x routed weight), and for the shared expert
+ * shared_ic1 [T, 2I], shared_h [T, I], shared_out [T, H]. Any of them may be NULL.
+ */
+FTB_API int ftb_moe_decode_debug(const uint16_t* x, const ftb_nvfp4_bank* bank,
+                         const ftb_nvfp4_bank* shared, const float* topk_w,
+                         const int32_t* topk_ids, int64_t T, int H, int I, int top_k,
+                         float act_limit, uint16_t* out, void* workspace, size_t workspace_bytes,
+                         uint16_t* ic1, uint16_t* h, uint16_t* ic3, uint16_t* shared_ic1,
+                         uint16_t* shared_h, uint16_t* shared_out, ftb_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FTB_H_ */

@@ -1,0 +1,66 @@
+"""The C ABI library: it loads without a GPU, exports every symbol include/ftb.h declares,
+and its host-only queries answer (no kernel is launched here)."""
+import os
+import re
+
+import pytest
+
+from ftb import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    names = set()
+    for fn in os.listdir(os.path.join(ROOT, "include")):
+        if fn.endswith(".h"):
+            text = open(os.path.join(ROOT, "include", fn)).read()
+            names |= set(re.findall(r"^FTB_API\s+[\w\s\*]+?\b(ftb_\w+)\s*\(", text, re.M))
+    return sorted(names)
+
+
+def test_header_declares_entry_points():
+    names = declared_symbols()
+    assert "ftb_moe_decode" in names and "ftb_route_topk" in names and len(names) >= 10
+
+
+@pytest.mark.parametrize("name", declared_symbols())
+def test_library_exports_symbol(name):
+    lib = _lib.load()
+    assert hasattr(lib, name)
+    assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_status_strings_and_version():
+    lib = _lib.load()
+    assert lib.ftb_version() >= 1
+    for s in range(8):
+        assert lib.ftb_status_string(s)
+    assert lib.ftb_status_string(0) == b"ok"
+
+
+def test_workspace_queries_host_only():
+    lib = _lib.load()
+    small = lib.ftb_moe_decode_workspace_bytes(4, 2048, 768, 64, 8, 0)
+    big = lib.ftb_moe_decode_workspace_bytes(64, 4096, 1536, 256, 8, 1)
+    assert 0 < small < big
+    assert small % 256 == 0 and big % 256 == 0
+    assert lib.ftb_moe_align_workspace_bytes(4096, 8, 256) >= 4096 * 8 * 4
+
+
+def test_bad_shapes_rejected_before_any_launch():
+    lib = _lib.load()
+    # top_k > 32 and E > 1024 are rejected on the host
+    assert lib.ftb_route_topk(None, 4, 64, 33, 0, None, 1.0, 1, None, None, None) == _lib.FTB_ERR_SHAPE
+    assert lib.ftb_route_topk(None, 4, 2048, 8, 0, None, 1.0, 1, None, None, None) == _lib.FTB_ERR_SHAPE
+    assert lib.ftb_route_topk(None, 4, 64, 8, 7, None, 1.0, 1, None, None, None) == _lib.FTB_ERR_ARG
+    # H not a multiple of 128
+    b = _lib.Nvfp4BankStruct(16, 16, 16, 16, 16, 16, 8)
+    import ctypes
+    st = lib.ftb_moe_decode(None, ctypes.byref(b), None, None, None, 4, 100, 128, 2, 1.0, None,
+                            None, 0, None)
+    assert st == _lib.FTB_ERR_SHAPE
+    # T == 0 is a no-op
+    st = lib.ftb_moe_decode(None, ctypes.byref(b), None, None, None, 0, 256, 128, 2, 1.0, None,
+                            None, 0, None)
+    assert st == _lib.FTB_OK

@@ -51,14 +51,15 @@ DecodeWs carve_decode(void* ws, int64_t T, int H, int I, int64_t E, int top_k, i
   const int64_t Rs = R + (has_shared ? T : 0);
   Carver c(ws);
   DecodeWs w;
-  w.status = c.take<int32_t>(1);
+  w.status = c.take<int32_t>(4);  // [0] status, [1..2] GEMV work counters
   w.x16 = c.take<__half>(T * H);
   w.xscale = c.take<float>(T);
   w.offsets = c.take<int32_t>(E + 1);
   w.sorted = c.take<int32_t>(Rs);
-  w.seg_expert = c.take<int32_t>(E + 1);
-  w.seg_off = c.take<int32_t>(E + 1);
-  w.seg_cnt = c.take<int32_t>(E + 1);
+  const int64_t S = max_segments(R, E, T, has_shared);
+  w.seg_expert = c.take<int32_t>(S);
+  w.seg_off = c.take<int32_t>(S);
+  w.seg_cnt = c.take<int32_t>(S);
   w.n_seg = c.take<int32_t>(1);
   w.h16 = c.take<__half>(Rs * I);
   w.ic3 = c.take<uint16_t>(R * H);
@@ -89,9 +90,11 @@ AlignWs carve_align(void* ws, int64_t T, int top_k, int E) {
 }
 
 bool bank_ok(const ftb_nvfp4_bank* b) {
+  // every bank is a bulk-copy (TMA) source: 16-byte aligned
   return b && b->gate_up_packed && b->gate_up_scale && b->gate_up_global && b->down_packed &&
          b->down_scale && b->down_global && aligned16(b->gate_up_packed) &&
-         aligned16(b->down_packed);
+         aligned16(b->gate_up_scale) && aligned16(b->gate_up_global) &&
+         aligned16(b->down_packed) && aligned16(b->down_scale) && aligned16(b->down_global);
 }
 
 BankView view_gu(const ftb_nvfp4_bank* b, const ftb_nvfp4_bank* s) {
@@ -150,7 +153,7 @@ static int decode_impl(const uint16_t* x, const ftb_nvfp4_bank* bank, const ftb_
   const DecodeWs w = carve_decode(workspace, T, H, I, E, top_k, has_shared);
   const int64_t R = T * top_k;
 
-  int st = cuda_status(cudaMemsetAsync(w.status, 0, sizeof(int32_t), stream));
+  int st = cuda_status(cudaMemsetAsync(w.status, 0, 4 * sizeof(int32_t), stream));
   if (st) return st;
 
   SortParams sp{};
@@ -199,6 +202,7 @@ static int decode_impl(const uint16_t* x, const ftb_nvfp4_bank* bank, const ftb_
   dp.ic3s = w.ic3s;
   dp.out = out;
   dp.status = w.status;
+  dp.work_counter = w.status + 1;
   dp.dbg_ic1 = dbg_ic1;
   dp.dbg_h = dbg_h;
   dp.dbg_sic1 = dbg_sic1;

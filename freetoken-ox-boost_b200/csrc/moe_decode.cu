@@ -308,7 +308,7 @@ int persistent_grid(K kernel, int64_t work) {
 
 }  // namespace
 
-int launch_decode_gemvs(const DecodeParams& P, cudaStream_t stream) {
+int launch_decode_gemvs_ldg(const DecodeParams& P, cudaStream_t stream) {
   constexpr int NT = 2;
   // upper bound on segments: distinct experts hit (<= min(E, R)) plus the shared expert
   const int64_t max_seg = (P.R < P.E ? P.R : P.E) + (P.has_shared ? 1 : 0);
@@ -320,14 +320,22 @@ int launch_decode_gemvs(const DecodeParams& P, cudaStream_t stream) {
   const int g2 = persistent_grid(k_down<NT>, max_seg * (P.H / 32));
   if (g2 < 0) return -g2;
   k_down<NT><<<g2, kThreads, 0, stream>>>(P);
-  st = cuda_status(cudaGetLastError());
-  if (st) return st;
+  return cuda_status(cudaGetLastError());
+}
+
+int launch_combine(const DecodeParams& P, cudaStream_t stream) {
   const int64_t nv = P.T * (P.H / 8);
   int64_t g3 = ceil_div(nv, 256);
   const int64_t cap = (int64_t)sm_count() * 8;
   if (g3 > cap) g3 = cap;
   k_combine<<<(unsigned)g3, 256, 0, stream>>>(P);
   return cuda_status(cudaGetLastError());
+}
+
+int launch_decode_gemvs(const DecodeParams& P, cudaStream_t stream) {
+  const int st = launch_decode_gemvs_tma(P, stream);
+  if (st) return st;
+  return launch_combine(P, stream);
 }
 
 }  // namespace ftb

@@ -8,6 +8,16 @@ namespace ftb {
 // Bits of the device status word (workspace), OR-ed by kernels.
 constexpr int kStatusBadId = 1;         // a top-k id outside [0, E): route skipped
 constexpr int kStatusF16Overflow = 2;   // |activation| >= 65504 met on the f16 MMA operand
+constexpr int kStatusTimeout = 4;       // a bounded device-side wait gave up
+
+// Work segments hold at most this many routes of one expert (one pass of two mma n-tiles);
+// an expert with more routes is split into several segments.
+constexpr int kSegRoutes = 16;
+
+// Capacity of the segment table for R routed routes, E experts and T shared-expert routes.
+__host__ __device__ inline int64_t max_segments(int64_t R, int64_t E, int64_t T, int has_shared) {
+  return (R < E ? R : E) + R / kSegRoutes + 1 + (has_shared ? T / kSegRoutes + 1 : 0);
+}
 
 struct SortParams {
   const int32_t* ids;  // [R] flat topk ids
@@ -20,9 +30,10 @@ struct SortParams {
   // outputs (decode segment table); seg_expert may be null
   int32_t* offsets;    // [E+1] unpadded, required
   int32_t* sorted;     // [R (+T)] route ids sorted by expert; shared routes appended as R+t
-  int32_t* seg_expert; // [E+1] active experts ascending, shared marker E last
-  int32_t* seg_off;    // [E+1]
-  int32_t* seg_cnt;    // [E+1]
+  int32_t* seg_expert; // [max_segments] experts ascending (<= kSegRoutes routes each),
+                       // then the shared expert (marker E)
+  int32_t* seg_off;    // [max_segments] first sorted position
+  int32_t* seg_cnt;    // [max_segments] routes in the segment
   int32_t* n_seg;      // [1]
   // align outputs (block_m > 0)
   int32_t* sorted_ids;
@@ -73,6 +84,7 @@ struct DecodeParams {
   uint16_t* ic3s;          // [T, H] shared expert output
   uint16_t* out;           // [T, H]
   int32_t* status;
+  int* work_counter;       // [2] tile-chunk counters of the gate_up / down launches, zeroed
   // optional debug copies (route order)
   uint16_t* dbg_ic1;       // [R, 2I]
   uint16_t* dbg_h;         // [R, I]
@@ -81,6 +93,12 @@ struct DecodeParams {
   int has_shared;
 };
 
+// gate_up+SwiGLU and down GEMVs, then the combine.
 int launch_decode_gemvs(const DecodeParams& P, cudaStream_t stream);
+// TMA-fed pipelined GEMVs (moe_decode_tma.cu).
+int launch_decode_gemvs_tma(const DecodeParams& P, cudaStream_t stream);
+// Register-streaming GEMVs (moe_decode.cu), kept for A/B timing.
+int launch_decode_gemvs_ldg(const DecodeParams& P, cudaStream_t stream);
+int launch_combine(const DecodeParams& P, cudaStream_t stream);
 
 }  // namespace ftb

@@ -97,14 +97,18 @@ __device__ void sort_block(const SortParams& P, int* hist /* [32][E] */) {
     run_off += tot;
     const int poff = run_pad + block_exclusive_scan(P.block_m > 0 ? pad : 0, sm_scan, &tot);
     run_pad += tot;
-    const int aidx = run_act + block_exclusive_scan(cnt > 0 ? 1 : 0, sm_scan, &tot);
+    // an expert's routes become ceil(cnt / kSegRoutes) segments of <= kSegRoutes routes
+    const int nsub = (int)ceil_div(cnt, kSegRoutes);
+    const int aidx = run_act + block_exclusive_scan(nsub, sm_scan, &tot);
     run_act += tot;
     if (e < E) {
       P.offsets[e] = off;
-      if (cnt > 0 && P.seg_expert) {
-        P.seg_expert[aidx] = e;
-        P.seg_off[aidx] = off;
-        P.seg_cnt[aidx] = cnt;
+      if (P.seg_expert) {
+        for (int k = 0; k < nsub; ++k) {
+          P.seg_expert[aidx + k] = e;
+          P.seg_off[aidx + k] = off + k * kSegRoutes;
+          P.seg_cnt[aidx + k] = min(kSegRoutes, cnt - k * kSegRoutes);
+        }
       }
       // turn hist[w][e] into the base position of warp w's first route of expert e
       int run = off;
@@ -128,10 +132,11 @@ __device__ void sort_block(const SortParams& P, int* hist /* [32][E] */) {
     if (P.seg_expert) {
       int n = run_act;
       if (P.has_shared && P.T > 0) {
-        P.seg_expert[n] = E;  // marker: the shared expert
-        P.seg_off[n] = (int)R;
-        P.seg_cnt[n] = (int)P.T;
-        ++n;
+        for (int64_t t0 = 0; t0 < P.T; t0 += kSegRoutes, ++n) {
+          P.seg_expert[n] = E;  // marker: the shared expert
+          P.seg_off[n] = (int)(R + t0);
+          P.seg_cnt[n] = (int)min((int64_t)kSegRoutes, P.T - t0);
+        }
       }
       *P.n_seg = n;
     }

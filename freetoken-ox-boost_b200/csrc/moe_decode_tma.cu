@@ -49,8 +49,11 @@ struct TileShape {
 
 struct Layout {
   int K;             // reduction length (H for gate_up, I for down)
-  int packed_bytes;  // rows * K/2
-  int glob_off;      // rows' fp16 global scales (after rows * K/16 scale bytes)
+  int padded;        // rows copied one by one into padded pitches (K % 256 == 0)
+  int pitch;         // packed row pitch in the stage: K/2 (+64 when padded)
+  int spitch;        // scale row pitch: K/16 (+16 when padded)
+  int scale_off;     // rows * pitch
+  int glob_off;      // rows' fp16 global scales
   int red_off;       // reduction slot: kRedBytes
   int stage_bytes;
   int load_bytes;    // bytes the producer copies per stage (expect_tx)
@@ -58,15 +61,20 @@ struct Layout {
   int bar_off, cnt_off, tile_off, flag_off, stage_off, total;
 };
 
+// Rows are copied as contiguous blocks (a few large bulk copies per stage): measured faster
+// than per-row copies into bank-padded pitches, although consecutive rows then share banks.
 template <int MODE>
 __host__ __device__ inline Layout make_layout(int K) {
   constexpr int rows = TileShape<MODE>::kRows;
   Layout L;
   L.K = K;
-  L.packed_bytes = rows * (K / 2);
-  L.glob_off = L.packed_bytes + rows * (K / 16);
-  L.load_bytes = L.glob_off + rows * 2;
-  L.red_off = (L.load_bytes + 127) / 128 * 128;
+  L.padded = 0;  // per-row copies measured slower: the TMA engine wants few large copies
+  L.pitch = K / 2 + (L.padded ? 64 : 0);
+  L.spitch = K / 16 + (L.padded ? 16 : 0);
+  L.scale_off = rows * L.pitch;
+  L.glob_off = L.scale_off + (rows * L.spitch + 15) / 16 * 16;
+  L.load_bytes = rows * (K / 2) + rows * (K / 16) + rows * 2;
+  L.red_off = (L.glob_off + rows * 2 + 127) / 128 * 128;
   L.stage_bytes = L.red_off + kRedBytes;
   L.bar_off = 0;
   L.cnt_off = 2 * kMaxStages * 8;
@@ -141,59 +149,93 @@ __device__ __forceinline__ TileSrc tile_src(const DecodeParams& P, int a, int p)
   return s;
 }
 
-constexpr int kChunk = 4;  // consecutive tiles claimed at once (same expert -> warm L1)
+constexpr int kChunk = 4;  // measured best of 1..16 (larger chunks lost DRAM/tail balance)
 
-// Producer: claims chunks of kChunk tiles from the launch-wide counter (dynamic balance of
-// tiles of unequal cost), publishes each stage's tile id, then one sentinel (-1) stage per
-// consumer group.
+// Producer warp: lane 0 claims chunks of kChunk consecutive tiles from the launch-wide
+// counter (dynamic balance of tiles of unequal cost; consecutive tiles of one expert reuse
+// its activation rows from L1), arms the stage barrier and publishes the tile id;
+// then all 32 lanes issue the stage's bulk copies (one per row when padded). After the
+// work, one sentinel (-1) stage per consumer group.
 template <int MODE>
 __device__ void producer(const DecodeParams& P, const Layout& L, uint8_t* stages, const Sync& sy,
                          int64_t ntiles, int tpe, int* work_counter) {
-  if ((threadIdx.x & 31) != 0) return;
+  const int lane = threadIdx.x & 31;
+  constexpr int rows = TileShape<MODE>::kRows;
   uint32_t last_parity[kMaxStages];
   bool issued[kMaxStages];
   for (int s = 0; s < kMaxStages; ++s) issued[s] = false, last_parity[s] = 0;
   const int K = L.K;
+  const int64_t chunk = kChunk;
   int i = 0;
   int64_t tile = 0, chunk_end = 0;
   int sentinels = 0;
   bool aborted = false;
   while (sentinels < kGroups) {
-    if (tile >= chunk_end && tile >= 0) {
-      const int64_t c = atomicAdd(work_counter, 1);
-      tile = c * kChunk;
-      chunk_end = tile + kChunk < ntiles ? tile + kChunk : ntiles;
-      if (tile >= ntiles) tile = -1;
-    }
     const int s = i % L.stages;
     const int round = i / L.stages;
-    if (round > 0 && !aborted && !sy.wait(&sy.empty[s], (round - 1) & 1)) aborted = true;
-    if (aborted) break;  // consumers see the abort flag and stop
-    sy.tile_of[s] = tile;
+    int go = 1;  // lane 0's decision for this stage: 1 = tile, 0 = sentinel, -1 = abort
+    if (lane == 0) {
+      if (tile >= chunk_end && tile >= 0) {
+        const int64_t c = atomicAdd(work_counter, 1);
+        tile = c * chunk;
+        chunk_end = tile + chunk < ntiles ? tile + chunk : ntiles;
+        if (tile >= ntiles) tile = -1;
+      }
+      if (round > 0 && !sy.wait(&sy.empty[s], (round - 1) & 1)) {
+        go = -1;
+      } else {
+        sy.tile_of[s] = tile;
+        if (tile < 0) {
+          mbar_arrive(&sy.full[s]);  // sentinel stage: no bytes, completes at once
+          go = 0;
+        } else {
+          mbar_arrive_expect_tx(&sy.full[s], (uint32_t)L.load_bytes);
+        }
+      }
+    }
+    go = __shfl_sync(0xffffffffu, go, 0);
+    const int64_t t = __shfl_sync(0xffffffffu, tile, 0);
+    if (go < 0) {
+      aborted = true;
+      break;  // consumers see the abort flag and stop
+    }
     issued[s] = true;
     last_parity[s] = round & 1;
-    if (tile < 0) {
-      mbar_arrive(&sy.full[s]);  // sentinel stage: no bytes, completes at once
+    if (go == 0) {
       ++sentinels;
     } else {
-      const TileSrc src = tile_src<MODE>(P, (int)(tile / tpe), (int)(tile % tpe));
+      const TileSrc src = tile_src<MODE>(P, (int)(t / tpe), (int)(t % tpe));
       uint8_t* st = stages + (size_t)s * L.stage_bytes;
-      mbar_arrive_expect_tx(&sy.full[s], (uint32_t)L.load_bytes);
-      const uint32_t pbytes = (uint32_t)(src.rows_per_block * (K / 2));
-      const uint32_t sbytes = (uint32_t)(src.rows_per_block * (K / 16));
-      const uint32_t gbytes = (uint32_t)(src.rows_per_block * 2);
-      for (int b = 0; b < src.nblocks; ++b) {
-        bulk_g2s(st + b * pbytes, src.packed[b], pbytes, &sy.full[s]);
-        bulk_g2s(st + L.packed_bytes + b * sbytes, src.scale[b], sbytes, &sy.full[s]);
-        bulk_g2s(st + L.glob_off + b * gbytes, src.global[b], gbytes, &sy.full[s]);
+      const int rpb = src.rows_per_block;
+      if (L.padded) {
+        // copies: rows packed rows, rows scale rows, nblocks global blocks
+        for (int c = lane; c < 2 * rows + src.nblocks; c += kWarp) {
+          if (c < rows) {
+            const int b = c / rpb, rr = c % rpb;
+            bulk_g2s(st + c * L.pitch, src.packed[b] + (int64_t)rr * (K / 2), K / 2, &sy.full[s]);
+          } else if (c < 2 * rows) {
+            const int r = c - rows, b = r / rpb, rr = r % rpb;
+            bulk_g2s(st + L.scale_off + r * L.spitch, src.scale[b] + (int64_t)rr * (K / 16),
+                     K / 16, &sy.full[s]);
+          } else {
+            const int b = c - 2 * rows;
+            bulk_g2s(st + L.glob_off + b * rpb * 2, src.global[b], rpb * 2, &sy.full[s]);
+          }
+        }
+      } else if (lane < src.nblocks) {
+        const int b = lane;
+        bulk_g2s(st + b * rpb * L.pitch, src.packed[b], rpb * (K / 2), &sy.full[s]);
+        bulk_g2s(st + L.scale_off + b * rpb * L.spitch, src.scale[b], rpb * (K / 16),
+                 &sy.full[s]);
+        bulk_g2s(st + L.glob_off + b * rpb * 2, src.global[b], rpb * 2, &sy.full[s]);
       }
-      ++tile;
+      if (lane == 0) ++tile;
     }
     ++i;
   }
   // After an abort, copies may still be in flight into stages no consumer waited for: they
   // must land before the CTA exits. (Without an abort every issued stage was consumed.)
-  if (!aborted && !*sy.abort) return;
+  if (lane != 0 || (!aborted && !*sy.abort)) return;
   for (int s = 0; s < L.stages; ++s) {
     if (!issued[s]) continue;
     for (uint32_t it = 0; it < kSpinLimit; ++it) {
@@ -358,10 +400,10 @@ __device__ __forceinline__ void warp_tile(const DecodeParams& P, const Layout& L
   const bool sh = (e == P.E);
   const int K = L.K, rounds = K / 128;
   const int lr = 16 * mt + g;  // local row of the lane's first A row
-  const uint8_t* r0 = st + lr * (K / 2) + 16 * tig;
-  const uint8_t* r1 = r0 + 8 * (K / 2);
-  const uint8_t* s0 = st + L.packed_bytes + lr * (K / 16) + 2 * tig;
-  const uint8_t* s1 = s0 + 8 * (K / 16);
+  const uint8_t* r0 = st + lr * L.pitch + 16 * tig;
+  const uint8_t* r1 = r0 + 8 * L.pitch;
+  const uint8_t* s0 = st + L.scale_off + lr * L.spitch + 2 * tig;
+  const uint8_t* s1 = s0 + 8 * L.spitch;
   const __half* brow[NT];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {

@@ -1,0 +1,414 @@
+#!/usr/bin/env python
+"""NVFP4 MoE layer benchmark on B200 (BASELINE metric: NVFP4 MoE layer tokens/s + HBM GB/s).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ftb|reference]
+
+N=1 workload: BASELINE config 1 decode at T=64 tokens (H=4096, I=1536, 256 routed experts,
+top-8, one shared expert; the largest decode batch of config 1). A step = one layer forward:
+softmax top-k routing of the step's logits -> sort -> gate_up GEMV + SwiGLU -> down GEMV ->
+combine + shared expert, through the C-ABI library. Four layers with distinct weights
+(4 x 2.7 GB > L2) are rotated so no step reads weights another step left in L2.
+N>1 (torchrun): BASELINE config 3, expert-parallel decode, T=64 tokens per rank, experts
+sharded contiguously, NCCL all-to-all dispatch/combine; value = tokens/s of the whole box.
+
+Prints one JSON line (rank 0). `--impl reference` times the reference's CPU MoE executor
+semantics (the C++ restatement in oracle/, the reference's own executor being unbuildable)
+on the host cores for the same metric and config.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "freetoken-ox-boost_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+H, I, E, TOPK = 4096, 1536, 256, 8
+METRIC = "NVFP4 MoE layer tokens/s (decode, BASELINE config 1/3)"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ftb", "reference"], default="ftb")
+    ap.add_argument("--tokens", type=int, default=64, help="tokens per step (per rank)")
+    ap.add_argument("--layers", type=int, default=4, help="distinct layer banks rotated")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the T=1/4/16 decode sweep")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs, copy)"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback (6.65 TB/s, earlier measurement on this pool)"
+
+
+class ClockSampler:
+    """SM clock and clock-event (throttle) reasons sampled every 10 ms through NVML while the
+    timed region runs (the data nvidia-smi's clocks/clocks_event_reasons query reports).
+    The GPU is addressed by the UUID of the CUDA device, so device renumbering is harmless."""
+
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+               "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
+
+    def __init__(self, torch, device: int = 0):
+        self.samples, self.reasons, self.err = [], set(), None
+        self.stop_flag = False
+        self.thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            if not uuid.startswith("GPU-"):
+                uuid = "GPU-" + uuid
+            self.nvml = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # noqa: BLE001 - report, never fail the bench
+            self.nvml, self.err = None, f"nvml unavailable: {e}"
+
+    def _run(self):
+        import threading  # noqa: F401
+
+        while not self.stop_flag:
+            try:
+                self.samples.append(self.nvml.nvmlDeviceGetClockInfo(self.h,
+                                                                    self.nvml.NVML_CLOCK_SM))
+                r = self.nvml.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for name, bit in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception as e:  # noqa: BLE001
+                self.err = str(e)
+                return
+            time.sleep(0.01)
+
+    def start(self):
+        import threading
+
+        if self.nvml is None:
+            return
+        self.thread = threading.Thread(target=self._run, daemon=True)
+        self.thread.start()
+        time.sleep(0.02)
+
+    def stop(self) -> dict:
+        if self.nvml is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": self.err}
+        self.stop_flag = True
+        self.thread.join(timeout=2)
+        out = {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+               "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+               "samples": len(self.samples), "source": "NVML, 10 ms, during the timed region"}
+        if self.err:
+            out["note"] = self.err
+        return out
+
+
+def gate_up_bytes_per_expert(h=H, i=I):
+    return 2 * i * (h // 2 + h // 16 + 2)
+
+
+class Layers:
+    """L distinct synthetic layers on the GPU plus per-layer step inputs."""
+
+    def __init__(self, torch, ftb, synth, n_layers: int, tokens: int, experts, device, seed0=0):
+        self.torch, self.ftb = torch, ftb
+        self.T = tokens
+        self.banks, self.shared, self.inputs, self.outs = [], [], [], []
+        for l in range(n_layers):
+            bank = synth.make_bank(E, H, I, seed=seed0 + l, device=device)
+            if experts is not None:  # this rank's contiguous expert shard
+                bank = bank.select(experts)
+            self.banks.append(bank)
+            self.shared.append(synth.make_shared(H, I, seed=seed0 + l, device=device))
+            self.inputs.append(synth.make_inputs(tokens, H, E, seed=1000 + seed0 + l,
+                                                 device=device))
+            self.outs.append(torch.empty(tokens, H, dtype=torch.bfloat16, device=device))
+        self.routes = [ftb.fused_topk(None, inp.logits, TOPK, True) for inp in self.inputs]
+        self.uniq = [int(torch.unique(r[1]).numel()) for r in self.routes]
+
+    def step(self, i: int):
+        l = i % len(self.banks)
+        inp = self.inputs[l]
+        w, ids = self.ftb.fused_topk(None, inp.logits, TOPK, True)
+        self.ftb.moe_decode(inp.x, self.banks[l], w, ids, shared=self.shared[l], out=self.outs[l])
+
+
+def time_steps(torch, fn, steps: int) -> float:
+    """Device time of `steps` calls (CUDA events on the current stream), ms per step."""
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        fn(i)
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def kernel_times(ftb_lib, torch, fn, steps: int):
+    """Per-launch durations of the library's kernels over `steps` calls (CUDA events on the
+    launching stream, recorded by the library around each launch)."""
+    import ctypes
+
+    lib = ftb_lib.load()
+    torch.cuda.synchronize()
+    lib.ftb_profile_begin()
+    for i in range(steps):
+        fn(i)
+    torch.cuda.synchronize()
+    cap = 64 * steps + 64
+    ids = (ctypes.c_int32 * cap)()
+    ms = (ctypes.c_float * cap)()
+    n = lib.ftb_profile_end(ids, ms, cap)
+    if n < 0:
+        raise RuntimeError(f"ftb_profile_end failed ({n})")
+    out = {}
+    for k in range(min(n, cap)):
+        out.setdefault(ftb_lib.KERNEL_NAMES.get(ids[k], str(ids[k])), []).append(ms[k])
+    return out
+
+
+def e2e_steps(torch, ftb, layers: "Layers", steps: int):
+    """End to end through the public API with host buffers: each step copies its x and logits
+    from pinned host memory, runs routing + the layer, and reads the output back to host."""
+    T = layers.T
+    hx = [inp.x.cpu().pin_memory() for inp in layers.inputs]
+    hl = [inp.logits.cpu().pin_memory() for inp in layers.inputs]
+    hout = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+    dx = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    dl = torch.empty(T, E, dtype=torch.float32, device="cuda")
+    dout = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+
+    def one(i):
+        l = i % len(layers.banks)
+        dx.copy_(hx[l], non_blocking=True)
+        dl.copy_(hl[l], non_blocking=True)
+        w, ids = ftb.fused_topk(dx, dl, TOPK, True)
+        ftb.moe_decode(dx, layers.banks[l], w, ids, shared=layers.shared[l], out=dout)
+        hout.copy_(dout, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    for i in range(3):
+        one(i)
+    t0 = time.perf_counter()
+    for i in range(steps):
+        one(i)
+    dt = (time.perf_counter() - t0) / steps
+    return dt, T * H * 2 + T * E * 4, T * H * 2
+
+
+def cpu_baseline(torch, layers: "Layers", budget_s: float):
+    """The C++ CPU restatement of the layer (oracle/cpu_moe.cpp) on all host threads, on a
+    bounded sample: whole T-token steps of layer 0 until ~budget_s of CPU time."""
+    from oracle import cpu_moe
+
+    bank = layers.banks[0].numpy()
+    shared = layers.shared[0].numpy()
+    inp = layers.inputs[0]
+    x_bits = inp.x.cpu().contiguous().view(torch.int16).numpy().view("uint16")
+    w, ids = layers.routes[0]
+    w, ids = w.cpu().numpy(), ids.cpu().numpy()
+    threads = cpu_moe.max_threads()
+    cpu_moe.moe_layer(x_bits, bank, w, ids, shared, nthreads=threads)  # warm (page in)
+    times = []
+    t_start = time.perf_counter()
+    while not times or (time.perf_counter() - t_start < budget_s and len(times) < 20):
+        t0 = time.perf_counter()
+        cpu_moe.moe_layer(x_bits, bank, w, ids, shared, nthreads=threads)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {"value": layers.T / t, "unit": "tokens/s", "cores": threads,
+            "kind": "port",
+            "sample": f"{len(times)} full T={layers.T} layer steps (config 1 shape, layer 0, "
+                      f"{layers.uniq[0]} routed experts + shared), median {t * 1e3:.0f} ms; "
+                      f"avx512={cpu_moe.has_avx512()}"}
+
+
+def roofline_entry(kt: dict, layers: "Layers", steps: int):
+    """Dominant kernel (gate_up GEMV): algorithmic bytes per launch = (distinct routed experts
+    + shared) x gate_up bytes per expert; achieved = total bytes / total event time."""
+    peak, peak_src = measured_peaks()
+    gu = kt.get("gate_up_gemv", [])
+    n = len(gu)
+    if n == 0:
+        return None
+    byts = sum((layers.uniq[i % len(layers.uniq)] + 1) * gate_up_bytes_per_expert()
+               for i in range(n))
+    achieved = byts / (sum(gu) * 1e-3) / 1e9
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "decode_gate_up_traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            d = json.load(f)
+        # ncu dram bytes per streamed expert, scaled to this workload's experts per launch
+        per_unit = d.get("dram_bytes_per_expert")
+        if per_unit:
+            traffic = per_unit * (sum(layers.uniq) / len(layers.uniq) + 1)
+    return {"kernel": "gate_up_gemv (k_gemv_tma<0>)", "bound": "hbm",
+            "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "peak_source": peak_src,
+            "traffic": traffic, "algorithmic_bytes_per_launch": byts / n,
+            "launches": n, "avg_launch_ms": sum(gu) / n}
+
+
+def run_ftb_single(args, torch):
+    import ftb
+    from ftb import _lib, synth
+
+    torch.cuda.set_device(0)
+    layers = Layers(torch, ftb, synth, args.layers, args.tokens, None, "cuda")
+    for i in range(max(3, args.warmup)):
+        layers.step(i)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(torch, 0)
+    clocks.start()
+    ms = time_steps(torch, layers.step, args.steps)
+    clk = clocks.stop()
+    kt = kernel_times(_lib, torch, layers.step, min(args.steps, 64))
+    e2e_dt, h2d, d2h = e2e_steps(torch, ftb, layers, min(args.steps, 64))
+    value = args.tokens * 1e3 / ms
+    per_exp = ftb.bank_bytes_per_expert(H, I)
+    layer_bytes = statistics.mean((u + 1) * per_exp for u in layers.uniq) + 2 * args.tokens * H * 2
+    out = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "nvfp4 (e2m1+e4m3) x bf16 -> fp32 accumulate, bf16 out",
+        "data": "synthetic: seeded NVFP4 banks and N(0,1) logits/activations per BASELINE config 1",
+        "config": {"workload": f"config 1 decode T={args.tokens}: H{H} I{I} E{E} top{TOPK} "
+                               f"+1 shared expert, softmax-renorm router",
+                   "tokens_per_step": args.tokens, "layers_rotated": args.layers,
+                   "l2": f"inputs larger than L2: {args.layers} distinct 2.7 GB layer banks "
+                         "rotated across steps",
+                   "routed_experts_per_step": round(statistics.mean(layers.uniq), 1)},
+        "layer_hbm_gbs": round(layer_bytes / (ms * 1e-3) / 1e9, 1),
+        "roofline": roofline_entry(kt, layers, args.steps),
+        "kernels_ms": {k: round(statistics.mean(v), 4) for k, v in kt.items()},
+        "e2e": {"value": round(args.tokens / e2e_dt, 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": 5 * args.steps,  # route_topk, sort_stage, gate_up, down, combine
+        "clocks": clk,
+    }
+    if not args.no_sweep:
+        out["decode_sweep"] = sweep_decode(torch, ftb, layers, args)
+    if not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(torch, layers, args.cpu_seconds)
+    return out
+
+
+def sweep_decode(torch, ftb, layers: "Layers", args):
+    """Tokens/s at T = 1, 4, 16 on the same layer banks (fresh routing per T)."""
+    from ftb import synth
+
+    res = {}
+    for T in (1, 4, 16):
+        inps = [synth.make_inputs(T, H, E, seed=2000 + T * 10 + l, device="cuda")
+                for l in range(len(layers.banks))]
+        outs = [torch.empty(T, H, dtype=torch.bfloat16, device="cuda") for _ in inps]
+
+        def step(i, inps=inps, outs=outs):
+            l = i % len(inps)
+            w, ids = ftb.fused_topk(None, inps[l].logits, TOPK, True)
+            ftb.moe_decode(inps[l].x, layers.banks[l], w, ids, shared=layers.shared[l],
+                           out=outs[l])
+
+        for i in range(3):
+            step(i)
+        ms = time_steps(torch, step, min(max(8, args.steps), 200))
+        res[f"T={T}"] = {"tokens_per_s": round(T * 1e3 / ms, 1), "ms_per_step": round(ms, 4)}
+    return res
+
+
+def run_reference(args, torch):
+    """The reference arm: the reference's CPU MoE executor semantics (C++ restatement in
+    oracle/cpu_moe.cpp; the reference's cpu_moe_ext.cpp is absent and unbuildable) on all
+    host threads, same metric/config; each step = one T-token layer sample on layer 0."""
+    import ftb
+    from ftb import synth
+    from oracle import cpu_moe
+
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    layers = Layers(torch, ftb, synth, 1, args.tokens, None, dev) if dev == "cuda" else None
+    if layers is None:
+        raise RuntimeError("the reference arm generates its banks on the GPU")
+    bank, shared = layers.banks[0].numpy(), layers.shared[0].numpy()
+    x_bits = layers.inputs[0].x.cpu().contiguous().view(torch.int16).numpy().view("uint16")
+    w, ids = layers.routes[0]
+    w, ids = w.cpu().numpy(), ids.cpu().numpy()
+    threads = cpu_moe.max_threads()
+    for _ in range(args.warmup):
+        cpu_moe.moe_layer(x_bits, bank, w, ids, shared, nthreads=threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_moe.moe_layer(x_bits, bank, w, ids, shared, nthreads=threads)
+    dt = (time.perf_counter() - t0) / args.steps
+    value = args.tokens / dt
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": "tokens/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt * 1e3, 2), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "nvfp4 x bf16 -> fp32 (CPU)",
+        "data": "synthetic: seeded NVFP4 banks and N(0,1) logits/activations per BASELINE config 1",
+        "config": {"workload": f"config 1 decode T={args.tokens}: H{H} I{I} E{E} top{TOPK} "
+                               "+1 shared expert, softmax-renorm router",
+                   "tokens_per_step": args.tokens},
+        "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": threads,
+                         "kind": "port",
+                         "sample": f"{args.steps} full T={args.tokens} layer steps on layer 0 "
+                                   "(C++ restatement of the reference CPU executor semantics)"},
+        "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    args = parse_args()
+    rank, world, local = dist_env()
+    import torch
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0  # the reference arm runs on rank 0 only
+        print(json.dumps(run_reference(args, torch)), flush=True)
+        return 0
+    if world > 1:
+        from ftb import ep_bench
+
+        out = ep_bench.run(args, torch, rank, world, local)
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+        return 0
+    print(json.dumps(run_ftb_single(args, torch)), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

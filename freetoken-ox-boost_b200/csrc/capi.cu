@@ -109,6 +109,45 @@ BankView view_dn(const ftb_nvfp4_bank* b, const ftb_nvfp4_bank* s) {
 
 }  // namespace
 
+namespace {
+struct ProfRec {
+  int id;
+  cudaEvent_t start, stop;
+};
+std::mutex g_prof_mu;
+bool g_prof_on = false;
+std::vector<ProfRec> g_prof;
+std::vector<cudaEvent_t> g_prof_pool;
+
+cudaEvent_t prof_event() {
+  if (!g_prof_pool.empty()) {
+    cudaEvent_t e = g_prof_pool.back();
+    g_prof_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+}  // namespace
+
+void prof_mark(int id, bool start, cudaStream_t stream) {
+  std::lock_guard<std::mutex> lock(g_prof_mu);
+  if (!g_prof_on) return;
+  cudaEvent_t e = prof_event();
+  cudaEventRecord(e, stream);
+  if (start) {
+    g_prof.push_back(ProfRec{id, e, nullptr});
+  } else {
+    for (auto it = g_prof.rbegin(); it != g_prof.rend(); ++it)
+      if (it->id == id && it->stop == nullptr) {
+        it->stop = e;
+        return;
+      }
+    g_prof_pool.push_back(e);
+  }
+}
+
 int cuda_status(cudaError_t err) {
   if (err == cudaSuccess) return FTB_OK;
   std::snprintf(g_last_error, sizeof(g_last_error), "%s: %s", cudaGetErrorName(err),
@@ -244,6 +283,37 @@ const char* ftb_status_string(int status) {
 }
 
 int ftb_version(void) { return 1; }
+
+int ftb_profile_begin(void) {
+  std::lock_guard<std::mutex> lock(g_prof_mu);
+  for (auto& r : g_prof) {
+    g_prof_pool.push_back(r.start);
+    if (r.stop) g_prof_pool.push_back(r.stop);
+  }
+  g_prof.clear();
+  g_prof_on = true;
+  return FTB_OK;
+}
+
+int ftb_profile_end(int32_t* kernel_ids, float* ms, int max_n) {
+  std::lock_guard<std::mutex> lock(g_prof_mu);
+  g_prof_on = false;
+  int n = 0;
+  for (auto& r : g_prof) {
+    if (!r.stop) continue;
+    cudaError_t e = cudaEventSynchronize(r.stop);
+    if (e != cudaSuccess) return -cuda_status(e);
+    float t = 0.f;
+    e = cudaEventElapsedTime(&t, r.start, r.stop);
+    if (e != cudaSuccess) return -cuda_status(e);
+    if (n < max_n && kernel_ids && ms) {
+      kernel_ids[n] = r.id;
+      ms[n] = t;
+    }
+    ++n;
+  }
+  return n;
+}
 
 const char* ftb_last_cuda_error(void) { return g_last_error; }
 

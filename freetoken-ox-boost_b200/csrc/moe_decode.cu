@@ -328,7 +328,9 @@ int launch_combine(const DecodeParams& P, cudaStream_t stream) {
   int64_t g3 = ceil_div(nv, 256);
   const int64_t cap = (int64_t)sm_count() * 8;
   if (g3 > cap) g3 = cap;
+  prof_mark(FTB_KERNEL_COMBINE, true, stream);
   k_combine<<<(unsigned)g3, 256, 0, stream>>>(P);
+  prof_mark(FTB_KERNEL_COMBINE, false, stream);
   return cuda_status(cudaGetLastError());
 }
 

@@ -510,9 +510,14 @@ int launch_one(const DecodeParams& P, int64_t max_tiles, cudaStream_t stream) {
 
 int launch_decode_gemvs_tma(const DecodeParams& P, cudaStream_t stream) {
   const int64_t max_seg = max_segments(P.R, P.E, P.T, P.has_shared);
+  prof_mark(FTB_KERNEL_GATE_UP, true, stream);
   int st = launch_one<kGateUp>(P, max_seg * (P.I / 8), stream);
+  prof_mark(FTB_KERNEL_GATE_UP, false, stream);
   if (st) return st;
-  return launch_one<kDown>(P, max_seg * (P.H / 32), stream);
+  prof_mark(FTB_KERNEL_DOWN, true, stream);
+  st = launch_one<kDown>(P, max_seg * (P.H / 32), stream);
+  prof_mark(FTB_KERNEL_DOWN, false, stream);
+  return st;
 }
 
 }  // namespace ftb

@@ -101,4 +101,8 @@ int launch_decode_gemvs_tma(const DecodeParams& P, cudaStream_t stream);
 int launch_decode_gemvs_ldg(const DecodeParams& P, cudaStream_t stream);
 int launch_combine(const DecodeParams& P, cudaStream_t stream);
 
+// Measurement hook (ftb_profile_begin/end): records an event on `stream` before (start=true)
+// or after a launch of kernel `id`; a no-op unless profiling is on.
+void prof_mark(int id, bool start, cudaStream_t stream);
+
 }  // namespace ftb

@@ -253,7 +253,9 @@ int launch_sort_stage(const SortParams& P, cudaStream_t stream) {
     if (e != cudaSuccess) return cuda_status(e);
   }
   const int64_t blocks = 1 + (P.x16 ? P.T : 0);
+  prof_mark(FTB_KERNEL_SORT, true, stream);
   k_sort_stage<<<(unsigned)blocks, kSortThreads, smem, stream>>>(P);
+  prof_mark(FTB_KERNEL_SORT, false, stream);
   return cuda_status(cudaGetLastError());
 }
 

@@ -6,6 +6,7 @@
 // torch.topk. Selected lanes are masked by a per-lane bitmask, so NaN/-inf rows still
 // produce top_k distinct ids.
 #include "ftb_common.cuh"
+#include "moe_kernels.cuh"
 
 namespace ftb {
 namespace {
@@ -150,8 +151,10 @@ int launch_route_topk(const float* logits, int64_t T, int E, int top_k, int mode
   if (T == 0) return FTB_OK;
   const int wpb = 4;
   const int64_t blocks = ceil_div(T, wpb);
+  prof_mark(FTB_KERNEL_ROUTE, true, stream);
   k_route_topk<<<(unsigned)blocks, 32 * wpb, 0, stream>>>(logits, T, E, top_k, mode, bias,
                                                           scaling, renorm, w, ids);
+  prof_mark(FTB_KERNEL_ROUTE, false, stream);
   return cuda_status(cudaGetLastError());
 }
 

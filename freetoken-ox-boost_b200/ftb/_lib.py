@@ -59,7 +59,11 @@ SIGNATURES = {
                               _sz, _vp]),
     "ftb_moe_decode_debug": (_i32, [_vp, _BP, _BP, _vp, _vp, _i64, _i32, _i32, _i32, _f32, _vp,
                                     _vp, _sz, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "ftb_profile_begin": (_i32, []),
+    "ftb_profile_end": (_i32, [_vp, _vp, _i32]),
 }
+
+KERNEL_NAMES = {0: "sort_stage", 1: "gate_up_gemv", 2: "down_gemv", 3: "combine", 4: "route_topk"}
 
 
 class FtbLibraryError(RuntimeError):

@@ -135,6 +135,23 @@ FTB_API int ftb_moe_decode_debug(const uint16_t* x, const ftb_nvfp4_bank* bank,
                          uint16_t* ic1, uint16_t* h, uint16_t* ic3, uint16_t* shared_ic1,
                          uint16_t* shared_h, uint16_t* shared_out, ftb_stream_t stream);
 
+/*
+ * Measurement hooks (no counterpart in the reference): between ftb_profile_begin() and
+ * ftb_profile_end() the library records a CUDA event pair on the launching stream around
+ * each of its kernel launches (ids: FTB_KERNEL_*). ftb_profile_end() synchronises those
+ * events, writes up to max_n (kernel id, milliseconds) pairs and returns how many launches
+ * were recorded (or a negative status). Not for use under CUDA-graph capture.
+ */
+enum {
+  FTB_KERNEL_SORT = 0,
+  FTB_KERNEL_GATE_UP = 1,
+  FTB_KERNEL_DOWN = 2,
+  FTB_KERNEL_COMBINE = 3,
+  FTB_KERNEL_ROUTE = 4
+};
+FTB_API int ftb_profile_begin(void);
+FTB_API int ftb_profile_end(int32_t* kernel_ids, float* ms, int max_n);
+
 #ifdef __cplusplus
 }
 #endif

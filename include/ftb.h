@@ -136,6 +136,20 @@ FTB_API int ftb_moe_decode_debug(const uint16_t* x, const ftb_nvfp4_bank* bank,
                          uint16_t* shared_h, uint16_t* shared_out, ftb_stream_t stream);
 
 /*
+ * The decode layer for callers that cannot allocate device memory (no counterpart in the
+ * reference): same arguments and result as ftb_moe_decode() without the workspace, which is
+ * taken from a 16 MiB scratch array the library holds in device memory on every GPU that
+ * loads it, until the process exits. Larger needs return FTB_ERR_WORKSPACE (config-1 shape
+ * with a shared expert: T <= 150). The first call on a device looks the scratch up; make it
+ * before any CUDA-graph capture. All calls share the scratch: calls that may overlap on the
+ * GPU race and must be serialised by the caller. Allocates nothing.
+ */
+FTB_API int ftb_moe_decode_noalloc(const uint16_t* x, const ftb_nvfp4_bank* bank,
+                                   const ftb_nvfp4_bank* shared, const float* topk_w,
+                                   const int32_t* topk_ids, int64_t T, int H, int I, int top_k,
+                                   float act_limit, uint16_t* out, ftb_stream_t stream);
+
+/*
  * Measurement hooks (no counterpart in the reference): between ftb_profile_begin() and
  * ftb_profile_end() the library records a CUDA event pair on the launching stream around
  * each of its kernel launches (ids: FTB_KERNEL_*). ftb_profile_end() synchronises those

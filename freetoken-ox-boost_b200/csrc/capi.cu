@@ -377,6 +377,27 @@ int ftb_moe_align(const int32_t* topk_ids, int64_t T, int top_k, int E, int bloc
   return st;
 }
 
+int ftb_moe_combine(const uint16_t* ic3, const int32_t* topk_ids, const uint16_t* shared_out,
+                    int64_t T, int H, int top_k, int E, uint16_t* out, ftb_stream_t stream) {
+  if (T < 0 || H <= 0 || H % 8 || top_k < 1 || E < 1) return FTB_ERR_SHAPE;
+  if (T == 0) return FTB_OK;
+  if (!ic3 || !topk_ids || !out) return FTB_ERR_ARG;
+  if (!aligned16(ic3) || !aligned16(out) || (shared_out && !aligned16(shared_out)))
+    return FTB_ERR_ALIGN;
+  DecodeParams dp{};
+  dp.H = H;
+  dp.E = E;
+  dp.top_k = top_k;
+  dp.T = T;
+  dp.R = T * top_k;
+  dp.topk_ids = topk_ids;
+  dp.ic3 = const_cast<uint16_t*>(ic3);
+  dp.ic3s = const_cast<uint16_t*>(shared_out);
+  dp.has_shared = shared_out ? 1 : 0;
+  dp.out = out;
+  return launch_combine(dp, (cudaStream_t)stream);
+}
+
 size_t ftb_moe_decode_workspace_bytes(int64_t T, int H, int I, int E, int top_k, int has_shared) {
   return carve_decode(nullptr, T, H, I, E, top_k, has_shared).bytes;
 }

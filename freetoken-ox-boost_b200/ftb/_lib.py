@@ -59,6 +59,7 @@ SIGNATURES = {
                               _sz, _vp]),
     "ftb_moe_decode_debug": (_i32, [_vp, _BP, _BP, _vp, _vp, _i64, _i32, _i32, _i32, _f32, _vp,
                                     _vp, _sz, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "ftb_moe_combine": (_i32, [_vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp]),
     "ftb_moe_decode_noalloc": (_i32, [_vp, _BP, _BP, _vp, _vp, _i64, _i32, _i32, _i32, _f32,
                                       _vp, _vp]),
     "ftb_profile_begin": (_i32, []),

@@ -169,6 +169,25 @@ def fused_experts_nvfp4(
                       act_limit=act_limit, shared=shared)
 
 
+def moe_sum_reduce(ic3: torch.Tensor, topk_ids: torch.Tensor, num_experts: int,
+                   shared_out: torch.Tensor | None = None, out: torch.Tensor | None = None):
+    """``moe_sum_reduce_triton(ic3, out)`` (patches/moe_fused_nvfp4.patch:147-148): out[t] =
+    bf16(sum_k ic3[t, k]) in k order (fp32), then ``+ shared_out`` in bf16 when given. Routes
+    with ids outside [0, num_experts) contribute nothing."""
+    dev = require_cuda(ic3, topk_ids)
+    require(ic3, "ic3", torch.bfloat16)
+    require(topk_ids, "topk_ids", torch.int32)
+    T, K, H = ic3.shape
+    if out is None:
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    if shared_out is not None:
+        require(shared_out, "shared_out", torch.bfloat16, (T, H))
+    st = _lib.load().ftb_moe_combine(ptr(ic3), ptr(topk_ids), ptr(shared_out), T, H, K,
+                                     num_experts, ptr(out), stream_handle(dev))
+    _lib.check("ftb_moe_combine", st)
+    return out
+
+
 def moe_align_block_size(topk_ids: torch.Tensor, block_size: int, num_experts: int):
     """Stable, deterministic permutation: (sorted_ids [cap], expert_ids [cap/bm],
     num_tokens_post_padded int32 [1]); cap = T*top_k + E*(block_size-1)."""

@@ -136,6 +136,18 @@ FTB_API int ftb_moe_decode_debug(const uint16_t* x, const ftb_nvfp4_bank* bank,
                          uint16_t* shared_h, uint16_t* shared_out, ftb_stream_t stream);
 
 /*
+ * Fixed-order combine, replacing moe_sum_reduce_triton(ic3, out)
+ * (patches/moe_fused_nvfp4.patch:147-148) plus the model block's shared add
+ * (patches/models_glm_moe_dsa_moe.patch:203-206): out[t] = bf16(sum over k of ic3[t,k]
+ * in k order, fp32) and, when shared_out != NULL, out[t] = bf16(that + shared_out[t]).
+ * Routes whose topk_ids entry is outside [0, E) contribute nothing. ic3 [T, top_k, H] and
+ * shared_out [T, H] bf16; H % 8 == 0; 16-byte aligned.
+ */
+FTB_API int ftb_moe_combine(const uint16_t* ic3, const int32_t* topk_ids, const uint16_t* shared_out,
+                            int64_t T, int H, int top_k, int E, uint16_t* out,
+                            ftb_stream_t stream);
+
+/*
  * The decode layer for callers that cannot allocate device memory (no counterpart in the
  * reference): same arguments and result as ftb_moe_decode() without the workspace, which is
  * taken from a 16 MiB scratch array the library holds in device memory on every GPU that

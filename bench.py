@@ -9,7 +9,10 @@ softmax top-k routing of the step's logits -> sort -> gate_up GEMV + SwiGLU -> d
 combine + shared expert, through the C-ABI library. Four layers with distinct weights
 (4 x 2.7 GB > L2) are rotated so no step reads weights another step left in L2.
 N>1 (torchrun): BASELINE config 3, expert-parallel decode, T=64 tokens per rank, experts
-sharded contiguously, NCCL all-to-all dispatch/combine; value = tokens/s of the whole box.
+sharded contiguously; tokens and outputs move over NVLink peer memory inside the layer's own
+kernels (--ep-transport p2p, default) or by NCCL all_to_all (--ep-transport nccl, the
+collective-library baseline); value = tokens/s of the whole box.
+Timed steps replay one CUDA graph per layer (--no-graphs: eager launches).
 
 Prints one JSON line (rank 0). `--impl reference` times the reference's CPU MoE executor
 semantics (the C++ restatement in oracle/, the reference's own executor being unbuildable)
@@ -48,6 +51,10 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="skip the T=1/4/16 decode sweep")
+    ap.add_argument("--no-graphs", dest="graphs", action="store_false",
+                    help="time eager launches instead of CUDA-graph replay")
+    ap.add_argument("--ep-transport", choices=["p2p", "nccl"], default="p2p",
+                    help="expert-parallel transport for --gpus > 1")
     return ap.parse_args()
 
 
@@ -162,15 +169,41 @@ class Layers:
 
 
 def time_steps(torch, fn, steps: int) -> float:
-    """Device time of `steps` calls (CUDA events on the current stream), ms per step."""
+    """Device time of `steps` calls (CUDA events on the current stream), ms per step. The
+    host time spent issuing them is kept in time_steps.host_ms (ms per step)."""
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
+    t0 = time.perf_counter()
     for i in range(steps):
         fn(i)
+    time_steps.host_ms = (time.perf_counter() - t0) * 1e3 / steps
     e1.record()
     torch.cuda.synchronize()
     return e0.elapsed_time(e1) / steps
+
+
+time_steps.host_ms = None
+
+
+def graph_steps(torch, fn, n: int):
+    """Captures fn(0) .. fn(n-1) (one step per distinct layer, after eager warm-up) into CUDA
+    graphs and returns a step function that replays graph i % n: the same launches with the
+    host's per-launch work removed."""
+    graphs = []
+    torch.cuda.synchronize()
+    for l in range(n):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn(l)
+        graphs.append(g)
+    torch.cuda.synchronize()
+
+    def step(i):
+        graphs[i % n].replay()
+
+    step.graphs = graphs
+    return step
 
 
 def kernel_times(ftb_lib, torch, fn, steps: int):
@@ -288,9 +321,14 @@ def run_ftb_single(args, torch):
     for i in range(max(3, args.warmup)):
         layers.step(i)
     torch.cuda.synchronize()
+    timed = graph_steps(torch, layers.step, args.layers) if args.graphs else layers.step
+    for i in range(max(3, args.warmup)):
+        timed(i)
+    torch.cuda.synchronize()
     clocks = ClockSampler(torch, 0)
     clocks.start()
-    ms = time_steps(torch, layers.step, args.steps)
+    ms = time_steps(torch, timed, args.steps)
+    host_ms = time_steps.host_ms
     clk = clocks.stop()
     kt = kernel_times(_lib, torch, layers.step, min(args.steps, 64))
     e2e_dt, h2d, d2h = e2e_steps(torch, ftb, layers, min(args.steps, 64))
@@ -308,7 +346,10 @@ def run_ftb_single(args, torch):
                    "tokens_per_step": args.tokens, "layers_rotated": args.layers,
                    "l2": f"inputs larger than L2: {args.layers} distinct 2.7 GB layer banks "
                          "rotated across steps",
-                   "routed_experts_per_step": round(statistics.mean(layers.uniq), 1)},
+                   "routed_experts_per_step": round(statistics.mean(layers.uniq), 1),
+                   "launch": "CUDA graph per layer (route + layer), replayed" if args.graphs
+                             else "eager launches",
+                   "host_issue_ms_per_step": round(host_ms, 4)},
         "layer_hbm_gbs": round(layer_bytes / (ms * 1e-3) / 1e9, 1),
         "roofline": roofline_entry(kt, layers, args.steps),
         "kernels_ms": {k: round(statistics.mean(v), 4) for k, v in kt.items()},
@@ -342,8 +383,12 @@ def sweep_decode(torch, ftb, layers: "Layers", args):
 
         for i in range(3):
             step(i)
-        ms = time_steps(torch, step, min(max(8, args.steps), 200))
-        res[f"T={T}"] = {"tokens_per_s": round(T * 1e3 / ms, 1), "ms_per_step": round(ms, 4)}
+        timed = graph_steps(torch, step, len(inps)) if args.graphs else step
+        for i in range(3):
+            timed(i)
+        ms = time_steps(torch, timed, min(max(8, args.steps), 200))
+        res[f"T={T}"] = {"tokens_per_s": round(T * 1e3 / ms, 1), "ms_per_step": round(ms, 4),
+                         "host_issue_ms_per_step": round(time_steps.host_ms, 4)}
     return res
 
 
@@ -391,21 +436,25 @@ def run_reference(args, torch):
 
 def run_ep(args, torch, rank: int, world: int, local: int):
     """expert-parallel decode, T tokens per rank, 256 experts sharded
-    contiguously over the ranks, NCCL all-to-all dispatch and combine. value = tokens/s of
-    the whole box = world * T / (max over ranks of the per-step device time)."""
+    contiguously over the ranks. value = tokens/s of the whole box = world * T / (max over
+    ranks of the per-step device time). Transport "p2p" (default): the layer's own kernels
+    move tokens and outputs over NVLink peer memory; "nccl": all_to_all_single dispatch and
+    combine (the collective-library baseline)."""
     import datetime
 
     import torch.distributed as dist
 
     import ftb
     from ftb import _lib, synth
-    from ftb.ep import ExpertParallelMoE, shard_range
+    from ftb.ep import EpGroup, ExpertParallelMoE, shard_range
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    transport = args.ep_transport
     e0, e1 = shard_range(E, rank, world)
-    layers = []
+    group = EpGroup(args.tokens, H, I, E, TOPK, True, rank, world) if transport == "p2p" else None
+    layers, hits = [], []
     for l in range(args.layers):
         full = synth.make_bank(E, H, I, seed=l, device=dev)
         bank = full.select(slice(e0, e1))
@@ -413,7 +462,13 @@ def run_ep(args, torch, rank: int, world: int, local: int):
         torch.cuda.empty_cache()
         shared = synth.make_shared(H, I, seed=l, device=dev)
         inp = synth.make_inputs(args.tokens, H, E, seed=1000 + l, stream=rank, device=dev)
-        layers.append((ExpertParallelMoE(bank, shared, E, TOPK, rank, world), inp))
+        layers.append((ExpertParallelMoE(bank, shared, E, TOPK, rank, world,
+                                         transport=transport, ep_group=group), inp))
+        # owned experts hit by every rank's routes of this layer (the bytes this rank streams)
+        ids = torch.cat([ftb.fused_topk(r.x, r.logits, TOPK, True)[1].flatten() for r in
+                         (synth.make_inputs(args.tokens, H, E, seed=1000 + l, stream=q, device=dev)
+                          for q in range(world))])
+        hits.append(int(torch.unique(ids[(ids >= e0) & (ids < e1)]).numel()))
 
     def step(i):
         ep, inp = layers[i % len(layers)]
@@ -423,29 +478,76 @@ def run_ep(args, torch, rank: int, world: int, local: int):
         step(i)
     torch.cuda.synchronize()
     dist.barrier()
+    # the NCCL transport reads receive counts on the host every step: not capturable
+    use_graphs = args.graphs and transport == "p2p"
+    timed = graph_steps(torch, step, len(layers)) if use_graphs else step
+    for i in range(max(3, args.warmup)):
+        timed(i)
+    torch.cuda.synchronize()
+    dist.barrier()
     clocks = ClockSampler(torch, local) if rank == 0 else None
     if clocks:
         clocks.start()
-    ms = time_steps(torch, step, args.steps)
+    ms = time_steps(torch, timed, args.steps)
+    host_ms = time_steps.host_ms
     dist.barrier()
     clk = clocks.stop() if clocks else None
     t = torch.tensor([ms], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
-    # kernel events on every rank (same collectives), gate_up roofline from rank 0's launches
+
+    # end to end through the public API: pinned host x/logits in, host output back, per step
+    hx = [inp.x.cpu().pin_memory() for _, inp in layers]
+    hl = [inp.logits.cpu().pin_memory() for _, inp in layers]
+    hout = torch.empty(args.tokens, H, dtype=torch.bfloat16).pin_memory()
+    dx = torch.empty(args.tokens, H, dtype=torch.bfloat16, device=dev)
+    dl = torch.empty(args.tokens, E, dtype=torch.float32, device=dev)
+
+    def e2e_one(i):
+        l = i % len(layers)
+        dx.copy_(hx[l], non_blocking=True)
+        dl.copy_(hl[l], non_blocking=True)
+        hout.copy_(layers[l][0].forward(dx, dl), non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    n_e2e = min(args.steps, 64)
+    for i in range(3):
+        e2e_one(i)
+    dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(n_e2e):
+        e2e_one(i)
+    e2e_dt = torch.tensor([(time.perf_counter() - t0) / n_e2e], dtype=torch.float64, device=dev)
+    dist.all_reduce(e2e_dt, op=dist.ReduceOp.MAX)
+    e2e_s = float(e2e_dt.item())
+
+    # kernel events on every rank (same steps), gate_up roofline from rank 0's launches
     nprof = min(args.steps, 32)
     kt = kernel_times(_lib, torch, step, nprof)
     local_experts = [layers[i % len(layers)][0].last_local_experts for i in range(nprof)]
+    status = group.status() if group is not None else 0
     dist.barrier()
+    if group is not None:
+        group.close()
     dist.destroy_process_group()
+    if status:
+        raise RuntimeError(f"EP device status word {status:#x} on rank {rank}")
     if rank != 0:
         return None
     peak, peak_src = measured_peaks()
     gu = kt.get("gate_up_gemv", [])
-    # gate_up launches alternate: routed experts (received routes), then the shared expert
-    routed = gu[0::2]
-    byts = sum((local_experts[i % len(local_experts)]) * gate_up_bytes_per_expert()
-               for i in range(len(routed)))
+    if transport == "p2p":
+        # one gate_up launch per step: owned experts hit + the shared expert
+        routed = gu
+        byts = sum((hits[i % len(hits)] + 1) * gate_up_bytes_per_expert()
+                   for i in range(len(routed)))
+        launches = 6  # route, publish, front (sort+stage), gate_up, down, combine
+    else:
+        # launches alternate: routed experts (received routes), then the shared expert
+        routed = gu[0::2]
+        byts = sum(local_experts[i % len(local_experts)] * gate_up_bytes_per_expert()
+                   for i in range(len(routed)))
+        launches = 10  # route, 4 for received routes, 4 for the shared expert, combine
     achieved = byts / (sum(routed) * 1e-3) / 1e9 if routed else None
     value = world * args.tokens * 1e3 / ms_max
     return {
@@ -456,16 +558,26 @@ def run_ep(args, torch, rank: int, world: int, local: int):
         "data": "synthetic: seeded NVFP4 banks and N(0,1) logits/activations per BASELINE config 3",
         "config": {"workload": f"config 3 expert-parallel decode: T={args.tokens} tokens per GPU, "
                                f"H{H} I{I} E{E} top{TOPK} +1 replicated shared expert, "
-                               f"{E // world} experts per GPU, NCCL all_to_all dispatch/combine",
+                               f"{E // world} experts per GPU, transport {transport}",
+                   "transport": transport,
                    "tokens_per_step_per_gpu": args.tokens, "layers_rotated": args.layers,
+                   "owned_experts_hit_per_layer_rank0": hits,
+                   "launch": "CUDA graph per layer (route + layer), replayed" if use_graphs
+                             else "eager launches",
+                   "host_issue_ms_per_step_rank0": round(host_ms, 4),
                    "l2": f"{args.layers} distinct layer shards rotated across steps",
                    "timing": "per-rank CUDA events, max over ranks"},
+        "e2e": {"value": round(world * args.tokens / e2e_s, 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": args.tokens * (H * 2 + E * 4),
+                "d2h_bytes_per_step": args.tokens * H * 2,
+                "note": "per rank: pinned x+logits H2D, route + layer, output D2H, host sync; "
+                        "max over ranks"},
         "roofline": None if achieved is None else {
-            "kernel": "gate_up_gemv (k_gemv_tma<0>), routed launch, rank 0", "bound": "hbm",
+            "kernel": "gate_up_gemv (k_gemv_tma<0>), rank 0", "bound": "hbm",
             "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
             "frac": round(achieved / peak, 4), "peak_source": peak_src, "traffic": None},
         "kernels_ms": {k: round(statistics.mean(v), 4) for k, v in kt.items()},
-        "gpu_launches": 10 * args.steps,  # per step: route, 4 for received routes, 4 for the shared expert, combine
+        "gpu_launches": launches * args.steps,
         "clocks": clk,
     }
 

@@ -17,19 +17,6 @@ int launch_router_gemv(const uint16_t* x, const float* G, int64_t T, int H, int 
 namespace {
 thread_local char g_last_error[256] = "";
 
-// Carves 256-byte aligned sub-buffers out of a workspace.
-struct Carver {
-  char* base;
-  size_t off = 0;
-  explicit Carver(void* p) : base(static_cast<char*>(p)) {}
-  template <typename T>
-  T* take(int64_t n) {
-    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
-    off += (size_t)ceil_div((int64_t)(n * (int64_t)sizeof(T)), 256) * 256;
-    return p;
-  }
-};
-
 struct DecodeWs {
   int32_t* status;
   __half* x16;
@@ -87,24 +74,6 @@ AlignWs carve_align(void* ws, int64_t T, int top_k, int E) {
   w.padded_cnt = c.take<int32_t>(E);
   w.bytes = c.off;
   return w;
-}
-
-bool bank_ok(const ftb_nvfp4_bank* b) {
-  // every bank is a bulk-copy (TMA) source: 16-byte aligned
-  return b && b->gate_up_packed && b->gate_up_scale && b->gate_up_global && b->down_packed &&
-         b->down_scale && b->down_global && aligned16(b->gate_up_packed) &&
-         aligned16(b->gate_up_scale) && aligned16(b->gate_up_global) &&
-         aligned16(b->down_packed) && aligned16(b->down_scale) && aligned16(b->down_global);
-}
-
-BankView view_gu(const ftb_nvfp4_bank* b, const ftb_nvfp4_bank* s) {
-  return BankView{b->gate_up_packed, b->gate_up_scale, b->gate_up_global,
-                  s ? s->gate_up_packed : nullptr, s ? s->gate_up_scale : nullptr,
-                  s ? s->gate_up_global : nullptr};
-}
-BankView view_dn(const ftb_nvfp4_bank* b, const ftb_nvfp4_bank* s) {
-  return BankView{b->down_packed, b->down_scale, b->down_global, s ? s->down_packed : nullptr,
-                  s ? s->down_scale : nullptr, s ? s->down_global : nullptr};
 }
 
 }  // namespace
@@ -199,6 +168,7 @@ static int decode_impl(const uint16_t* x, const ftb_nvfp4_bank* bank, const ftb_
   sp.ids = topk_ids;
   sp.R = R;
   sp.T = T;
+  sp.Ts = T;
   sp.E = (int)E;
   sp.top_k = top_k;
   sp.has_shared = has_shared;
@@ -226,6 +196,7 @@ static int decode_impl(const uint16_t* x, const ftb_nvfp4_bank* bank, const ftb_
   dp.top_k = top_k;
   dp.T = T;
   dp.R = R;
+  dp.Ts = T;
   dp.limit = act_limit;
   dp.topk_w = topk_w;
   dp.topk_ids = topk_ids;

@@ -1,5 +1,13 @@
 // moe_decode_tma.cu - TMA-fed decode GEMVs (sm_100a), the decode path of the layer.
 //
+// Expert-major: the work tiles are rows of the activated experts' segments (built by the
+// sort kernel), so each activated expert's packed weights are read from HBM once per call
+// however many routes hit it (the reference's route-major grid re-reads them per route;
+// patches/moe_fused_nvfp4.patch:66, kernel_triton_nvfp4_fused_moe.patch:3-47). The mma's k
+// order is a fixed permutation of the row's k (lane tig owns k = kb + 32*tig + [0, 32)); the
+// activation fragments use the same permutation, so every product is the reference's and
+// only the fp32 summation order differs.
+//
 // One persistent CTA per SM owns a contiguous range of work tiles (so an expert's
 // activation rows stay hot in L1 across its tiles). Warps:
 //   producer (last warp)  streams each tile's packed E2M1 rows, E4M3 scales and fp16 global
@@ -509,7 +517,7 @@ int launch_one(const DecodeParams& P, int64_t max_tiles, cudaStream_t stream) {
 }  // namespace
 
 int launch_decode_gemvs_tma(const DecodeParams& P, cudaStream_t stream) {
-  const int64_t max_seg = max_segments(P.R, P.E, P.T, P.has_shared);
+  const int64_t max_seg = max_segments(P.R, P.E, P.Ts, P.has_shared);
   prof_mark(FTB_KERNEL_GATE_UP, true, stream);
   int st = launch_one<kGateUp>(P, max_seg * (P.I / 8), stream);
   prof_mark(FTB_KERNEL_GATE_UP, false, stream);

@@ -15,14 +15,41 @@ constexpr int kStatusTimeout = 4;       // a bounded device-side wait gave up
 constexpr int kSegRoutes = 16;
 
 // Capacity of the segment table for R routed routes, E experts and T shared-expert routes.
+// (T here is the shared expert's token count.)
 __host__ __device__ inline int64_t max_segments(int64_t R, int64_t E, int64_t T, int has_shared) {
   return (R < E ? R : E) + R / kSegRoutes + 1 + (has_shared ? T / kSegRoutes + 1 : 0);
 }
+
+// Expert-parallel group, device side: every rank's exchange region is mapped into every
+// rank's address space (CUDA IPC). world == 0 means "not expert-parallel".
+constexpr int kEpMaxWorld = 8;
+struct EpLinks {
+  int world, rank;
+  int64_t tblk;                       // tokens per rank per step
+  int e0, per, E;                     // first owned global expert, experts per rank, all experts
+  int top_k, H;
+  const uint16_t* x[kEpMaxWorld];     // rank p's published activations [tblk, H] bf16
+  const int32_t* ids[kEpMaxWorld];    // rank p's published top-k ids [tblk, top_k] (global)
+  const float* w[kEpMaxWorld];        // rank p's published routed weights [tblk, top_k]
+  const uint16_t* ic3[kEpMaxWorld];   // rank p's route outputs [world*tblk*top_k, H] bf16
+  uint32_t* in_sig[kEpMaxWorld];      // rank p's in_flag[this rank]
+  uint32_t* done_sig[kEpMaxWorld];    // rank p's done_flag[this rank]
+  const uint32_t* in_flag;            // this rank's in_flag[world]: "inputs of step n published"
+  const uint32_t* done_flag;          // this rank's done_flag[world]: "outputs of step n ready"
+  uint32_t* epoch;                    // steps completed by this rank (device counter)
+  int* done_blocks;                   // last-block detection of the combine, starts at 0
+  int32_t* ids_all;                   // [world*tblk*top_k] gathered ids, local (-1: not owned)
+  float* w_all;                       // [world*tblk*top_k] gathered routed weights
+  int64_t wait_ns;                    // bound of every flag wait
+};
 
 struct SortParams {
   const int32_t* ids;  // [R] flat topk ids
   int64_t R;           // T * top_k
   int64_t T;
+  int64_t Ts;          // shared-expert tokens: rows 0..Ts-1 (Ts <= T)
+  int skip_neg;        // negative ids are skipped without setting kStatusBadId
+  EpLinks ep;          // ep.world > 0: ids/x are gathered from the group (block 0 / blocks 1..T)
   int E;
   int top_k;
   int has_shared;
@@ -66,6 +93,7 @@ struct DecodeParams {
   BankView gu, dn;
   int H, I, E, top_k;
   int64_t T, R;
+  int64_t Ts;              // shared-expert tokens (rows 0..Ts-1 of x16)
   float limit;
   const float* topk_w;     // [R]
   const int32_t* topk_ids; // [R]
@@ -93,12 +121,44 @@ struct DecodeParams {
   int has_shared;
 };
 
+// ---- host helpers shared by the entry points ----
+
+// Carves 256-byte aligned sub-buffers out of a workspace.
+struct Carver {
+  char* base;
+  size_t off = 0;
+  explicit Carver(void* p) : base(static_cast<char*>(p)) {}
+  template <typename T>
+  T* take(int64_t n) {
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off += (size_t)ceil_div((int64_t)(n * (int64_t)sizeof(T)), 256) * 256;
+    return p;
+  }
+};
+
+inline bool bank_ok(const ftb_nvfp4_bank* b) {
+  // every bank is a bulk-copy (TMA) source: 16-byte aligned
+  return b && b->gate_up_packed && b->gate_up_scale && b->gate_up_global && b->down_packed &&
+         b->down_scale && b->down_global && aligned16(b->gate_up_packed) &&
+         aligned16(b->gate_up_scale) && aligned16(b->gate_up_global) &&
+         aligned16(b->down_packed) && aligned16(b->down_scale) && aligned16(b->down_global);
+}
+
+inline BankView view_gu(const ftb_nvfp4_bank* b, const ftb_nvfp4_bank* s) {
+  return BankView{b->gate_up_packed, b->gate_up_scale, b->gate_up_global,
+                  s ? s->gate_up_packed : nullptr, s ? s->gate_up_scale : nullptr,
+                  s ? s->gate_up_global : nullptr};
+}
+inline BankView view_dn(const ftb_nvfp4_bank* b, const ftb_nvfp4_bank* s) {
+  return BankView{b->down_packed, b->down_scale, b->down_global, s ? s->down_packed : nullptr,
+                  s ? s->down_scale : nullptr, s ? s->down_global : nullptr};
+}
+
+
 // gate_up+SwiGLU and down GEMVs, then the combine.
 int launch_decode_gemvs(const DecodeParams& P, cudaStream_t stream);
 // TMA-fed pipelined GEMVs (moe_decode_tma.cu).
 int launch_decode_gemvs_tma(const DecodeParams& P, cudaStream_t stream);
-// Register-streaming GEMVs (moe_decode.cu), kept for A/B timing.
-int launch_decode_gemvs_ldg(const DecodeParams& P, cudaStream_t stream);
 int launch_combine(const DecodeParams& P, cudaStream_t stream);
 
 // Measurement hook (ftb_profile_begin/end): records an event on `stream` before (start=true)

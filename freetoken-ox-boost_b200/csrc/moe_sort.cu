@@ -13,6 +13,7 @@
 // (no atomics decide positions).
 #include "ftb_common.cuh"
 #include "moe_kernels.cuh"
+#include "ep_sync.cuh"
 
 namespace ftb {
 
@@ -73,7 +74,7 @@ __device__ void sort_block(const SortParams& P, int* hist /* [32][E] */) {
     if (r < end) {
       e = P.ids[r];
       if (e < 0 || e >= E) {
-        atomicOr(P.status, kStatusBadId);
+        if (!(P.skip_neg && e < 0)) atomicOr(P.status, kStatusBadId);
         e = -1;
       }
     }
@@ -131,11 +132,11 @@ __device__ void sort_block(const SortParams& P, int* hist /* [32][E] */) {
     if (P.ntpp) *P.ntpp = run_pad;
     if (P.seg_expert) {
       int n = run_act;
-      if (P.has_shared && P.T > 0) {
-        for (int64_t t0 = 0; t0 < P.T; t0 += kSegRoutes, ++n) {
+      if (P.has_shared && P.Ts > 0) {
+        for (int64_t t0 = 0; t0 < P.Ts; t0 += kSegRoutes, ++n) {
           P.seg_expert[n] = E;  // marker: the shared expert
           P.seg_off[n] = (int)(R + t0);
-          P.seg_cnt[n] = (int)min((int64_t)kSegRoutes, P.T - t0);
+          P.seg_cnt[n] = (int)min((int64_t)kSegRoutes, P.Ts - t0);
         }
       }
       *P.n_seg = n;
@@ -163,7 +164,7 @@ __device__ void sort_block(const SortParams& P, int* hist /* [32][E] */) {
     __syncwarp();
   }
   if (P.has_shared && P.sorted)
-    for (int64_t t = tid; t < P.T; t += kSortThreads) P.sorted[R + t] = (int)(R + t);
+    for (int64_t t = tid; t < P.Ts; t += kSortThreads) P.sorted[R + t] = (int)(R + t);
 
   if (P.block_m > 0) {
     __syncthreads();
@@ -181,10 +182,11 @@ __device__ void sort_block(const SortParams& P, int* hist /* [32][E] */) {
   }
 }
 
-__device__ void stage_token(const SortParams& P, int64_t t) {
+// Stages token t (x16 row t, xscale[t]) from the bf16 row `src`.
+__device__ void stage_token(const SortParams& P, int64_t t, const uint16_t* src) {
   __shared__ float sm_max[32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const uint4* xr = reinterpret_cast<const uint4*>(P.x + t * P.H);
+  const uint4* xr = reinterpret_cast<const uint4*>(src);
   const int nv = P.H / 8;
   float m = 0.f;
   for (int i = tid; i < nv; i += blockDim.x) {
@@ -232,12 +234,69 @@ __device__ void stage_token(const SortParams& P, int64_t t) {
   }
 }
 
+// Expert-parallel front (P.ep.world > 0). Token slots are ordered by rank starting with this
+// one: slot block b (tokens b*tblk .. b*tblk+tblk-1) holds rank (rank + b) % world's tokens,
+// so this rank's own tokens are rows 0..tblk-1 (the shared expert's rows).
+//   every block: announce "inputs of step n published" to every rank (the publish kernel ran
+//                before this one), then wait for the ranks whose data it reads;
+//   block 0:     gathers every rank's routes, keeping those of the experts this rank owns
+//                (local ids; others -1) with their weights, then sorts them;
+//   block 1+t:   stages token slot t from its home rank's published row (a peer load).
+__device__ void ep_front(const SortParams& P, int* hist) {
+  const EpLinks& L = P.ep;
+  __shared__ int sm_ok;
+  if (threadIdx.x == 0) {
+    const uint32_t epoch = *L.epoch + 1;
+    ep_signal(L.in_sig, L.world, epoch);
+    bool ok = true;
+    if (blockIdx.x == 0) {
+      for (int p = 0; p < L.world && ok; ++p) ok = ep_wait(L.in_flag + p, epoch, L.wait_ns);
+    } else {
+      const int b = (int)(((int64_t)blockIdx.x - 1) / L.tblk);
+      ok = ep_wait(L.in_flag + (L.rank + b) % L.world, epoch, L.wait_ns);
+    }
+    if (!ok) atomicOr(P.status, kStatusTimeout);
+    sm_ok = ok;
+  }
+  __syncthreads();
+  const bool ok = sm_ok != 0;
+  if (blockIdx.x == 0) {
+    const int64_t per_rank = L.tblk * L.top_k;
+    const int64_t n = (int64_t)L.world * per_rank;
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+      const int b = (int)(i / per_rank);
+      const int64_t j = i - b * per_rank;
+      int loc = -1;
+      float w = 0.f;
+      if (ok) {
+        const int p = (L.rank + b) % L.world;
+        const int e = L.ids[p][j];
+        w = L.w[p][j];
+        if (e >= L.e0 && e < L.e0 + L.per) loc = e - L.e0;
+        if (b == 0 && (e < 0 || e >= L.E)) atomicOr(P.status, kStatusBadId);
+      }
+      L.ids_all[i] = loc;
+      L.w_all[i] = w;
+    }
+    __syncthreads();
+    sort_block(P, hist);  // P.ids == L.ids_all, P.skip_neg set
+  } else if (ok) {
+    const int64_t t = (int64_t)blockIdx.x - 1;
+    const int b = (int)(t / L.tblk);
+    const uint16_t* src = L.x[(L.rank + b) % L.world] + (t - b * L.tblk) * P.H;
+    stage_token(P, t, src);
+  }
+}
+
 __global__ void __launch_bounds__(kSortThreads) k_sort_stage(SortParams P) {
   extern __shared__ int hist[];
-  if (blockIdx.x == 0) {
+  if (P.ep.world > 0) {
+    ep_front(P, hist);
+  } else if (blockIdx.x == 0) {
     sort_block(P, hist);
   } else {
-    stage_token(P, (int64_t)blockIdx.x - 1);
+    const int64_t t = (int64_t)blockIdx.x - 1;
+    stage_token(P, t, P.x + t * P.H);
   }
 }
 

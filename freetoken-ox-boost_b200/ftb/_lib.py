@@ -26,6 +26,9 @@ FTB_ROUTE_SIGMOID = 1
 
 STATUS_BAD_ID = 1
 STATUS_F16_OVERFLOW = 2
+STATUS_TIMEOUT = 4
+
+EP_HANDLE_BYTES = 64
 
 # Every symbol include/ftb.h declares, with (restype, argtypes).
 _vp, _i32, _i64, _f32, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
@@ -62,11 +65,21 @@ SIGNATURES = {
     "ftb_moe_combine": (_i32, [_vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp]),
     "ftb_moe_decode_noalloc": (_i32, [_vp, _BP, _BP, _vp, _vp, _i64, _i32, _i32, _i32, _f32,
                                       _vp, _vp]),
+    "ftb_ep_region_bytes": (_sz, [_i32, _i64, _i32, _i32]),
+    "ftb_ep_create": (_i32, [_i32, _i32, _i64, _i32, _i32, _i32, _i32, _i32,
+                             ctypes.POINTER(_vp)]),
+    "ftb_ep_handle": (_i32, [_vp, _vp]),
+    "ftb_ep_open": (_i32, [_vp, _vp]),
+    "ftb_ep_set_wait_ns": (_i32, [_vp, _i64]),
+    "ftb_ep_forward": (_i32, [_vp, _vp, _vp, _vp, _BP, _BP, _f32, _vp, _vp]),
+    "ftb_ep_status": (_i32, [_vp, _i32, _vp]),
+    "ftb_ep_destroy": (_i32, [_vp]),
     "ftb_profile_begin": (_i32, []),
     "ftb_profile_end": (_i32, [_vp, _vp, _i32]),
 }
 
-KERNEL_NAMES = {0: "sort_stage", 1: "gate_up_gemv", 2: "down_gemv", 3: "combine", 4: "route_topk"}
+KERNEL_NAMES = {0: "sort_stage", 1: "gate_up_gemv", 2: "down_gemv", 3: "combine", 4: "route_topk",
+                5: "ep_publish", 6: "ep_combine"}
 
 
 class FtbLibraryError(RuntimeError):

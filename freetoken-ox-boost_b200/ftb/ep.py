@@ -1,31 +1,42 @@
 """Expert-parallel NVFP4 MoE layer (BASELINE configs 3 and 4): one process per GPU.
 
 Rank r owns experts [r*E/W, (r+1)*E/W) (contiguous shards) and a replica of the shared
-expert. A step on each rank, for its own T tokens:
+expert. Two transports move tokens to experts and outputs back:
+
+``"p2p"`` (default on CUDA; ``EpGroup``, libftb ``ftb_ep_*``): every rank publishes its
+tokens and routes in an exchange region that all ranks map (CUDA IPC over NVLink); the
+layer's own kernels pull the routes and rows they need, run the GEMVs over the owned
+experts, and each rank pulls its routes' outputs back and combines them. Fixed launch
+shapes, no host synchronisation, device-side step flags with bounded waits.
+
+``"nccl"`` (the collective-library baseline, and the CPU/gloo test path), per step:
   1. route (softmax top-k) on the token's home rank;
   2. sort the T*k routes by destination rank (stable, so routes stay in flat order within a
      destination) and exchange the counts (all_to_all of W int64);
-  3. dispatch: NCCL all_to_all_single of the routes' activation rows and (local expert id,
+  3. dispatch: all_to_all_single of the routes' activation rows and (local expert id,
      routed weight) metadata;
   4. each rank runs the decode kernels on its received routes as top-1 routes, so each
      route's output is bf16(acc * global * w) exactly as on one GPU (the per-route GEMV is
      batch-invariant: its bits do not depend on the other routes);
   5. combine: the reverse all_to_all_single brings each route's output home; the home rank
      sums them in k order (fp32) and adds the shared expert (computed locally) in bf16.
-Because steps 4 and 5 reproduce the single-GPU arithmetic, the W-rank output equals the
-1-GPU output bit for bit.
+  The counts exchange needs the receive sizes on the host (one device->host read per step).
+  The expert, shared-expert and combine computations are pluggable, so this transport also
+  runs on CPU gloo ranks in tests (with the CPU oracle as compute).
 
-The counts exchange needs the receive sizes on the host (one device->host read per step).
-The expert, shared-expert and combine computations are pluggable, so the dispatch/combine
-logic also runs on CPU gloo ranks in tests (with the CPU oracle as compute).
+Both reproduce the single-GPU arithmetic, so the W-rank output equals the 1-GPU output bit
+for bit.
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Callable
 
 import torch
 import torch.distributed as dist
 
+from . import _lib
+from ._runtime import ptr, require, require_cuda, stream_handle
 from .banks import Nvfp4Bank
 
 
@@ -36,13 +47,96 @@ def shard_range(num_experts: int, rank: int, world: int):
     return rank * per, (rank + 1) * per
 
 
+class EpGroup:
+    """This rank's member of a peer-memory expert-parallel group (``ftb_ep_*``): an exchange
+    region and workspace for steps of exactly ``tokens_per_rank`` tokens, shared by every
+    layer of that shape (layers run one after another on the stream).
+
+    Construction is collective: every rank of ``group`` must construct its member together
+    (the IPC handles are exchanged with ``all_gather_object``). ``close()`` is collective too
+    (it starts with a barrier)."""
+
+    def __init__(self, tokens_per_rank: int, hidden: int, inter: int, num_experts: int,
+                 top_k: int, has_shared: bool, rank: int, world: int, group=None,
+                 wait_ns: int | None = None):
+        lib = _lib.load()
+        self.T, self.H, self.I, self.E, self.K = tokens_per_rank, hidden, inter, num_experts, top_k
+        self.has_shared, self.rank, self.world, self.group = has_shared, rank, world, group
+        self.per = num_experts // world
+        h = ctypes.c_void_p()
+        _lib.check("ftb_ep_create", lib.ftb_ep_create(rank, world, tokens_per_rank, hidden,
+                                                      inter, num_experts, top_k,
+                                                      1 if has_shared else 0, ctypes.byref(h)))
+        self._h = h
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        if wait_ns is not None:
+            _lib.check("ftb_ep_set_wait_ns", lib.ftb_ep_set_wait_ns(h, int(wait_ns)))
+        if world > 1:
+            buf = ctypes.create_string_buffer(_lib.EP_HANDLE_BYTES)
+            _lib.check("ftb_ep_handle", lib.ftb_ep_handle(h, buf))
+            handles = [None] * world
+            dist.all_gather_object(handles, bytes(buf.raw), group=group)
+            joined = b"".join(handles)
+            _lib.check("ftb_ep_open", lib.ftb_ep_open(h, joined))
+
+    def forward(self, x: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor,
+                bank: Nvfp4Bank, shared: Nvfp4Bank | None, act_limit: float = float("inf"),
+                out: torch.Tensor | None = None) -> torch.Tensor:
+        if self._h is None:
+            raise RuntimeError("EpGroup is closed")
+        dev = require_cuda(x, topk_weights, topk_ids, bank.gate_up_packed)
+        require(x, "hidden_states", torch.bfloat16, (self.T, self.H))
+        require(topk_weights, "topk_weights", torch.float32, (self.T, self.K))
+        require(topk_ids, "topk_ids", torch.int32, (self.T, self.K))
+        bank.validate()
+        if bank.num_experts != self.per or bank.hidden != self.H or bank.inter != self.I:
+            raise ValueError(f"local bank must hold {self.per} experts of H{self.H} I{self.I}")
+        if (shared is not None) != self.has_shared:
+            raise ValueError("shared expert presence differs from the group's")
+        if out is None:
+            out = torch.empty(self.T, self.H, dtype=torch.bfloat16, device=dev)
+        b = bank.struct()
+        s = shared.struct() if shared is not None else None
+        st = _lib.load().ftb_ep_forward(self._h, ptr(x), ptr(topk_weights), ptr(topk_ids),
+                                        ctypes.byref(b), ctypes.byref(s) if s is not None else None,
+                                        float(act_limit), ptr(out), stream_handle(dev))
+        _lib.check("ftb_ep_forward", st)
+        return out
+
+    def status(self, clear: bool = True) -> int:
+        """The sticky device status word (synchronises the current stream)."""
+        v = _lib.load().ftb_ep_status(self._h, 1 if clear else 0, stream_handle(self.device))
+        if v < 0:
+            _lib.check("ftb_ep_status", -v)
+        return v
+
+    def close(self):
+        if self._h is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        h, self._h = self._h, None
+        _lib.check("ftb_ep_destroy", _lib.load().ftb_ep_destroy(h))
+
+
 class ExpertParallelMoE:
     """Expert-parallel routed experts + replicated shared expert of one MoE layer."""
 
     def __init__(self, local_bank: Nvfp4Bank | None, shared: Nvfp4Bank | None, num_experts: int,
                  top_k: int, rank: int, world: int, group=None, activation: str = "silu",
                  act_limit: float = 7.0, expert_fn: Callable | None = None,
-                 shared_fn: Callable | None = None, combine_fn: Callable | None = None):
+                 shared_fn: Callable | None = None, combine_fn: Callable | None = None,
+                 transport: str | None = None, ep_group: EpGroup | None = None):
+        if transport is None:  # peer memory for libftb compute on CUDA banks, else NCCL
+            on_cuda = local_bank is not None and local_bank.gate_up_packed.is_cuda
+            custom = expert_fn or shared_fn or combine_fn
+            transport = "p2p" if on_cuda and not custom else "nccl"
+        if transport not in ("nccl", "p2p"):
+            raise ValueError(f"transport {transport!r}: expected 'nccl' or 'p2p'")
+        if transport == "p2p" and (expert_fn or shared_fn or combine_fn):
+            raise ValueError("the p2p transport runs libftb's kernels; custom compute needs 'nccl'")
+        self.transport, self.ep_group = transport, ep_group
         self.E, self.K = num_experts, top_k
         self.rank, self.world, self.group = rank, world, group
         self.e0, self.e1 = shard_range(num_experts, rank, world)
@@ -86,6 +180,21 @@ class ExpertParallelMoE:
 
     def routed_forward(self, x: torch.Tensor, topk_weights: torch.Tensor,
                        topk_ids: torch.Tensor) -> torch.Tensor:
+        if self.transport == "p2p":
+            return self._p2p_forward(x, topk_weights, topk_ids)
+        return self._nccl_forward(x, topk_weights, topk_ids)
+
+    def _p2p_forward(self, x, topk_weights, topk_ids):
+        from .fused_nvfp4 import _act_limit
+
+        if self.ep_group is None:
+            self.ep_group = EpGroup(x.shape[0], x.shape[1], self.bank.inter, self.E, self.K,
+                                    self.shared is not None, self.rank, self.world, self.group)
+        limit = _act_limit(self.activation, self.act_limit)
+        return self.ep_group.forward(x, topk_weights, topk_ids, self.bank, self.shared, limit)
+
+    def _nccl_forward(self, x: torch.Tensor, topk_weights: torch.Tensor,
+                      topk_ids: torch.Tensor) -> torch.Tensor:
         T, H = x.shape
         K, W = self.K, self.world
         R = T * K

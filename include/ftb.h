@@ -162,6 +162,42 @@ FTB_API int ftb_moe_decode_noalloc(const uint16_t* x, const ftb_nvfp4_bank* bank
                                    float act_limit, uint16_t* out, ftb_stream_t stream);
 
 /*
+ * Expert-parallel decode layer over peer memory (no counterpart in the reference, which streams
+ * host-resident experts through an offload cache; here the expert set is resident and sharded).
+ * One process per GPU; rank r of `world` (<= 8) owns experts [r*E/world, (r+1)*E/world) and a
+ * replica of the shared expert (has_shared). Every step of every rank has exactly
+ * tokens_per_rank tokens.
+ * Setup, collective over the group: ftb_ep_create() on each rank (current device = its GPU;
+ * allocates its exchange region and workspace), exchange the FTB_EP_HANDLE_BYTES-byte
+ * ftb_ep_handle() of every rank on the host (any channel), then ftb_ep_open() with the handles
+ * in rank order (maps every peer's region with CUDA IPC). world == 1 needs no open.
+ * ftb_ep_forward(): one layer step on `stream`, the same result as ftb_moe_decode() of the
+ * full layer on this rank's tokens (topk ids are global expert ids; local_bank holds the
+ * owned experts, num_experts == E/world). It launches four kernels with fixed shapes and no
+ * host synchronisation; ranks order their steps with device-side flags. Every rank must call
+ * it the same number of times, in the same layer order. A flag wait that exceeds the wait
+ * bound (default 5 s, ftb_ep_set_wait_ns) gives up and sets bit 2 of the status word;
+ * bit 0 / bit 1 as for ftb_moe_decode. The status word is sticky: ftb_ep_status() returns it
+ * (>= 0; negative = -FTB_ERR_*) after synchronising `stream`, and clears it when clear != 0.
+ * After a timeout the group's step counters disagree: destroy and recreate it.
+ * ftb_ep_destroy(): call on every rank after a host barrier that follows the last step.
+ */
+#define FTB_EP_HANDLE_BYTES 64
+typedef struct ftb_ep ftb_ep;
+FTB_API size_t ftb_ep_region_bytes(int world, int64_t tokens_per_rank, int H, int top_k);
+FTB_API int ftb_ep_create(int rank, int world, int64_t tokens_per_rank, int H, int I, int E,
+                          int top_k, int has_shared, ftb_ep** out);
+FTB_API int ftb_ep_handle(const ftb_ep* ep, void* handle);
+FTB_API int ftb_ep_open(ftb_ep* ep, const void* handles);
+FTB_API int ftb_ep_set_wait_ns(ftb_ep* ep, int64_t ns);
+FTB_API int ftb_ep_forward(ftb_ep* ep, const uint16_t* x, const float* topk_w,
+                           const int32_t* topk_ids, const ftb_nvfp4_bank* local_bank,
+                           const ftb_nvfp4_bank* shared, float act_limit, uint16_t* out,
+                           ftb_stream_t stream);
+FTB_API int ftb_ep_status(ftb_ep* ep, int clear, ftb_stream_t stream);
+FTB_API int ftb_ep_destroy(ftb_ep* ep);
+
+/*
  * Measurement hooks (no counterpart in the reference): between ftb_profile_begin() and
  * ftb_profile_end() the library records a CUDA event pair on the launching stream around
  * each of its kernel launches (ids: FTB_KERNEL_*). ftb_profile_end() synchronises those
@@ -173,7 +209,9 @@ enum {
   FTB_KERNEL_GATE_UP = 1,
   FTB_KERNEL_DOWN = 2,
   FTB_KERNEL_COMBINE = 3,
-  FTB_KERNEL_ROUTE = 4
+  FTB_KERNEL_ROUTE = 4,
+  FTB_KERNEL_EP_PUBLISH = 5,
+  FTB_KERNEL_EP_COMBINE = 6
 };
 FTB_API int ftb_profile_begin(void);
 FTB_API int ftb_profile_end(int32_t* kernel_ids, float* ms, int max_n);

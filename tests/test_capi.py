@@ -64,3 +64,22 @@ def test_bad_shapes_rejected_before_any_launch():
     st = lib.ftb_moe_decode(None, ctypes.byref(b), None, None, None, 0, 256, 128, 2, 1.0, None,
                             None, 0, None)
     assert st == _lib.FTB_OK
+
+
+def test_ep_host_checks():
+    """Expert-parallel group: region size is a host-only query, and bad group arguments are
+    rejected before any device call."""
+    import ctypes
+
+    lib = _lib.load()
+    T, H, K, W = 64, 4096, 8, 2
+    want = 256 + 256 + T * H * 2 + T * K * 4 + T * K * 4 + W * T * K * H * 2
+    assert lib.ftb_ep_region_bytes(W, T, H, K) == want
+    h = ctypes.c_void_p()
+    assert lib.ftb_ep_create(0, 9, T, H, 1536, 256, K, 1, ctypes.byref(h)) == _lib.FTB_ERR_ARG
+    assert lib.ftb_ep_create(2, 2, T, H, 1536, 256, K, 1, ctypes.byref(h)) == _lib.FTB_ERR_ARG
+    assert lib.ftb_ep_create(0, 3, T, H, 1536, 256, K, 1, ctypes.byref(h)) == _lib.FTB_ERR_SHAPE
+    assert lib.ftb_ep_create(0, 2, T, 100, 1536, 256, K, 1, ctypes.byref(h)) == _lib.FTB_ERR_SHAPE
+    assert not h.value
+    assert lib.ftb_ep_destroy(None) == _lib.FTB_OK
+    assert lib.ftb_ep_forward(None, None, None, None, None, None, 0.0, None, None) == _lib.FTB_ERR_ARG

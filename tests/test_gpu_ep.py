@@ -1,16 +1,24 @@
-"""Expert parallelism on 2 GPUs (NCCL): each rank's output equals the single-GPU decode of
-the same tokens with the full bank, bit for bit. Skipped with fewer than 2 GPUs."""
+"""Expert parallelism on the GPU.
+
+* 1 GPU: an ``EpGroup`` of world 1 (the peer-memory path with no peers) returns the
+  single-GPU decode bit for bit, over several steps and two layers sharing the group.
+* 2 GPUs, both transports (NCCL all_to_all and peer memory): each rank's output equals the
+  single-GPU decode of the same tokens with the full bank, bit for bit, over several steps.
+* 2 GPUs, peer memory: a rank that stops stepping makes its peer's bounded flag waits give
+  up and report the timeout bit, with the peer's process and GPU still usable.
+Multi-GPU cases are skipped with fewer than 2 GPUs.
+"""
 import datetime
 import os
 import socket
 
-import numpy as np
 import pytest
 import torch
 import torch.multiprocessing as mp
 
 pytestmark = pytest.mark.gpu
 W = 2
+E, H, I, T, K = 16, 512, 256, 9, 4
 
 
 def _port():
@@ -19,47 +27,104 @@ def _port():
         return s.getsockname()[1]
 
 
-def _worker(rank, port, out_dir):
+def _paths():
     import sys
-
-    import torch.distributed as dist
 
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     for p in (root, os.path.join(root, "freetoken-ox-boost_b200")):
         if p not in sys.path:
             sys.path.insert(0, p)
+
+
+def test_ep_world1_p2p_bit_exact():
     import ftb
     from ftb import synth
-    from ftb.ep import ExpertParallelMoE, shard_range
+    from ftb.ep import EpGroup, ExpertParallelMoE
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    banks = [synth.make_bank(E, H, I, seed=s, device=dev) for s in (11, 12)]
+    shared = [synth.make_shared(H, I, seed=s, device=dev) for s in (11, 12)]
+    group = EpGroup(T, H, I, E, K, True, 0, 1)
+    layers = [ExpertParallelMoE(b, s, E, K, 0, 1, transport="p2p", ep_group=group)
+              for b, s in zip(banks, shared)]
+    try:
+        for step in range(4):
+            layer = step % 2
+            inp = synth.make_inputs(T, H, E, seed=100 + step, device=dev)
+            w, ids = ftb.fused_topk(inp.x, inp.logits, K, True)
+            if step == 3:
+                ids = ids.clone()
+                ids[2, 1] = E + 3  # out of range: skipped, status bit 0
+            out = layers[layer].routed_forward(inp.x, w, ids)
+            ref = ftb.moe_decode(inp.x, banks[layer], w, ids, shared=shared[layer])
+            torch.cuda.synchronize()
+            assert torch.equal(out.view(torch.int16), ref.view(torch.int16)), step
+        assert group.status() == 1  # the planted bad id, nothing else
+        assert group.status() == 0  # cleared
+    finally:
+        group.close()
+
+
+def _worker(rank, port, out_dir, transport, mode):
+    _paths()
+    import torch.distributed as dist
+
+    import ftb
+    from ftb import synth
+    from ftb.ep import EpGroup, ExpertParallelMoE, shard_range
 
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     dev = torch.device("cuda", rank)
     torch.cuda.set_device(dev)
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
                             world_size=W, timeout=datetime.timedelta(seconds=60), device_id=dev)
+    result = "error"
+    group = None
     try:
-        E, H, I, T, K = 16, 512, 256, 9, 4
         full = synth.make_bank(E, H, I, seed=5, device=dev)
         shared = synth.make_shared(H, I, seed=5, device=dev)
         e0, e1 = shard_range(E, rank, W)
-        ep = ExpertParallelMoE(full.select(slice(e0, e1)), shared, E, K, rank, W)
-        inp = synth.make_inputs(T, H, E, seed=5, stream=rank, device=dev)
-        out = ep.forward(inp.x, inp.logits)
-        w, ids = ftb.fused_topk(inp.x, inp.logits, K, True)
-        ref = ftb.moe_decode(inp.x, full, w, ids, shared=shared)
-        torch.cuda.synchronize()
-        same = bool(torch.equal(out.view(torch.int16), ref.view(torch.int16)))
-        with open(os.path.join(out_dir, f"r{rank}.txt"), "w") as f:
-            f.write("same" if same else "differ")
+        if transport == "p2p":
+            group = EpGroup(T, H, I, E, K, True, rank, W,
+                            wait_ns=200_000_000 if mode == "dead_peer" else None)
+        ep = ExpertParallelMoE(full.select(slice(e0, e1)), shared, E, K, rank, W,
+                               transport=transport, ep_group=group)
+        if mode == "dead_peer":
+            # rank 1 never steps; rank 0's waits must give up and say so
+            if rank == 0:
+                inp = synth.make_inputs(T, H, E, seed=5, stream=rank, device=dev)
+                ep.forward(inp.x, inp.logits)
+                torch.cuda.synchronize()
+                st = group.status()
+                probe = torch.ones(4, device=dev).sum().item()  # the context still works
+                result = f"status={st} probe={probe:.0f}"
+            else:
+                result = "idle"
+        else:
+            same = True
+            for step in range(3):
+                inp = synth.make_inputs(T, H, E, seed=5 + step, stream=rank, device=dev)
+                out = ep.forward(inp.x, inp.logits)
+                w, ids = ftb.fused_topk(inp.x, inp.logits, K, True)
+                ref = ftb.moe_decode(inp.x, full, w, ids, shared=shared)
+                torch.cuda.synchronize()
+                same = same and bool(torch.equal(out.view(torch.int16), ref.view(torch.int16)))
+            st = group.status() if group is not None else 0
+            result = "same" if same and st == 0 else f"differ (status {st})"
     finally:
+        with open(os.path.join(out_dir, f"r{rank}.txt"), "w") as f:
+            f.write(result)
+        if group is not None:
+            group.close()
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < W, reason="needs 2 GPUs")
-def test_ep_two_gpus_bit_exact(tmp_path):
+def _spawn(tmp_path, transport, mode="parity"):
     ctx = mp.get_context("spawn")
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, port, str(tmp_path))) for r in range(W)]
+    procs = [ctx.Process(target=_worker, args=(r, port, str(tmp_path), transport, mode))
+             for r in range(W)]
     for p in procs:
         p.start()
     for p in procs:
@@ -67,5 +132,17 @@ def test_ep_two_gpus_bit_exact(tmp_path):
     for p in procs:
         if p.is_alive():
             p.kill()
-    for r in range(W):
-        assert (tmp_path / f"r{r}.txt").read_text() == "same"
+    return [(tmp_path / f"r{r}.txt").read_text() for r in range(W)]
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < W, reason="needs 2 GPUs")
+@pytest.mark.parametrize("transport", ["nccl", "p2p"])
+def test_ep_two_gpus_bit_exact(tmp_path, transport):
+    assert _spawn(tmp_path, transport) == ["same", "same"]
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < W, reason="needs 2 GPUs")
+def test_ep_p2p_dead_peer_times_out(tmp_path):
+    r0, r1 = _spawn(tmp_path, "p2p", "dead_peer")
+    assert r1 == "idle"
+    assert r0 == "status=4 probe=4", r0

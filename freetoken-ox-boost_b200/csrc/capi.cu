@@ -147,7 +147,7 @@ static int decode_impl(const uint16_t* x, const ftb_nvfp4_bank* bank, const ftb_
                        uint16_t* dbg_ic3, uint16_t* dbg_sic1, uint16_t* dbg_sh,
                        uint16_t* dbg_sout, cudaStream_t stream) {
   if (T < 0 || H <= 0 || I <= 0 || top_k < 1) return FTB_ERR_SHAPE;
-  if (H % 128 || I % 128) return FTB_ERR_SHAPE;
+  if (H % 256 || I % 256) return FTB_ERR_SHAPE;
   if (!bank_ok(bank) || (shared && !bank_ok(shared))) return FTB_ERR_ARG;
   const int64_t E = bank->num_experts;
   if (E < 1 || E > 1024 || (shared && shared->num_experts < 1)) return FTB_ERR_SHAPE;

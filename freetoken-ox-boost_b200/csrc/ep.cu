@@ -272,7 +272,7 @@ int ftb_ep_create(int rank, int world, int64_t tokens_per_rank, int H, int I, in
   if (!out) return FTB_ERR_ARG;
   *out = nullptr;
   if (world < 1 || world > kEpMaxWorld || rank < 0 || rank >= world) return FTB_ERR_ARG;
-  if (tokens_per_rank < 1 || H <= 0 || I <= 0 || H % 128 || I % 128 || top_k < 1 || top_k > 32)
+  if (tokens_per_rank < 1 || H <= 0 || I <= 0 || H % 256 || I % 256 || top_k < 1 || top_k > 32)
     return FTB_ERR_SHAPE;
   if (E < 1 || E % world || E / world > 1024 || top_k > E) return FTB_ERR_SHAPE;
   if ((int64_t)world * tokens_per_rank * (top_k + 1) >= (int64_t(1) << 31)) return FTB_ERR_SHAPE;

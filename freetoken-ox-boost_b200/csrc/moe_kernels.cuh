@@ -14,6 +14,13 @@ constexpr int kStatusTimeout = 4;       // a bounded device-side wait gave up
 // an expert with more routes is split into several segments.
 constexpr int kSegRoutes = 16;
 
+// Activation rows (x16, h16) are stored "round-interleaved": in each 128-k round, the 16-byte
+// chunk holding k = 32*tig + 8q .. +8 sits at chunk position 4q + tig, the order in which a
+// GEMV lane (tig) reads its mma fragments. Maps a logical 16-byte chunk index to its position.
+__host__ __device__ __forceinline__ int64_t ri_chunk(int64_t c) {
+  return (c & ~int64_t(15)) | ((c & 3) << 2) | ((c >> 2) & 3);
+}
+
 // Capacity of the segment table for R routed routes, E experts and T shared-expert routes.
 // (T here is the shared expert's token count.)
 __host__ __device__ inline int64_t max_segments(int64_t R, int64_t E, int64_t T, int has_shared) {

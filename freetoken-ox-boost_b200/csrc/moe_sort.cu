@@ -6,7 +6,8 @@
 //                BLOCK_M-padded sorted_ids / expert_ids of moe_align_block_size;
 //   blocks 1..T  one token each: bf16 row -> f16 row scaled by 2^-s (s from the row's max
 //                exponent so that max|x|*2^-s lies in [2^14, 2^15): the f16 tensor-core
-//                operand is then exact for every element within 2^-31 of the row max).
+//                operand is then exact for every element within 2^-31 of the row max),
+//                stored round-interleaved (ri_chunk) for the GEMV's fragment loads.
 //
 // The sort is single-CTA: 32 warps each own a contiguous chunk of routes; __match_any_sync
 // ranks equal experts inside a 32-route group, so the result is the same on every run
@@ -230,7 +231,7 @@ __device__ void stage_token(const SortParams& P, int64_t t, const uint16_t* src)
                                           __uint_as_float(w[j] & 0xffff0000u) * down);
       o[j] = *reinterpret_cast<const uint32_t*>(&h);
     }
-    yr[i] = make_uint4(o[0], o[1], o[2], o[3]);
+    yr[ri_chunk(i)] = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 

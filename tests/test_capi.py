@@ -54,14 +54,15 @@ def test_bad_shapes_rejected_before_any_launch():
     assert lib.ftb_route_topk(None, 4, 64, 33, 0, None, 1.0, 1, None, None, None) == _lib.FTB_ERR_SHAPE
     assert lib.ftb_route_topk(None, 4, 2048, 8, 0, None, 1.0, 1, None, None, None) == _lib.FTB_ERR_SHAPE
     assert lib.ftb_route_topk(None, 4, 64, 8, 7, None, 1.0, 1, None, None, None) == _lib.FTB_ERR_ARG
-    # H not a multiple of 128
+    # H and I must be multiples of 256 (TMA row strides of the scale banks)
     b = _lib.Nvfp4BankStruct(16, 16, 16, 16, 16, 16, 8)
     import ctypes
-    st = lib.ftb_moe_decode(None, ctypes.byref(b), None, None, None, 4, 100, 128, 2, 1.0, None,
-                            None, 0, None)
-    assert st == _lib.FTB_ERR_SHAPE
+    for h, i in ((100, 256), (384, 256), (256, 128), (256, 384)):
+        st = lib.ftb_moe_decode(None, ctypes.byref(b), None, None, None, 4, h, i, 2, 1.0, None,
+                                None, 0, None)
+        assert st == _lib.FTB_ERR_SHAPE, (h, i)
     # T == 0 is a no-op
-    st = lib.ftb_moe_decode(None, ctypes.byref(b), None, None, None, 0, 256, 128, 2, 1.0, None,
+    st = lib.ftb_moe_decode(None, ctypes.byref(b), None, None, None, 0, 256, 256, 2, 1.0, None,
                             None, 0, None)
     assert st == _lib.FTB_OK
 

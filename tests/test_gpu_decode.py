@@ -31,7 +31,7 @@ def run_gpu(case, limit=float("inf"), debug=True, activation=None):
 
 @pytest.mark.parametrize("T", [1, 3, 17])
 def test_decode_small_with_shared(T):
-    case = build_case(8, 256, 128, T, 2, seed=T)
+    case = build_case(8, 256, 256, T, 2, seed=T)
     ref = oracle_layer(case)
     out, it = run_gpu(case)
     torch.cuda.synchronize()
@@ -78,7 +78,7 @@ def test_decode_hot_expert_many_routes():
     T, K, E = 40, 2, 8
     ids = np.stack([np.full(T, 3), np.arange(T) % E], 1).astype(np.int32)
     ids[:, 1] = np.where(ids[:, 1] == 3, 4, ids[:, 1])
-    case = build_case(E, 256, 128, T, K, seed=5, ids=ids)
+    case = build_case(E, 256, 256, T, K, seed=5, ids=ids)
     ref = oracle_layer(case)
     out, _ = run_gpu(case)
     assert compare(to_f32(out), ref["out"])[0] <= TOL
@@ -86,7 +86,7 @@ def test_decode_hot_expert_many_routes():
 
 def test_batch_invariance_bitwise():
     """A token's output bits do not depend on the rest of the batch."""
-    case = build_case(8, 256, 128, 9, 2, seed=9)
+    case = build_case(8, 256, 256, 9, 2, seed=9)
     full, _ = run_gpu(case)
     sub = dict(case)
     sub["inp"] = synth.Inputs(case["inp"].x[2:5].clone(), case["inp"].logits[2:5].clone())
@@ -96,7 +96,7 @@ def test_batch_invariance_bitwise():
 
 
 def test_bad_ids_flagged_and_skipped():
-    case = build_case(8, 256, 128, 3, 2, seed=4, shared=False)
+    case = build_case(8, 256, 256, 3, 2, seed=4, shared=False)
     case["ids"] = case["ids"].copy()
     case["ids"][1, 1] = 99
     out, it = run_gpu(case)
@@ -110,7 +110,7 @@ def test_bad_ids_flagged_and_skipped():
 
 
 def test_empty_batch():
-    case = build_case(8, 256, 128, 1, 2, seed=1)
+    case = build_case(8, 256, 256, 1, 2, seed=1)
     bank = case["bank"].to(DEV)
     x = torch.empty(0, 256, dtype=torch.bfloat16, device=DEV)
     out = ftb.moe_decode(x, bank, torch.empty(0, 2, device=DEV),

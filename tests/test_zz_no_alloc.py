@@ -44,7 +44,7 @@ def _noalloc(case, limit=float("inf")):
 
 
 def test_noalloc_matches_workspace_entry_point_twice():
-    first = build_case(8, 256, 128, 17, 2, seed=41)
+    first = build_case(8, 256, 256, 17, 2, seed=41)
     second = build_case(8, 256, 256, 3, 2, seed=42)
     for case in (first, second):
         out, ref = _noalloc(case)

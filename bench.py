@@ -366,8 +366,9 @@ def run_ftb_single(args, torch):
 
 
 def sweep_decode(torch, ftb, layers: "Layers", args):
-    """Tokens/s at T = 1, 4, 16 on the same layer banks (fresh routing per T)."""
-    from ftb import synth
+    """Tokens/s at T = 1, 4, 16 on the same layer banks (fresh routing per T), with each
+    kernel's eager CUDA-event time."""
+    from ftb import _lib, synth
 
     res = {}
     for T in (1, 4, 16):
@@ -387,8 +388,11 @@ def sweep_decode(torch, ftb, layers: "Layers", args):
         for i in range(3):
             timed(i)
         ms = time_steps(torch, timed, min(max(8, args.steps), 200))
+        host_ms = time_steps.host_ms
+        kt = kernel_times(_lib, torch, step, 16)
         res[f"T={T}"] = {"tokens_per_s": round(T * 1e3 / ms, 1), "ms_per_step": round(ms, 4),
-                         "host_issue_ms_per_step": round(time_steps.host_ms, 4)}
+                         "host_issue_ms_per_step": round(host_ms, 4),
+                         "kernels_ms": {k: round(statistics.mean(v), 4) for k, v in kt.items()}}
     return res
 
 

@@ -45,6 +45,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <unordered_map>
 
@@ -53,9 +54,6 @@
 namespace ftb {
 namespace {
 
-constexpr int kConsumerWarps = 8;
-constexpr int kThreads = (kConsumerWarps + 1) * kWarp;
-constexpr int kProducerWarp = kConsumerWarps;
 constexpr int kMaxStages = 8;
 constexpr int kSmemLimit = 227 * 1024;
 constexpr int kStageK = 256;               // k per stage (two 128-k rounds)
@@ -80,9 +78,10 @@ struct Layout {
   int total;
 };
 
-__host__ __device__ inline Layout make_layout(int G) {
+// NW consumer warps x MT m16 tiles each: RT = 16 * NW * MT rows per tile.
+__host__ __device__ inline Layout make_layout(int MT, int NW) {
   Layout L;
-  L.RT = 128 * G;
+  L.RT = 16 * NW * MT;
   L.wbytes = L.RT * 128;
   L.sbytes = L.RT * 16;
   L.s_off = L.wbytes;
@@ -137,7 +136,7 @@ __device__ __forceinline__ int tile_rows_total(const DecodeParams& P) {
 // arms the full barrier with the stage's byte count, publishes the tile id and issues the
 // copies (lane 0: the TMA boxes; lanes j < cnt: activation row j). Ends with one sentinel
 // stage (tile -1) that all consumer warps read.
-template <int MODE, int G>
+template <int MODE>
 __device__ void producer(const DecodeParams& P, const GemvMaps& M, const Layout& L,
                          uint8_t* stages, const Sync& sy, int64_t ntiles, int tpe, int nk,
                          int* work_counter) {
@@ -256,22 +255,22 @@ __device__ __forceinline__ void dequant16(const uint4& w, uint32_t s_lo, uint32_
 }
 
 // Swizzle lines of the two A rows (g, g+8) of the warp's m16 tile m.
-template <int MODE, int G>
+template <int MODE, int MT, int NW>
 __device__ __forceinline__ void a_lines(int w, int m, int g, int& l0, int& l1) {
-  const int mi = G * w + m;
+  const int mi = MT * w + m;
   if (MODE == kGateUp) {
     l0 = 8 * mi + rho(g);        // gate rows: lines [0, RT/2)
-    l1 = 64 * G + l0;            // up rows:   lines [RT/2, RT)
+    l1 = 8 * MT * NW + l0;       // up rows:   lines [RT/2, RT)
   } else {
     l0 = 16 * mi + rho(g);
     l1 = l0 + 8;
   }
 }
 
-// One 128-k round (kh = 0/1 of the stage) for the warp's G m16 tiles and NT n-tiles.
-template <int MODE, int G, int NT>
+// One 128-k round (kh = 0/1 of the stage) for the warp's MT m16 tiles and NT n-tiles.
+template <int MODE, int MT, int NW, int NT>
 __device__ __forceinline__ void stage_round(const uint8_t* st, const Layout& L, int w, int lane,
-                                            int kh, float (&acc)[G][NT][4]) {
+                                            int kh, float (&acc)[MT][NT][4]) {
   const int g = lane >> 2, tig = lane & 3;
   uint4 xb[NT][4];
 #pragma unroll
@@ -281,9 +280,9 @@ __device__ __forceinline__ void stage_round(const uint8_t* st, const Layout& L, 
       xb[nt][q] = *reinterpret_cast<const uint4*>(st + L.x_off + (8 * nt + g) * kXPitch +
                                                   256 * kh + (4 * q + tig) * 16);
 #pragma unroll
-  for (int m = 0; m < G; ++m) {
+  for (int m = 0; m < MT; ++m) {
     int l0, l1;
-    a_lines<MODE, G>(w, m, g, l0, l1);
+    a_lines<MODE, MT, NW>(w, m, g, l0, l1);
     const uint4 w0 = *reinterpret_cast<const uint4*>(st + swz(l0, 4 * kh + tig));
     const uint4 w1 = *reinterpret_cast<const uint4*>(st + swz(l1, 4 * kh + tig));
     const uint32_t sx0 =
@@ -309,36 +308,87 @@ __device__ __forceinline__ void stage_round(const uint8_t* st, const Layout& L, 
 // Position of logical k index n in a round-interleaved activation row.
 __device__ __forceinline__ int64_t ri_pos(int n) { return ri_chunk(n >> 3) * 8 + (n & 7); }
 
+// Everything the epilogue reads from global memory: per column j = 8nt + 2tig + jj of the
+// segment the route id (-1 past cnt) and its factor (gate_up: the token's 2^s; down: the
+// routed weight, 1 for the shared expert), and the fp16 global scales of the lane's two rows
+// per m16 tile.
+template <int MT, int NT>
+struct EpiPre {
+  int r[NT][2];
+  float f[NT][2];
+  float g0[MT], g1[MT];
+};
+
+template <int MODE, int MT, int NW, int NT>
+__device__ __forceinline__ void epi_prefetch(const DecodeParams& P, EpiPre<MT, NT>& q, int w,
+                                             int lane, int p, int e, int off, int cnt) {
+  const int g = lane >> 2, tig = lane & 3;
+  const bool sh = (e == P.E);
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int jj = 0; jj < 2; ++jj) {
+      const int j = nt * 8 + 2 * tig + jj;
+      q.r[nt][jj] = j < cnt ? P.sorted[off + j] : -1;
+    }
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int jj = 0; jj < 2; ++jj) {
+      const int r = q.r[nt][jj];
+      float f = 1.f;
+      if (r >= 0) {
+        if (MODE == kGateUp)
+          f = P.xscale[sh ? (int64_t)r - P.R : (int64_t)r / P.top_k];
+        else if (!sh)
+          f = P.topk_w[r];
+      }
+      q.f[nt][jj] = f;
+    }
+#pragma unroll
+  for (int m = 0; m < MT; ++m) {
+    if (MODE == kGateUp) {
+      const int I = P.I;
+      const uint16_t* glob = sh ? P.gu.s_global : P.gu.global + (int64_t)e * 2 * I;
+      const int ng = 8 * MT * NW * p + 8 * (MT * w + m) + rho(g);
+      q.g0[m] = __half2float(__ushort_as_half(glob[ng]));
+      q.g1[m] = __half2float(__ushort_as_half(glob[I + ng]));
+    } else {
+      const uint16_t* glob = sh ? P.dn.s_global : P.dn.global + (int64_t)e * P.H;
+      const int na = 16 * MT * NW * p + 16 * (MT * w + m) + rho(g);
+      q.g0[m] = __half2float(__ushort_as_half(glob[na]));
+      q.g1[m] = __half2float(__ushort_as_half(glob[na + 8]));
+    }
+  }
+}
+
 // gate_up epilogue: lane (g, tig) holds, for m16 tile m, gate (c 0/1) and up (c 2/3) of row
 // j = (RT/2) p + 8 mi + rho(g) for routes 8nt + 2tig + {0, 1} of the segment.
-template <int G, int NT>
-__device__ void epi_gate_up(const DecodeParams& P, const float (&acc)[G][NT][4], int w, int lane,
-                            int p, int e, int off, int cnt) {
+template <int MT, int NW, int NT>
+__device__ void epi_gate_up(const DecodeParams& P, const float (&acc)[MT][NT][4],
+                            const EpiPre<MT, NT>& q, int w, int lane, int p, int e, int off) {
   const int g = lane >> 2, tig = lane & 3;
   const bool sh = (e == P.E);
   const int I = P.I;
-  const uint16_t* glob = sh ? P.gu.s_global : P.gu.global + (int64_t)e * 2 * I;
 #pragma unroll
-  for (int m = 0; m < G; ++m) {
-    const int ng = 64 * G * p + 8 * (G * w + m) + rho(g);
-    const float glg = __half2float(__ushort_as_half(glob[ng]));
-    const float glu = __half2float(__ushort_as_half(glob[I + ng]));
+  for (int m = 0; m < MT; ++m) {
+    const int ng = 8 * MT * NW * p + 8 * (MT * w + m) + rho(g);
     const int64_t hp = ri_pos(ng);
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
       for (int jj = 0; jj < 2; ++jj) {
+        const int r = q.r[nt][jj];
+        if (r < 0) continue;
         const int j = nt * 8 + 2 * tig + jj;
-        if (j >= cnt) continue;
-        const int r = P.sorted[off + j];
-        const int64_t t = sh ? (int64_t)r - P.R : (int64_t)r / P.top_k;
-        const float xs = P.xscale[t];
-        const float gv = bf16_round((acc[m][nt][jj] * xs) * glg);
-        const float uv = bf16_round((acc[m][nt][2 + jj] * xs) * glu);
+        const float xs = q.f[nt][jj];
+        const float gv = bf16_round((acc[m][nt][jj] * xs) * q.g0[m]);
+        const float uv = bf16_round((acc[m][nt][2 + jj] * xs) * q.g1[m]);
         const float hv = bf16_round(swiglu_f32(gv, uv, P.limit));
         if (fabsf(hv) > 65504.f) atomicOr(P.status, kStatusF16Overflow);
         P.h16[(int64_t)(off + j) * I + hp] = __float2half_rn(hv);
         if (sh) {
+          const int64_t t = (int64_t)r - P.R;
           if (P.dbg_sic1) {
             P.dbg_sic1[t * 2 * I + ng] = f32_to_bf16_bits(gv);
             P.dbg_sic1[t * 2 * I + I + ng] = f32_to_bf16_bits(uv);
@@ -357,33 +407,29 @@ __device__ void epi_gate_up(const DecodeParams& P, const float (&acc)[G][NT][4],
 }
 
 // down epilogue: lane holds rows na = RT p + 16 mi + rho(g) (c 0/1) and na + 8 (c 2/3).
-template <int G, int NT>
-__device__ void epi_down(const DecodeParams& P, const float (&acc)[G][NT][4], int w, int lane,
-                         int p, int e, int off, int cnt) {
-  const int g = lane >> 2, tig = lane & 3;
+template <int MT, int NW, int NT>
+__device__ void epi_down(const DecodeParams& P, const float (&acc)[MT][NT][4],
+                         const EpiPre<MT, NT>& q, int w, int lane, int p, int e) {
+  const int g = lane >> 2;
   const bool sh = (e == P.E);
   const int H = P.H;
-  const uint16_t* glob = sh ? P.dn.s_global : P.dn.global + (int64_t)e * H;
 #pragma unroll
-  for (int m = 0; m < G; ++m) {
-    const int na = 128 * G * p + 16 * (G * w + m) + rho(g), nb = na + 8;
-    const float ga = __half2float(__ushort_as_half(glob[na]));
-    const float gb = __half2float(__ushort_as_half(glob[nb]));
+  for (int m = 0; m < MT; ++m) {
+    const int na = 16 * MT * NW * p + 16 * (MT * w + m) + rho(g), nb = na + 8;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
       for (int jj = 0; jj < 2; ++jj) {
-        const int j = nt * 8 + 2 * tig + jj;
-        if (j >= cnt) continue;
-        const int r = P.sorted[off + j];
+        const int r = q.r[nt][jj];
+        if (r < 0) continue;
         if (sh) {
           const int64_t t = (int64_t)r - P.R;
-          P.ic3s[t * H + na] = f32_to_bf16_bits(acc[m][nt][jj] * ga);
-          P.ic3s[t * H + nb] = f32_to_bf16_bits(acc[m][nt][2 + jj] * gb);
+          P.ic3s[t * H + na] = f32_to_bf16_bits(acc[m][nt][jj] * q.g0[m]);
+          P.ic3s[t * H + nb] = f32_to_bf16_bits(acc[m][nt][2 + jj] * q.g1[m]);
         } else {
-          const float wr = P.topk_w[r];
-          P.ic3[(int64_t)r * H + na] = f32_to_bf16_bits((acc[m][nt][jj] * ga) * wr);
-          P.ic3[(int64_t)r * H + nb] = f32_to_bf16_bits((acc[m][nt][2 + jj] * gb) * wr);
+          const float wr = q.f[nt][jj];
+          P.ic3[(int64_t)r * H + na] = f32_to_bf16_bits((acc[m][nt][jj] * q.g0[m]) * wr);
+          P.ic3[(int64_t)r * H + nb] = f32_to_bf16_bits((acc[m][nt][2 + jj] * q.g1[m]) * wr);
         }
       }
     }
@@ -392,13 +438,13 @@ __device__ void epi_down(const DecodeParams& P, const float (&acc)[G][NT][4], in
 
 // The warp's share of one tile: nk stages starting at ring position i (whose full barrier
 // the caller has already waited on). Returns the next ring position, or -1 on abort.
-template <int MODE, int G, int NT>
+template <int MODE, int MT, int NW, int NT>
 __device__ int64_t warp_tile(const DecodeParams& P, const Layout& L, uint8_t* stages,
                              const Sync& sy, int64_t i, int nk, int K, int w, int lane, int p,
                              int e, int off, int cnt) {
-  float acc[G][NT][4];
+  float acc[MT][NT][4];
 #pragma unroll
-  for (int m = 0; m < G; ++m)
+  for (int m = 0; m < MT; ++m)
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -407,23 +453,27 @@ __device__ int64_t warp_tile(const DecodeParams& P, const Layout& L, uint8_t* st
     const int s = (int)(i % L.stages);
     if (kc > 0 && !sy.wait(&sy.full[s], (uint32_t)(i / L.stages) & 1u)) return -1;
     const uint8_t* st = stages + (size_t)s * L.stage_bytes;
-    stage_round<MODE, G, NT>(st, L, w, lane, 0, acc);
-    if (K - kc * kStageK > 128) stage_round<MODE, G, NT>(st, L, w, lane, 1, acc);
+    stage_round<MODE, MT, NW, NT>(st, L, w, lane, 0, acc);
+    if (K - kc * kStageK > 128) stage_round<MODE, MT, NW, NT>(st, L, w, lane, 1, acc);
     __syncwarp();
     if (lane == 0) mbar_arrive(&sy.empty[s]);
   }
+  // (loading these at the tile's start, to hide their latency, measured slower: it holds
+  // registers through the stage loop)
+  EpiPre<MT, NT> q;
+  epi_prefetch<MODE, MT, NW, NT>(P, q, w, lane, p, e, off, cnt);
   if (MODE == kGateUp)
-    epi_gate_up<G, NT>(P, acc, w, lane, p, e, off, cnt);
+    epi_gate_up<MT, NW, NT>(P, acc, q, w, lane, p, e, off);
   else
-    epi_down<G, NT>(P, acc, w, lane, p, e, off, cnt);
+    epi_down<MT, NW, NT>(P, acc, q, w, lane, p, e);
   return i;
 }
 
-template <int MODE, int G>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int MODE, int MT, int NW>
+__global__ void __launch_bounds__((NW + 1) * kWarp, 1)
     k_gemv_tma(const __grid_constant__ DecodeParams P, const __grid_constant__ GemvMaps M) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  const Layout L = make_layout(G);
+  const Layout L = make_layout(MT, NW);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + kMaxStages;
   int64_t* tile_of = reinterpret_cast<int64_t*>(empty + kMaxStages);
@@ -433,7 +483,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < L.stages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumerWarps);
+      mbar_init(&empty[s], NW);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -444,8 +494,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nk = (K + kStageK - 1) / kStageK;
   const int tpe = tile_rows_total<MODE>(P) / L.RT;
   const int64_t ntiles = (int64_t)(*P.n_seg) * tpe;
-  if (warp == kProducerWarp) {
-    producer<MODE, G>(P, M, L, stages, sy, ntiles, tpe, nk, P.work_counter + MODE);
+  if (warp == NW) {
+    producer<MODE>(P, M, L, stages, sy, ntiles, tpe, nk, P.work_counter + MODE);
     return;
   }
   int64_t i = 0;
@@ -457,9 +507,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int a = (int)(tile / tpe), p = (int)(tile % tpe);
     const int e = P.seg_expert[a], off = P.seg_off[a], cnt = P.seg_cnt[a];
     if (cnt > 8)
-      i = warp_tile<MODE, G, 2>(P, L, stages, sy, i, nk, K, warp, lane, p, e, off, cnt);
+      i = warp_tile<MODE, MT, NW, 2>(P, L, stages, sy, i, nk, K, warp, lane, p, e, off, cnt);
     else
-      i = warp_tile<MODE, G, 1>(P, L, stages, sy, i, nk, K, warp, lane, p, e, off, cnt);
+      i = warp_tile<MODE, MT, NW, 1>(P, L, stages, sy, i, nk, K, warp, lane, p, e, off, cnt);
     if (i < 0) break;
   }
 }
@@ -529,11 +579,11 @@ int get_map(CUtensorMap* out, const void* base, uint64_t inner, uint64_t rows,
 }
 
 template <int MODE>
-int make_maps(const DecodeParams& P, int G, GemvMaps* M) {
+int make_maps(const DecodeParams& P, int RT, GemvMaps* M) {
   const BankView& b = MODE == kGateUp ? P.gu : P.dn;
   const uint64_t K = MODE == kGateUp ? P.H : P.I;
   const uint64_t rows_e = MODE == kGateUp ? 2 * (uint64_t)P.I : (uint64_t)P.H;
-  const uint32_t box_rows = MODE == kGateUp ? 64 * G : 128 * G;
+  const uint32_t box_rows = MODE == kGateUp ? RT / 2 : RT;
   int st = get_map(&M->w, b.packed, K / 2, rows_e * P.E, 128, box_rows, true);
   if (!st) st = get_map(&M->s, b.scale, K / 16, rows_e * P.E, 16, box_rows, false);
   if (st) return st;
@@ -547,20 +597,20 @@ int make_maps(const DecodeParams& P, int G, GemvMaps* M) {
   return st;
 }
 
-template <int MODE, int G>
+template <int MODE, int MT, int NW>
 int launch_one(const DecodeParams& P, int64_t est_tiles, cudaStream_t stream) {
-  const Layout L = make_layout(G);
+  const Layout L = make_layout(MT, NW);
   if (L.stages < 2) return FTB_ERR_SHAPE;
   GemvMaps M;
-  int st = make_maps<MODE>(P, G, &M);
+  int st = make_maps<MODE>(P, L.RT, &M);
   if (st) return st;
-  cudaError_t err = cudaFuncSetAttribute(k_gemv_tma<MODE, G>,
+  cudaError_t err = cudaFuncSetAttribute(k_gemv_tma<MODE, MT, NW>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, L.total);
   if (err != cudaSuccess) return cuda_status(err);
   int64_t grid = sm_count();
   if (est_tiles < grid) grid = est_tiles;
   if (grid < 1) grid = 1;
-  k_gemv_tma<MODE, G><<<(unsigned)grid, kThreads, L.total, stream>>>(P, M);
+  k_gemv_tma<MODE, MT, NW><<<(unsigned)grid, (NW + 1) * kWarp, L.total, stream>>>(P, M);
   return cuda_status(cudaGetLastError());
 }
 
@@ -575,17 +625,19 @@ int launch_decode_gemvs_tma(const DecodeParams& P, cudaStream_t stream) {
   const int64_t many = 4 * (int64_t)sm_count();
   int st;
   prof_mark(FTB_KERNEL_GATE_UP, true, stream);
-  if (est_seg * (2 * P.I / 256) >= many)
-    st = launch_one<kGateUp, 2>(P, max_seg * (2 * P.I / 256), stream);
-  else
-    st = launch_one<kGateUp, 1>(P, max_seg * (2 * P.I / 128), stream);
+  if (est_seg * (2 * P.I / 256) >= many) {
+    st = launch_one<kGateUp, 1, 16>(P, max_seg * (2 * P.I / 256), stream);
+  } else {
+    st = launch_one<kGateUp, 1, 8>(P, max_seg * (2 * P.I / 128), stream);
+  }
   prof_mark(FTB_KERNEL_GATE_UP, false, stream);
   if (st) return st;
   prof_mark(FTB_KERNEL_DOWN, true, stream);
-  if (est_seg * (P.H / 256) >= many)
-    st = launch_one<kDown, 2>(P, max_seg * (P.H / 256), stream);
-  else
-    st = launch_one<kDown, 1>(P, max_seg * (P.H / 128), stream);
+  if (est_seg * (P.H / 256) >= many) {
+    st = launch_one<kDown, 1, 16>(P, max_seg * (P.H / 256), stream);
+  } else {
+    st = launch_one<kDown, 1, 8>(P, max_seg * (P.H / 128), stream);
+  }
   prof_mark(FTB_KERNEL_DOWN, false, stream);
   return st;
 }

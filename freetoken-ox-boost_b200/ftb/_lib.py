@@ -10,7 +10,8 @@ import os
 import threading
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libftb.so")
+# FTB_LIBRARY names another build of the same library (same C ABI) to load instead.
+LIB_PATH = os.environ.get("FTB_LIBRARY") or os.path.join(_HERE, "libftb.so")
 
 FTB_OK = 0
 FTB_ERR_SHAPE = 1

@@ -161,10 +161,9 @@ static int decode_impl(const uint16_t* x, const ftb_nvfp4_bank* bank, const ftb_
   const DecodeWs w = carve_decode(workspace, T, H, I, E, top_k, has_shared);
   const int64_t R = T * top_k;
 
-  int st = cuda_status(cudaMemsetAsync(w.status, 0, 4 * sizeof(int32_t), stream));
-  if (st) return st;
-
   SortParams sp{};
+  sp.zero_words = w.status;  // status word and the two GEMV work counters
+  sp.n_zero = 4;
   sp.ids = topk_ids;
   sp.R = R;
   sp.T = T;
@@ -184,7 +183,7 @@ static int decode_impl(const uint16_t* x, const ftb_nvfp4_bank* bank, const ftb_
   sp.x16 = w.x16;
   sp.xscale = w.xscale;
   sp.H = H;
-  st = launch_sort_stage(sp, stream);
+  int st = launch_sort_stage(sp, stream);
   if (st) return st;
 
   DecodeParams dp{};
@@ -323,9 +322,9 @@ int ftb_moe_align(const int32_t* topk_ids, int64_t T, int top_k, int E, int bloc
   if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return FTB_ERR_ALIGN;
   const AlignWs w = carve_align(workspace, T, top_k, E);
   cudaStream_t s = (cudaStream_t)stream;
-  int st = cuda_status(cudaMemsetAsync(w.status, 0, sizeof(int32_t), s));
-  if (st) return st;
   SortParams sp{};
+  sp.zero_words = w.status;
+  sp.n_zero = 1;
   sp.ids = topk_ids;
   sp.R = T * top_k;
   sp.T = T;
@@ -340,7 +339,7 @@ int ftb_moe_align(const int32_t* topk_ids, int64_t T, int top_k, int E, int bloc
   sp.padded_off = w.padded_off;
   sp.padded_cnt = w.padded_cnt;
   sp.status = w.status;
-  st = launch_sort_stage(sp, s);
+  int st = launch_sort_stage(sp, s);
   if (st) return st;
   if (expert_offsets)
     st = cuda_status(cudaMemcpyAsync(expert_offsets, w.offsets, sizeof(int32_t) * (E + 1),

@@ -130,6 +130,8 @@ struct PublishParams {
 };
 
 __global__ void __launch_bounds__(256) k_ep_publish(const PublishParams P) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   for (int64_t i = i0; i < P.nx; i += stride) P.rx[i] = P.x[i];
@@ -151,6 +153,8 @@ struct CombineParams {
 // out[t] = bf16(f32(bf16(sum_k ic3[t,k])) + f32(shared[t])), k in order, fp32; ic3[t,k] read
 // from the rank that owns expert ids[t,k] (the same arithmetic as k_combine).
 __global__ void __launch_bounds__(256) k_ep_combine(const CombineParams C) {
+  pdl_launch_dependents();
+  pdl_wait();
   const EpLinks& L = C.ep;
   __shared__ int sm_ok;
   __shared__ uint32_t sm_epoch;
@@ -374,9 +378,8 @@ int ftb_ep_forward(ftb_ep* g, const uint16_t* x, const float* topk_w, const int3
   int64_t gp = ceil_div(pp.nx, 256);
   if (gp > sm_count()) gp = sm_count();
   prof_mark(FTB_KERNEL_EP_PUBLISH, true, s);
-  k_ep_publish<<<(unsigned)gp, 256, 0, s>>>(pp);
+  st = cuda_status(launch_pdl(k_ep_publish, dim3((unsigned)gp), dim3(256), 0, s, pp));
   prof_mark(FTB_KERNEL_EP_PUBLISH, false, s);
-  st = cuda_status(cudaGetLastError());
   if (st) return st;
 
   SortParams sp{};
@@ -443,9 +446,9 @@ int ftb_ep_forward(ftb_ep* g, const uint16_t* x, const float* topk_w, const int3
   int64_t gc = ceil_div(g->T * (g->H / 8), 256);
   if (gc > (int64_t)sm_count() * 4) gc = (int64_t)sm_count() * 4;
   prof_mark(FTB_KERNEL_EP_COMBINE, true, s);
-  k_ep_combine<<<(unsigned)gc, 256, 0, s>>>(cp);
+  st = cuda_status(launch_pdl(k_ep_combine, dim3((unsigned)gc), dim3(256), 0, s, cp));
   prof_mark(FTB_KERNEL_EP_COMBINE, false, s);
-  return cuda_status(cudaGetLastError());
+  return st;
 }
 
 int ftb_ep_status(ftb_ep* g, int clear, ftb_stream_t stream) {

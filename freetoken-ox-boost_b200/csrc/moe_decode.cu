@@ -11,6 +11,8 @@ namespace {
 
 // out[t] = bf16(f32(bf16(sum_k ic3[t,k])) + f32(shared[t])); k in order, fp32.
 __global__ void __launch_bounds__(256) k_combine(const DecodeParams P) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t nv = (int64_t)P.H / 8;
   const int64_t total = P.T * nv;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
@@ -56,9 +58,9 @@ int launch_combine(const DecodeParams& P, cudaStream_t stream) {
   const int64_t cap = (int64_t)sm_count() * 8;
   if (g3 > cap) g3 = cap;
   prof_mark(FTB_KERNEL_COMBINE, true, stream);
-  k_combine<<<(unsigned)g3, 256, 0, stream>>>(P);
+  const cudaError_t err = launch_pdl(k_combine, dim3((unsigned)g3), dim3(256), 0, stream, P);
   prof_mark(FTB_KERNEL_COMBINE, false, stream);
-  return cuda_status(cudaGetLastError());
+  return cuda_status(err);
 }
 
 int launch_decode_gemvs(const DecodeParams& P, cudaStream_t stream) {

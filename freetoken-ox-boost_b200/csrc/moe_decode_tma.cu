@@ -480,6 +480,7 @@ __global__ void __launch_bounds__((NW + 1) * kWarp, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tile_of + kMaxStages);
   uint8_t* stages = smem + kHeader;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_launch_dependents();
   if (threadIdx.x == 0) {
     for (int s = 0; s < L.stages; ++s) {
       mbar_init(&full[s], 1);
@@ -488,7 +489,12 @@ __global__ void __launch_bounds__((NW + 1) * kWarp, 1)
     *abort_flag = 0;
     fence_mbar_init();
   }
+  if (warp == NW && lane == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&M.w)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&M.s)) : "memory");
+  }
   __syncthreads();
+  pdl_wait();  // the segment table, activations and work counter come from earlier launches
   const Sync sy{full, empty, tile_of, abort_flag, P.status};
   const int K = MODE == kGateUp ? P.H : P.I;
   const int nk = (K + kStageK - 1) / kStageK;
@@ -610,8 +616,8 @@ int launch_one(const DecodeParams& P, int64_t est_tiles, cudaStream_t stream) {
   int64_t grid = sm_count();
   if (est_tiles < grid) grid = est_tiles;
   if (grid < 1) grid = 1;
-  k_gemv_tma<MODE, MT, NW><<<(unsigned)grid, (NW + 1) * kWarp, L.total, stream>>>(P, M);
-  return cuda_status(cudaGetLastError());
+  return cuda_status(launch_pdl(k_gemv_tma<MODE, MT, NW>, dim3((unsigned)grid),
+                                dim3((NW + 1) * kWarp), (size_t)L.total, stream, P, M));
 }
 
 }  // namespace

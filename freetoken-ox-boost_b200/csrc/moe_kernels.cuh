@@ -76,6 +76,8 @@ struct SortParams {
   int32_t* padded_off;  // [E] scratch
   int32_t* padded_cnt;  // [E] scratch
   int32_t* status;
+  int32_t* zero_words;  // [n_zero] cleared by block 0 before any other use (status, counters)
+  int n_zero;
   // activation staging (x16 == null: no staging blocks)
   const uint16_t* x;    // [T, H] bf16
   __half* x16;          // [T, H]

@@ -60,6 +60,7 @@ __device__ void sort_block(const SortParams& P, int* hist /* [32][E] */) {
   __shared__ int sm_scan[33];
   __shared__ int sm_total;
 
+  if (P.zero_words && tid < P.n_zero) P.zero_words[tid] = 0;
   for (int i = tid; i < kSortWarps * E; i += kSortThreads) hist[i] = 0;
   __syncthreads();
 
@@ -291,6 +292,8 @@ __device__ void ep_front(const SortParams& P, int* hist) {
 
 __global__ void __launch_bounds__(kSortThreads) k_sort_stage(SortParams P) {
   extern __shared__ int hist[];
+  pdl_launch_dependents();
+  pdl_wait();
   if (P.ep.world > 0) {
     ep_front(P, hist);
   } else if (blockIdx.x == 0) {
@@ -314,9 +317,10 @@ int launch_sort_stage(const SortParams& P, cudaStream_t stream) {
   }
   const int64_t blocks = 1 + (P.x16 ? P.T : 0);
   prof_mark(FTB_KERNEL_SORT, true, stream);
-  k_sort_stage<<<(unsigned)blocks, kSortThreads, smem, stream>>>(P);
+  const cudaError_t err =
+      launch_pdl(k_sort_stage, dim3((unsigned)blocks), dim3(kSortThreads), smem, stream, P);
   prof_mark(FTB_KERNEL_SORT, false, stream);
-  return cuda_status(cudaGetLastError());
+  return cuda_status(err);
 }
 
 }  // namespace ftb

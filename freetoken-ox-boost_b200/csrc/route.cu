@@ -1,60 +1,88 @@
 // route.cu - router GEMV and top-k (softmax-renormalise and sigmoid-bias modes).
 //
-// One warp per token; lane l holds experts l, l+32, ... in registers (E <= 1024). Top-k is
-// k rounds of a warp argmax on (score, index) with the larger score winning and the lower
-// index winning ties - the selection order of fused_route.py:50-56 and of a sorted
-// torch.topk. Selected lanes are masked by a per-lane bitmask, so NaN/-inf rows still
-// produce top_k distinct ids.
+// One warp per token; lane l holds experts l, l+32, ... in registers (E <= 1024), sorted per
+// lane. Top-k is k rounds of a warp argmax over the lanes' heads on (score, index), the
+// larger score winning and the lower index winning ties - the selection order of
+// fused_route.py:50-56 and of a sorted torch.topk. A selected candidate leaves its lane's
+// list, so NaN/-inf rows still produce top_k distinct ids.
 #include "ftb_common.cuh"
 #include "moe_kernels.cuh"
 
 namespace ftb {
 namespace {
 
-constexpr int kMaxPerLane = 32;  // E <= 1024
-
-struct Best {
-  float v;
-  int i;
+// A candidate: selection key, expert index (-1 = padding, loses to everything), and the
+// value its weight is made from (softmax: exp(logit - max); sigmoid: sigmoid(logit)).
+struct Cand {
+  float key;
+  int idx;
+  float val;
 };
 
-__device__ __forceinline__ Best better(Best a, Best b) {
-  // larger value wins; equal values -> lower index; index -1 = none
-  if (a.i < 0) return b;
-  if (b.i < 0) return a;
-  if (b.v > a.v || (b.v == a.v && b.i < a.i)) return b;
-  return a;
+// a is selected before b: larger key; equal keys -> lower index; padding last.
+__device__ __forceinline__ bool before(const Cand& a, const Cand& b) {
+  if (a.idx < 0) return false;
+  if (b.idx < 0) return true;
+  return a.key > b.key || (a.key == b.key && a.idx < b.idx);
 }
 
+__device__ __forceinline__ void cswap(Cand& a, Cand& b) {
+  if (before(b, a)) {
+    const Cand t = a;
+    a = b;
+    b = t;
+  }
+}
+
+// Sorts PER candidates (a power of two) in selection order: bitonic network in registers.
+template <int PER>
+__device__ __forceinline__ void sort_lane(Cand (&c)[PER]) {
+#pragma unroll
+  for (int k = 2; k <= PER; k <<= 1)
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1)
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const int l = i ^ j;
+        if (l > i) {
+          if ((i & k) == 0)
+            cswap(c[i], c[l]);
+          else
+            cswap(c[l], c[i]);
+        }
+      }
+}
+
+// One warp per token; lane l holds experts l, l+32, ..., sorted in selection order. Each of
+// the top_k rounds takes the warp-wide best of the lanes' heads (shuffle argmax with the
+// same order) and the winning lane pops its head.
+template <int PER>
 __global__ void __launch_bounds__(128) k_route_topk(const float* __restrict__ logits, int64_t T,
                                                     int E, int top_k, int mode,
                                                     const float* __restrict__ bias, float scaling,
                                                     int renorm, float* __restrict__ w_out,
                                                     int32_t* __restrict__ id_out) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (t >= T) return;
   const float* row = logits + t * E;
-  float key[kMaxPerLane];  // selection score
-  float val[kMaxPerLane];  // softmax: logit; sigmoid: sigmoid(logit)
-  const int per = (E + 31) / 32;
+  Cand c[PER];
   float m = -INFINITY;
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i) {
+  for (int i = 0; i < PER; ++i) {
     const int e = lane + 32 * i;
-    key[i] = -INFINITY;
-    val[i] = 0.f;
-    if (i < per && e < E) {
+    c[i] = Cand{-INFINITY, -1, 0.f};
+    if (e < E) {
       const float l = row[e];
       if (mode == FTB_ROUTE_SIGMOID) {
         const float s = 1.0f / (1.0f + expf(-l));
         float k = s + (bias ? bias[e] : 0.f);
         if (k != k) k = -3.4028234663852886e38f;  // NaN -> -FLT_MAX
-        key[i] = k;
-        val[i] = s;
+        c[i] = Cand{k, e, s};
       } else {
-        key[i] = (l != l) ? -INFINITY : l;
-        val[i] = l;
+        c[i] = Cand{(l != l) ? -INFINITY : l, e, l};
         m = fmaxf(m, l);
       }
     }
@@ -65,43 +93,43 @@ __global__ void __launch_bounds__(128) k_route_topk(const float* __restrict__ lo
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     float s = 0.f;
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) {
-      const int e = lane + 32 * i;
-      if (i < per && e < E) {
-        val[i] = expf(val[i] - m);
-        s += val[i];
+    for (int i = 0; i < PER; ++i) {
+      if (c[i].idx >= 0) {
+        c[i].val = expf(c[i].val - m);
+        s += c[i].val;
       }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     denom = s;
   }
-  uint32_t taken = 0;
+  sort_lane<PER>(c);
   float wsum = 0.f;
   float wk = 0.f;  // this lane keeps the weight of selection k == lane
   for (int k = 0; k < top_k; ++k) {
-    Best b{0.f, -1};
-#pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) {
-      const int e = lane + 32 * i;
-      if (i < per && e < E && !((taken >> i) & 1u)) b = better(b, Best{key[i], e});
-    }
+    Cand b = c[0];
+    int src = lane;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
-      Best c;
-      c.v = __shfl_xor_sync(0xffffffffu, b.v, o);
-      c.i = __shfl_xor_sync(0xffffffffu, b.i, o);
-      b = better(b, c);
+      Cand o_c;
+      o_c.key = __shfl_xor_sync(0xffffffffu, b.key, o);
+      o_c.idx = __shfl_xor_sync(0xffffffffu, b.idx, o);
+      o_c.val = __shfl_xor_sync(0xffffffffu, b.val, o);
+      const int o_src = __shfl_xor_sync(0xffffffffu, src, o);
+      if (before(o_c, b)) {
+        b = o_c;
+        src = o_src;
+      }
     }
-    int idx = b.i < 0 ? 0 : (b.i > E - 1 ? E - 1 : b.i);
-    // owner lane publishes the value of the chosen expert
-    const int owner = idx & 31, slot = idx >> 5;
-    float v = 0.f;
+    // every lane agrees on b (a total order); the owner pops its head
+    if (lane == src) {
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i)
-      if (i == slot) v = val[i];
-    v = __shfl_sync(0xffffffffu, v, owner);
-    if (lane == owner) taken |= 1u << slot;
+      for (int i = 0; i + 1 < PER; ++i) c[i] = c[i + 1];
+      c[PER - 1] = Cand{-INFINITY, -1, 0.f};
+    }
+    // no candidate left (top_k > experts cannot reach here: checked on the host)
+    const int idx = b.idx < 0 ? 0 : (b.idx > E - 1 ? E - 1 : b.idx);
+    float v = b.val;
     if (mode == FTB_ROUTE_SOFTMAX) v = v / denom;
     wsum += v;
     if (lane == k) wk = v;
@@ -123,6 +151,8 @@ __global__ void __launch_bounds__(128) k_route_topk(const float* __restrict__ lo
 __global__ void __launch_bounds__(256) k_router_gemv(const uint16_t* __restrict__ x,
                                                      const float* __restrict__ G, int64_t T, int H,
                                                      int E, float* __restrict__ logits) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int e = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int64_t t = blockIdx.y;
@@ -151,19 +181,34 @@ int launch_route_topk(const float* logits, int64_t T, int E, int top_k, int mode
   if (T == 0) return FTB_OK;
   const int wpb = 4;
   const int64_t blocks = ceil_div(T, wpb);
+  const int per = (E + 31) / 32;
   prof_mark(FTB_KERNEL_ROUTE, true, stream);
-  k_route_topk<<<(unsigned)blocks, 32 * wpb, 0, stream>>>(logits, T, E, top_k, mode, bias,
-                                                          scaling, renorm, w, ids);
+  cudaError_t err = cudaSuccess;
+#define FTB_ROUTE_LAUNCH(PER)                                                                \
+  err = launch_pdl(k_route_topk<PER>, dim3((unsigned)blocks), dim3(32 * wpb), 0, stream, logits, \
+                   T, E, top_k, mode, bias, scaling, renorm, w, ids)
+  if (per <= 1)
+    FTB_ROUTE_LAUNCH(1);
+  else if (per <= 2)
+    FTB_ROUTE_LAUNCH(2);
+  else if (per <= 4)
+    FTB_ROUTE_LAUNCH(4);
+  else if (per <= 8)
+    FTB_ROUTE_LAUNCH(8);
+  else if (per <= 16)
+    FTB_ROUTE_LAUNCH(16);
+  else
+    FTB_ROUTE_LAUNCH(32);
+#undef FTB_ROUTE_LAUNCH
   prof_mark(FTB_KERNEL_ROUTE, false, stream);
-  return cuda_status(cudaGetLastError());
+  return cuda_status(err);
 }
 
 int launch_router_gemv(const uint16_t* x, const float* G, int64_t T, int H, int E, float* logits,
                        cudaStream_t stream) {
   if (T == 0) return FTB_OK;
   dim3 grid((unsigned)ceil_div(E, 8), (unsigned)T);
-  k_router_gemv<<<grid, 256, 0, stream>>>(x, G, T, H, E, logits);
-  return cuda_status(cudaGetLastError());
+  return cuda_status(launch_pdl(k_router_gemv, grid, dim3(256), 0, stream, x, G, T, H, E, logits));
 }
 
 }  // namespace ftb

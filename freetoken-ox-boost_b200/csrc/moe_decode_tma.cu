@@ -625,9 +625,13 @@ int launch_one(const DecodeParams& P, int64_t est_tiles, cudaStream_t stream) {
 int launch_decode_gemvs_tma(const DecodeParams& P, cudaStream_t stream) {
   if (P.H % 256 || P.I % 256) return FTB_ERR_SHAPE;
   const int64_t max_seg = max_segments(P.R, P.E, P.Ts, P.has_shared);
-  // expected segments (distinct experts <= min(R, E), plus the shared expert's); 256-row tiles
-  // when they still give every SM several tiles, else 128-row tiles for balance
-  const int64_t est_seg = (P.R < P.E ? P.R : P.E) + (P.has_shared ? (P.Ts + kSegRoutes - 1) / kSegRoutes : 0);
+  // Expected segments: at least one per distinct expert (<= min(R, E)), at least
+  // R / kSegRoutes when experts hold more routes than a segment (expert-parallel ranks), plus
+  // the shared expert's. 256-row tiles (16 consumer warps) when that still gives every SM
+  // several tiles, else 128-row tiles (8 warps) for balance.
+  const int64_t routed_seg = (P.R < P.E ? P.R : P.E) > P.R / kSegRoutes ? (P.R < P.E ? P.R : P.E)
+                                                                          : P.R / kSegRoutes;
+  const int64_t est_seg = routed_seg + (P.has_shared ? (P.Ts + kSegRoutes - 1) / kSegRoutes : 0);
   const int64_t many = 4 * (int64_t)sm_count();
   int st;
   prof_mark(FTB_KERNEL_GATE_UP, true, stream);

@@ -30,10 +30,13 @@ struct DecodeWs {
   __half* h16;
   uint16_t* ic3;
   uint16_t* ic3s;
+  __half* xs;  // prefill only
   size_t bytes;
 };
 
-DecodeWs carve_decode(void* ws, int64_t T, int H, int I, int64_t E, int top_k, int has_shared) {
+// Workspace of one decode (cap = kSegRoutes) or prefill (cap = kPrefillSegRoutes) call.
+DecodeWs carve_decode(void* ws, int64_t T, int H, int I, int64_t E, int top_k, int has_shared,
+                      int cap = kSegRoutes) {
   const int64_t R = T * top_k;
   const int64_t Rs = R + (has_shared ? T : 0);
   Carver c(ws);
@@ -43,7 +46,7 @@ DecodeWs carve_decode(void* ws, int64_t T, int H, int I, int64_t E, int top_k, i
   w.xscale = c.take<float>(T);
   w.offsets = c.take<int32_t>(E + 1);
   w.sorted = c.take<int32_t>(Rs);
-  const int64_t S = max_segments(R, E, T, has_shared);
+  const int64_t S = max_segments(R, E, T, has_shared, cap);
   w.seg_expert = c.take<int32_t>(S);
   w.seg_off = c.take<int32_t>(S);
   w.seg_cnt = c.take<int32_t>(S);
@@ -51,6 +54,7 @@ DecodeWs carve_decode(void* ws, int64_t T, int H, int I, int64_t E, int top_k, i
   w.h16 = c.take<__half>(Rs * I);
   w.ic3 = c.take<uint16_t>(R * H);
   w.ic3s = c.take<uint16_t>(has_shared ? T * H : 1);
+  w.xs = cap == kPrefillSegRoutes ? c.take<__half>(Rs * H) : nullptr;
   w.bytes = c.off;
   return w;
 }
@@ -140,12 +144,13 @@ int sm_count() {
   return cache[dev];
 }
 
-static int decode_impl(const uint16_t* x, const ftb_nvfp4_bank* bank, const ftb_nvfp4_bank* shared,
-                       const float* topk_w, const int32_t* topk_ids, int64_t T, int H, int I,
-                       int top_k, float act_limit, uint16_t* out, void* workspace,
-                       size_t workspace_bytes, uint16_t* dbg_ic1, uint16_t* dbg_h,
-                       uint16_t* dbg_ic3, uint16_t* dbg_sic1, uint16_t* dbg_sh,
-                       uint16_t* dbg_sout, cudaStream_t stream) {
+// The layer, decode GEMVs (prefill == false) or tensor-core grouped GEMMs (prefill == true).
+static int layer_impl(bool prefill, const uint16_t* x, const ftb_nvfp4_bank* bank,
+                      const ftb_nvfp4_bank* shared, const float* topk_w, const int32_t* topk_ids,
+                      int64_t T, int H, int I, int top_k, float act_limit, uint16_t* out,
+                      void* workspace, size_t workspace_bytes, uint16_t* dbg_ic1, uint16_t* dbg_h,
+                      uint16_t* dbg_ic3, uint16_t* dbg_sic1, uint16_t* dbg_sh,
+                      uint16_t* dbg_sout, cudaStream_t stream) {
   if (T < 0 || H <= 0 || I <= 0 || top_k < 1) return FTB_ERR_SHAPE;
   if (H % 256 || I % 256) return FTB_ERR_SHAPE;
   if (!bank_ok(bank) || (shared && !bank_ok(shared))) return FTB_ERR_ARG;
@@ -155,10 +160,11 @@ static int decode_impl(const uint16_t* x, const ftb_nvfp4_bank* bank, const ftb_
   if (!x || !topk_w || !topk_ids || !out) return FTB_ERR_ARG;
   if (!aligned16(x) || !aligned16(out)) return FTB_ERR_ALIGN;
   const int has_shared = shared ? 1 : 0;
-  const DecodeWs need = carve_decode(nullptr, T, H, I, E, top_k, has_shared);
+  const int cap = prefill ? kPrefillSegRoutes : kSegRoutes;
+  const DecodeWs need = carve_decode(nullptr, T, H, I, E, top_k, has_shared, cap);
   if (!workspace || workspace_bytes < need.bytes) return FTB_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return FTB_ERR_ALIGN;
-  const DecodeWs w = carve_decode(workspace, T, H, I, E, top_k, has_shared);
+  const DecodeWs w = carve_decode(workspace, T, H, I, E, top_k, has_shared, cap);
   const int64_t R = T * top_k;
 
   SortParams sp{};
@@ -171,6 +177,8 @@ static int decode_impl(const uint16_t* x, const ftb_nvfp4_bank* bank, const ftb_
   sp.E = (int)E;
   sp.top_k = top_k;
   sp.has_shared = has_shared;
+  sp.seg_cap = cap;
+  sp.x_plain = prefill ? 1 : 0;
   sp.block_m = 0;
   sp.offsets = w.offsets;
   sp.sorted = w.sorted;
@@ -206,6 +214,7 @@ static int decode_impl(const uint16_t* x, const ftb_nvfp4_bank* bank, const ftb_
   dp.n_seg = w.n_seg;
   dp.x16 = w.x16;
   dp.xscale = w.xscale;
+  dp.xs = w.xs;
   dp.h16 = w.h16;
   dp.ic3 = w.ic3;
   dp.ic3s = w.ic3s;
@@ -217,7 +226,12 @@ static int decode_impl(const uint16_t* x, const ftb_nvfp4_bank* bank, const ftb_
   dp.dbg_sic1 = dbg_sic1;
   dp.dbg_sh = dbg_sh;
   dp.has_shared = has_shared;
-  st = launch_decode_gemvs(dp, stream);
+  if (prefill) {
+    st = launch_prefill_gemms(dp, stream);
+    if (!st) st = launch_combine(dp, stream);
+  } else {
+    st = launch_decode_gemvs(dp, stream);
+  }
   if (st) return st;
   if (dbg_ic3) {
     st = cuda_status(cudaMemcpyAsync(dbg_ic3, w.ic3, (size_t)R * H * 2, cudaMemcpyDeviceToDevice,
@@ -330,6 +344,7 @@ int ftb_moe_align(const int32_t* topk_ids, int64_t T, int top_k, int E, int bloc
   sp.T = T;
   sp.E = E;
   sp.top_k = top_k;
+  sp.seg_cap = kSegRoutes;
   sp.block_m = block_m;
   sp.offsets = w.offsets;
   sp.sorted = w.sorted;
@@ -372,11 +387,37 @@ size_t ftb_moe_decode_workspace_bytes(int64_t T, int H, int I, int E, int top_k,
   return carve_decode(nullptr, T, H, I, E, top_k, has_shared).bytes;
 }
 
+size_t ftb_moe_prefill_workspace_bytes(int64_t T, int H, int I, int E, int top_k,
+                                       int has_shared) {
+  return carve_decode(nullptr, T, H, I, E, top_k, has_shared, kPrefillSegRoutes).bytes;
+}
+
+int ftb_moe_prefill(const uint16_t* x, const ftb_nvfp4_bank* bank, const ftb_nvfp4_bank* shared,
+                    const float* topk_w, const int32_t* topk_ids, int64_t T, int H, int I,
+                    int top_k, float act_limit, uint16_t* out, void* workspace,
+                    size_t workspace_bytes, ftb_stream_t stream) {
+  return layer_impl(true, x, bank, shared, topk_w, topk_ids, T, H, I, top_k, act_limit, out,
+                    workspace, workspace_bytes, nullptr, nullptr, nullptr, nullptr, nullptr,
+                    nullptr, (cudaStream_t)stream);
+}
+
+int ftb_moe_prefill_debug(const uint16_t* x, const ftb_nvfp4_bank* bank,
+                          const ftb_nvfp4_bank* shared, const float* topk_w,
+                          const int32_t* topk_ids, int64_t T, int H, int I, int top_k,
+                          float act_limit, uint16_t* out, void* workspace,
+                          size_t workspace_bytes, uint16_t* ic1, uint16_t* h, uint16_t* ic3,
+                          uint16_t* shared_ic1, uint16_t* shared_h, uint16_t* shared_out,
+                          ftb_stream_t stream) {
+  return layer_impl(true, x, bank, shared, topk_w, topk_ids, T, H, I, top_k, act_limit, out,
+                    workspace, workspace_bytes, ic1, h, ic3, shared_ic1, shared_h, shared_out,
+                    (cudaStream_t)stream);
+}
+
 int ftb_moe_decode(const uint16_t* x, const ftb_nvfp4_bank* bank, const ftb_nvfp4_bank* shared,
                    const float* topk_w, const int32_t* topk_ids, int64_t T, int H, int I,
                    int top_k, float act_limit, uint16_t* out, void* workspace,
                    size_t workspace_bytes, ftb_stream_t stream) {
-  return decode_impl(x, bank, shared, topk_w, topk_ids, T, H, I, top_k, act_limit, out, workspace,
+  return layer_impl(false, x, bank, shared, topk_w, topk_ids, T, H, I, top_k, act_limit, out, workspace,
                      workspace_bytes, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
                      (cudaStream_t)stream);
 }
@@ -387,7 +428,7 @@ int ftb_moe_decode_debug(const uint16_t* x, const ftb_nvfp4_bank* bank,
                          float act_limit, uint16_t* out, void* workspace, size_t workspace_bytes,
                          uint16_t* ic1, uint16_t* h, uint16_t* ic3, uint16_t* shared_ic1,
                          uint16_t* shared_h, uint16_t* shared_out, ftb_stream_t stream) {
-  return decode_impl(x, bank, shared, topk_w, topk_ids, T, H, I, top_k, act_limit, out, workspace,
+  return layer_impl(false, x, bank, shared, topk_w, topk_ids, T, H, I, top_k, act_limit, out, workspace,
                      workspace_bytes, ic1, h, ic3, shared_ic1, shared_h, shared_out,
                      (cudaStream_t)stream);
 }

@@ -392,6 +392,7 @@ int ftb_ep_forward(ftb_ep* g, const uint16_t* x, const float* topk_w, const int3
   sp.E = g->per;
   sp.top_k = g->K;
   sp.has_shared = g->has_shared;
+  sp.seg_cap = kSegRoutes;
   sp.block_m = 0;
   sp.offsets = w.offsets;
   sp.sorted = w.sorted;

@@ -540,28 +540,33 @@ PFN_cuTensorMapEncodeTiled encode_fn() {
 struct MapKey {
   const void* base;
   uint64_t inner, rows;
-  uint32_t box_inner, box_rows, swizzle;
+  uint32_t box_inner, box_rows, swizzle, dtype;
   bool operator==(const MapKey& o) const {
     return base == o.base && inner == o.inner && rows == o.rows && box_inner == o.box_inner &&
-           box_rows == o.box_rows && swizzle == o.swizzle;
+           box_rows == o.box_rows && swizzle == o.swizzle && dtype == o.dtype;
   }
 };
 struct MapKeyHash {
   size_t operator()(const MapKey& k) const {
     size_t h = std::hash<const void*>()(k.base);
     h ^= std::hash<uint64_t>()(k.inner * 1315423911ull + k.rows) + 0x9e3779b97f4a7c15ull + (h << 6);
-    h ^= std::hash<uint64_t>()(((uint64_t)k.box_inner << 32) | (k.box_rows << 2) | k.swizzle) +
+    h ^= std::hash<uint64_t>()(((uint64_t)k.box_inner << 32) | (k.box_rows << 8) |
+                               (k.swizzle << 4) | k.dtype) +
          (h >> 2);
     return h;
   }
 };
 
-// A 2D u8 tensor [rows][inner] (row pitch = inner bytes), boxes of box_rows x box_inner.
-int get_map(CUtensorMap* out, const void* base, uint64_t inner, uint64_t rows,
-            uint32_t box_inner, uint32_t box_rows, bool swizzle128) {
+}  // namespace
+
+// A 2D tensor [rows][inner] of `esize`-byte elements (row pitch = inner elements), copied in
+// boxes of box_rows x box_inner; cached by address, shape and box.
+int get_map_2d(CUtensorMap* out, const void* base, CUtensorMapDataType dtype, int esize,
+               uint64_t inner, uint64_t rows, uint32_t box_inner, uint32_t box_rows,
+               bool swizzle128) {
   static std::mutex mu;
   static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
-  const MapKey key{base, inner, rows, box_inner, box_rows, swizzle128 ? 1u : 0u};
+  const MapKey key{base, inner, rows, box_inner, box_rows, swizzle128 ? 1u : 0u, (uint32_t)dtype};
   std::lock_guard<std::mutex> lock(mu);
   auto it = cache.find(key);
   if (it != cache.end()) {
@@ -571,17 +576,25 @@ int get_map(CUtensorMap* out, const void* base, uint64_t inner, uint64_t rows,
   PFN_cuTensorMapEncodeTiled fn = encode_fn();
   if (!fn) return FTB_ERR_CUDA;
   const cuuint64_t dims[2] = {inner, rows};
-  const cuuint64_t strides[1] = {inner};
+  const cuuint64_t strides[1] = {inner * (uint64_t)esize};
   const cuuint32_t box[2] = {box_inner, box_rows};
   const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = fn(out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims,
-                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  const CUresult r = fn(out, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
                         swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return FTB_ERR_CUDA;
   if (cache.size() > 4096) cache.clear();
   cache.emplace(key, *out);
   return FTB_OK;
+}
+
+namespace {
+
+int get_map(CUtensorMap* out, const void* base, uint64_t inner, uint64_t rows,
+            uint32_t box_inner, uint32_t box_rows, bool swizzle128) {
+  return get_map_2d(out, base, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, inner, rows, box_inner,
+                    box_rows, swizzle128);
 }
 
 template <int MODE>

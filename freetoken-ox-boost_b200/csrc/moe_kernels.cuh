@@ -13,6 +13,9 @@ constexpr int kStatusTimeout = 4;       // a bounded device-side wait gave up
 // Work segments hold at most this many routes of one expert (one pass of two mma n-tiles);
 // an expert with more routes is split into several segments.
 constexpr int kSegRoutes = 16;
+// Prefill (tensor-core) segments hold up to this many routes: the MMA's N (two accumulators
+// of this many fp32 columns and two A tiles share the 512 tensor-memory columns).
+constexpr int kPrefillSegRoutes = 192;
 
 // Activation rows (x16, h16) are stored "round-interleaved": in each 128-k round, the 16-byte
 // chunk holding k = 32*tig + 8q .. +8 sits at chunk position 4q + tig, the order in which a
@@ -23,8 +26,9 @@ __host__ __device__ __forceinline__ int64_t ri_chunk(int64_t c) {
 
 // Capacity of the segment table for R routed routes, E experts and T shared-expert routes.
 // (T here is the shared expert's token count.)
-__host__ __device__ inline int64_t max_segments(int64_t R, int64_t E, int64_t T, int has_shared) {
-  return (R < E ? R : E) + R / kSegRoutes + 1 + (has_shared ? T / kSegRoutes + 1 : 0);
+__host__ __device__ inline int64_t max_segments(int64_t R, int64_t E, int64_t T, int has_shared,
+                                                int64_t cap = kSegRoutes) {
+  return (R < E ? R : E) + R / cap + 1 + (has_shared ? T / cap + 1 : 0);
 }
 
 // Expert-parallel group, device side: every rank's exchange region is mapped into every
@@ -60,6 +64,8 @@ struct SortParams {
   int E;
   int top_k;
   int has_shared;
+  int seg_cap;         // routes per segment at most (kSegRoutes for the decode GEMVs)
+  int x_plain;         // stage x16 in natural k order (prefill) instead of round-interleaved
   int block_m;         // > 0: also emit the padded (moe_align) outputs
   // outputs (decode segment table); seg_expert may be null
   int32_t* offsets;    // [E+1] unpadded, required
@@ -115,6 +121,7 @@ struct DecodeParams {
   // staged activations
   const __half* x16;
   const float* xscale;
+  __half* xs;              // prefill: x16 rows in sorted (route) order [(R+Ts), H]
   // intermediates
   __half* h16;             // [(R+T), I] sorted order
   uint16_t* ic3;           // [R, H] route order
@@ -168,6 +175,8 @@ inline BankView view_dn(const ftb_nvfp4_bank* b, const ftb_nvfp4_bank* s) {
 int launch_decode_gemvs(const DecodeParams& P, cudaStream_t stream);
 // TMA-fed pipelined GEMVs (moe_decode_tma.cu).
 int launch_decode_gemvs_tma(const DecodeParams& P, cudaStream_t stream);
+// Tensor-core grouped GEMMs for prefill (moe_prefill.cu): segments of <= kPrefillSegRoutes.
+int launch_prefill_gemms(const DecodeParams& P, cudaStream_t stream);
 int launch_combine(const DecodeParams& P, cudaStream_t stream);
 
 // Measurement hook (ftb_profile_begin/end): records an event on `stream` before (start=true)

@@ -1,0 +1,677 @@
+// moe_prefill.cu - prefill (large T) NVFP4 grouped GEMMs on the 5th-generation tensor cores.
+//
+// The reference's prefill driver (fused_experts_nvfp4 -> _prefill_nvfp4_moe_kernel,
+// patches/kernel_triton_nvfp4_fused_moe.patch:73-106, patches/moe_fused_nvfp4.patch:153-179)
+// builds each weight tile as e2m1 x scale in bf16 (exact) and runs a dense dot per sorted
+// token block. Here one work item is a 128-row weight tile of one expert against one segment
+// of up to 192 of its routes (the MMA's N), full K:
+//   D[128 x N] (fp32, tensor memory) += A[128 x 64] (dequantised weights, f16, tensor memory)
+//                                      x B[N x 64]^T (the routes' f16 activation rows, smem)
+// with tcgen05.mma kind::f16 (M=128, K=16 per instruction, issued by one thread). B is a
+// K-major tile in the canonical 128-byte-swizzled layout (8-row atoms of 128-byte rows, the
+// 16-byte chunk c of row r stored at chunk c ^ (r & 7)). A lives in tensor memory (lane = row,
+// two f16 per 32-bit column): written there with tcgen05.st it costs no shared-memory
+// bandwidth, which the MMA's B reads and the TMA writes already use up (a first version with
+// A in shared memory measured 3-4x slower, every role stalled on shared memory). e2m1 x e4m3
+// products are exact in f16, so A is the reference's weight tile exactly.
+//
+// One persistent CTA per SM, warp roles (items assigned round-robin: CTA b takes items
+// b, b + grid, ...; every role walks the same sequence):
+//   warp 0     TMA producer of the packed weights and scales, 256 k per stage (2D boxes,
+//              the decode GEMV's tensor maps), no multicast;
+//   warp 14    TMA producer of the routes' activation rows, per 64-k block: 2D boxes of
+//              64 rows x 64 k over the rows in sorted order (gate_up: k_permute_rows copies
+//              each route's x row to its sorted position first; down: h is written in sorted
+//              order), no multicast; tile::gather4 straight from the token rows measured 7x
+//              fewer rows per microsecond than these boxes;
+//   warp 1     allocates the 512 tensor-memory columns (two D buffers of up to 192 columns
+//              and four 32-column A tiles) and, on one lane, issues the MMAs and the
+//              tcgen05.commit arrivals;
+//   warps 2-9  dequantise: warp group h (0/1) writes k 32h .. 32h+31 of each 64-k A tile;
+//              a thread owns the A row of its tensor-memory lane, reads 16 packed bytes and 2
+//              scales and stores 32 f16 values (cvt.rn.f16x2.e2m1x2, exact f16x2 scale
+//              multiply) with tcgen05.st;
+//   warps 10-13 epilogue: tcgen05.ld of D (each warp reads its 32-lane quarter), then the
+//              decode path's arithmetic: gate_up -> bf16 ic1, SwiGLU -> f16 h (sorted order);
+//              down -> bf16(acc x global x routed weight) per route.
+// gate_up's A rows pair gate and up rows 16 lanes apart (A row 32q + l = gate row 16q + l,
+// A row 32q + 16 + l = up row 16q + l of the tile, l < 16), so SwiGLU pairs tensor-memory
+// lanes l and l ^ 16 of a warp with one shuffle.
+//
+// Rings, each an mbarrier pair: packed stages (producer -> dequant), A tiles (dequant ->
+// MMA, released by tcgen05.commit), B tiles (producer -> MMA, released by commit), D buffers
+// (MMA -> epilogue). Every wait is bounded; a timeout raises the CTA abort flag and
+// kStatusTimeout, every role stops, the MMA lane waits for its MMAs to finish, the producer
+// for its copies, and the tensor memory is released before the CTA exits.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "moe_kernels.cuh"
+
+namespace ftb {
+
+// tensor maps of the decode GEMV (moe_decode_tma.cu): packed weights / scales, and a 2D f16
+// map for the activation rows
+int get_map_2d(CUtensorMap* out, const void* base, CUtensorMapDataType dtype, int esize,
+               uint64_t inner, uint64_t rows, uint32_t box_inner, uint32_t box_rows,
+               bool swizzle128);
+
+namespace {
+
+constexpr int kPfRows = 128;                 // MMA M
+constexpr int kBlkK = 64;                    // k per operand tile
+constexpr int kStgK = 256;                   // k per packed stage
+constexpr int kPStages = 4, kAStages = 4, kBStages = 4;
+constexpr int kPfWarps = 15;
+constexpr int kPfThreads = kPfWarps * kWarp;
+// warp roles: weights producer, MMA, 8 dequant warps, 4 epilogue warps, activations producer
+constexpr int kWarpTma = 0, kWarpMma = 1, kWarpDq = 2, kDqWarps = 8, kWarpEpi = 10, kWarpTmaB = 14;
+constexpr int kPBytes = kPfRows * 128 + kPfRows * 16;  // 18432
+constexpr int kBoxRows = 64;                 // rows per activation TMA box
+constexpr int kBBytes = (kPrefillSegRoutes + kBoxRows - 1) / kBoxRows * kBoxRows * kBlkK * 2;
+// tensor memory (512 columns x 128 lanes of 32 bit): two D buffers of up to
+// kPrefillSegRoutes fp32 columns, then kAStages A tiles of 64 k (32 columns of f16 pairs);
+// four A tiles keep the dequantisation far enough ahead of the MMAs (two measured
+// latency-bound)
+constexpr int kTmemCols = 512;
+constexpr int kTmemA = 2 * kPrefillSegRoutes;
+constexpr int kACols = kBlkK / 2;
+static_assert(kTmemA + kAStages * kACols <= kTmemCols, "tensor memory budget");
+constexpr int kPfHeader = 12288;
+constexpr int kPOff = kPfHeader;
+constexpr int kBOff = kPOff + kPStages * kPBytes;
+constexpr int kPfSmem = kBOff + kBStages * kBBytes;
+static_assert(kPBytes % 1024 == 0 && kBOff % 1024 == 0 && kBBytes % 1024 == 0, "1024-B atoms");
+static_assert(kPfSmem <= 227 * 1024, "shared memory");
+
+enum { kGateUp = 0, kDown = 1 };
+
+struct PfMaps {
+  CUtensorMap w, s, sw, ss;  // packed weights / scales: routed bank, shared expert
+  CUtensorMap act;           // activation rows in sorted order (xs or h16), f16, 64 x 16 boxes
+};
+
+// header layout
+struct PfShared {
+  uint64_t full_p[kPStages], empty_p[kPStages];
+  uint64_t full_a[kAStages], empty_a[kAStages];
+  uint64_t full_b[kBStages], empty_b[kBStages];
+  uint64_t full_d[2], empty_d[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+  // epilogue warp w (0..3): route id and factor of each column of its current item
+  int col_r[4][kPrefillSegRoutes];
+  float col_f[4][kPrefillSegRoutes];
+};
+static_assert(sizeof(PfShared) <= kPfHeader, "header");
+
+struct PfSync {
+  PfShared* sh;
+  int32_t* status;
+  __device__ bool wait(uint64_t* bar, uint32_t parity) const {
+    volatile int* ab = &sh->abort;
+    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+      if (*ab) return false;
+      if (mbar_try_wait(bar, parity)) return true;
+      if (i > 16) __nanosleep(64);
+    }
+    *ab = 1;
+    atomicOr(status, kStatusTimeout);
+    return false;
+  }
+};
+
+__device__ __forceinline__ int swz(int line, int c) { return line * 128 + ((c ^ (line & 7)) << 4); }
+
+__device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                       uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms 1024 B apart.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor, kind::f16: D fp32, A and B f16, both K-major, M = 128, N.
+__device__ __forceinline__ uint32_t f16_idesc(int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kPfRows >> 4) << 24);
+}
+
+// D += A (tensor memory, lanes = rows, f16 pairs per column) x B (shared memory).
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// SwiGLU for the prefill epilogue, which evaluates it for every (row, route): the hardware
+// exp2-based exponential and a correctly rounded reciprocal instead of expf and a division.
+// The result is rounded to bf16 right after, like the decode path's.
+__device__ __forceinline__ float swiglu_fast(float g, float u, float limit) {
+  if (limit > 0.f) {
+    g = fminf(g, limit);
+    u = fminf(fmaxf(u, -limit), limit);
+  }
+  const float sg = __frcp_rn(1.0f + __expf(-g));
+  return (g * sg) * u;
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+struct Item {
+  int e, off, cnt, mt, n;  // expert (E = shared), segment start/size, weight tile, MMA N
+  bool sh;
+};
+
+template <int MODE>
+__device__ __forceinline__ Item item_of(const DecodeParams& P, int64_t it, int mtiles) {
+  Item r;
+  const int a = (int)(it / mtiles);
+  r.mt = (int)(it % mtiles);
+  r.e = P.seg_expert[a];
+  r.off = P.seg_off[a];
+  r.cnt = P.seg_cnt[a];
+  r.sh = (r.e == P.E);
+  r.n = (r.cnt + 15) / 16 * 16;
+  return r;
+}
+
+// ---- roles -------------------------------------------------------------------------------
+
+template <int MODE>
+__device__ void pf_producer_w(const DecodeParams& P, const PfMaps& M, uint8_t* smem,
+                              const PfSync& sy, int64_t n_items, int mtiles, int nk) {
+  PfShared* sh = sy.sh;
+  const int lane = threadIdx.x & 31;
+  const int rows_e = MODE == kGateUp ? 2 * P.I : P.H;
+  int64_t pi = 0;
+  bool aborted = false;
+  for (int64_t it = blockIdx.x; it < n_items && !aborted; it += gridDim.x) {
+    const Item im = item_of<MODE>(P, it, mtiles);
+    const CUtensorMap* wm = im.sh ? &M.sw : &M.w;
+    const CUtensorMap* sm = im.sh ? &M.ss : &M.s;
+    const int ebase = im.sh ? 0 : im.e * rows_e;
+    for (int kc = 0; kc < nk; ++kc) {  // packed weights + scales of 128 rows x 256 k
+      const int s = (int)(pi % kPStages);
+      int go = 1;
+      if (lane == 0) {
+        if (pi >= kPStages && !sy.wait(&sh->empty_p[s], (uint32_t)((pi / kPStages) - 1) & 1u))
+          go = 0;
+        if (go) {
+          uint8_t* st = smem + kPOff + s * kPBytes;
+          const uint32_t bar = smem_u32(&sh->full_p[s]);
+          mbar_arrive_expect_tx(&sh->full_p[s], (uint32_t)kPBytes);
+          if (MODE == kGateUp) {
+            const int y0 = ebase + 64 * im.mt, y1 = ebase + P.I + 64 * im.mt;
+            tma_2d(smem_u32(st), wm, kc * 128, y0, bar);
+            tma_2d(smem_u32(st + 64 * 128), wm, kc * 128, y1, bar);
+            tma_2d(smem_u32(st + kPfRows * 128), sm, kc * 16, y0, bar);
+            tma_2d(smem_u32(st + kPfRows * 128 + 64 * 16), sm, kc * 16, y1, bar);
+          } else {
+            const int y = ebase + kPfRows * im.mt;
+            tma_2d(smem_u32(st), wm, kc * 128, y, bar);
+            tma_2d(smem_u32(st + kPfRows * 128), sm, kc * 16, y, bar);
+          }
+        }
+      }
+      go = __shfl_sync(0xffffffffu, go, 0);
+      if (!go) {
+        aborted = true;
+        break;
+      }
+      ++pi;
+    }
+  }
+  // copies in flight must land before the CTA exits (only after an abort can any be pending)
+  if (lane != 0 || !sh->abort) return;
+  for (int64_t j = pi - kPStages > 0 ? pi - kPStages : 0; j < pi; ++j)
+    for (uint32_t k = 0; k < kSpinLimit; ++k) {
+      if (mbar_try_wait(&sh->full_p[j % kPStages], (uint32_t)(j / kPStages) & 1u)) break;
+      __nanosleep(64);
+    }
+}
+
+template <int MODE>
+__device__ void pf_producer_b(const DecodeParams& P, const PfMaps& M, uint8_t* smem,
+                              const PfSync& sy, int64_t n_items, int mtiles, int nk) {
+  PfShared* sh = sy.sh;
+  const int lane = threadIdx.x & 31;
+  int64_t bi = 0;
+  bool aborted = false;
+  for (int64_t it = blockIdx.x; it < n_items && !aborted; it += gridDim.x) {
+    const Item im = item_of<MODE>(P, it, mtiles);
+    const int nblk = nk * (kStgK / kBlkK);
+    for (int blk = 0; blk < nblk; ++blk) {  // rows off .. off+n of the sorted rows, 64 k
+      const int s = (int)(bi % kBStages);
+      int go = 1;
+      if (lane == 0) {
+        if (bi >= kBStages && !sy.wait(&sh->empty_b[s], (uint32_t)((bi / kBStages) - 1) & 1u))
+          go = 0;
+        if (go) {
+          // 64-row boxes: rows past n (the next segment's, or zero fill) are never read
+          const int nbox = (im.n + kBoxRows - 1) / kBoxRows;
+          mbar_arrive_expect_tx(&sh->full_b[s], (uint32_t)(nbox * kBoxRows * 128));
+          uint8_t* bt = smem + kBOff + s * kBBytes;
+          for (int g = 0; g < nbox; ++g)
+            tma_2d(smem_u32(bt + g * kBoxRows * 128), &M.act, blk * kBlkK, im.off + kBoxRows * g,
+                   smem_u32(&sh->full_b[s]));
+        }
+      }
+      go = __shfl_sync(0xffffffffu, go, 0);
+      if (!go) {
+        aborted = true;
+        break;
+      }
+      ++bi;
+    }
+  }
+  if (lane != 0 || !sh->abort) return;
+  for (int64_t j = bi - kBStages > 0 ? bi - kBStages : 0; j < bi; ++j)
+    for (uint32_t k = 0; k < kSpinLimit; ++k) {
+      if (mbar_try_wait(&sh->full_b[j % kBStages], (uint32_t)(j / kBStages) & 1u)) break;
+      __nanosleep(64);
+    }
+}
+
+template <int MODE>
+__device__ void pf_dequant(uint8_t* smem, const PfSync& sy, int64_t n_items, int nk) {
+  PfShared* sh = sy.sh;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int half = (warp - kWarpDq) >> 2;  // k 32*half .. 32*half+31 of each A tile
+  const int t = 32 * (warp & 3) + lane;    // A row = the tensor-memory lane this warp may write
+  // packed-stage line of A row t. gate_up: lane l < 16 of a warp holds gate row 16q + l and
+  // lane l + 16 the matching up row (lines 0..63 gate, 64..127 up), so that an 8-lane phase
+  // reads 8 distinct swizzle lines (no bank conflicts) and SwiGLU pairs lanes l, l ^ 16.
+  const int line = MODE == kGateUp ? 16 * (warp & 3) + (lane & 15) + 64 * (lane >> 4) : t;
+  const uint32_t a_base = sh->tmem_base + ((uint32_t)(32 * (warp & 3)) << 16) +
+                          (uint32_t)(kTmemA + 16 * half);
+  int64_t pi = 0, ai = 0;
+  for (int64_t it = blockIdx.x; it < n_items; it += gridDim.x) {
+    for (int kc = 0; kc < nk; ++kc) {
+      const int s = (int)(pi % kPStages);
+      if (!sy.wait(&sh->full_p[s], (uint32_t)(pi / kPStages) & 1u)) return;
+      const uint8_t* st = smem + kPOff + s * kPBytes;
+      for (int j = 0; j < kStgK / kBlkK; ++j) {
+        const int sa = (int)(ai % kAStages);
+        if (ai >= kAStages && !sy.wait(&sh->empty_a[sa], (uint32_t)((ai / kAStages) - 1) & 1u))
+          return;
+        tc_fence_after();
+        // 16 packed bytes = k 64j + 32half .. +32 of the stage; scales of its two 16-k blocks
+        const uint4 w = *reinterpret_cast<const uint4*>(st + swz(line, 2 * j + half));
+        const uint16_t sc =
+            *reinterpret_cast<const uint16_t*>(st + kPfRows * 128 + line * 16 + 4 * j + 2 * half);
+        const uint32_t s01 = e4m3x2_to_f16x2(sc);
+        const uint32_t sb[2] = {f16x2_bcast_lo(s01), f16x2_bcast_hi(s01)};
+        const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+        uint32_t o[16];  // 32 f16 in k order: column c holds k (2c, 2c+1) of this half
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t h[4];
+          e2m1x8_to_f16x2x4(words[c], h);
+          const uint32_t s16 = sb[c >> 1];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) o[4 * c + q] = hmul2(h[q], s16);
+        }
+        tmem_st16(a_base + (uint32_t)(sa * kACols), o);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh->full_a[sa]);
+        ++ai;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh->empty_p[s]);
+      ++pi;
+    }
+  }
+}
+
+template <int MODE>
+__device__ void pf_mma(const DecodeParams& P, uint8_t* smem, const PfSync& sy, int64_t n_items,
+                       int mtiles, int nk) {
+  PfShared* sh = sy.sh;
+  const uint32_t tbase = sh->tmem_base;
+  int64_t ai = 0, bi = 0, di = 0;
+  bool issued = false;
+  for (int64_t it = blockIdx.x; it < n_items; it += gridDim.x) {
+    const Item im = item_of<MODE>(P, it, mtiles);
+    const int buf = (int)(di & 1);
+    if (di >= 2 && !sy.wait(&sh->empty_d[buf], (uint32_t)((di / 2) - 1) & 1u)) break;
+    tc_fence_after();
+    const uint32_t d = tbase + (uint32_t)(buf * kPrefillSegRoutes);
+    const uint32_t idesc = f16_idesc(im.n);
+    const int nblk = nk * (kStgK / kBlkK);
+    bool ok = true;
+    for (int b = 0; b < nblk; ++b) {
+      const int sa = (int)(ai % kAStages), sb = (int)(bi % kBStages);
+      if (!sy.wait(&sh->full_a[sa], (uint32_t)(ai / kAStages) & 1u) ||
+          !sy.wait(&sh->full_b[sb], (uint32_t)(bi / kBStages) & 1u)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t a0 = tbase + (uint32_t)(kTmemA + sa * kACols);
+      const uint32_t b0 = smem_u32(smem + kBOff + sb * kBBytes);
+#pragma unroll
+      for (int kk = 0; kk < kBlkK / 16; ++kk)
+        mma_f16_ts(d, a0 + (uint32_t)(kk * 8), sw128_desc(b0 + kk * 32), idesc,
+                   (b > 0 || kk > 0) ? 1u : 0u);
+      issued = true;
+      mma_commit(&sh->empty_a[sa]);
+      mma_commit(&sh->empty_b[sb]);
+      ++ai;
+      ++bi;
+    }
+    if (!ok) break;
+    mma_commit(&sh->full_d[buf]);
+    ++di;
+  }
+  // every MMA this thread issued has finished once the drain barrier completes
+  if (issued) {
+    mma_commit(&sh->drain);
+    for (uint32_t k = 0; k < kSpinLimit; ++k) {
+      if (mbar_try_wait(&sh->drain, 0)) break;
+      __nanosleep(64);
+    }
+  }
+}
+
+template <int MODE>
+__device__ void pf_epilogue(const DecodeParams& P, const PfSync& sy, int64_t n_items, int mtiles) {
+  PfShared* sh = sy.sh;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int quarter = warp & 3;       // tensor-memory lanes this warp may read
+  const int m = 32 * quarter + lane;  // D row (A row) of this thread
+  const int ew = warp - kWarpEpi;     // this warp's metadata slice
+  int* col_r = sh->col_r[ew];
+  float* col_f = sh->col_f[ew];
+  const uint32_t tbase = sh->tmem_base + ((uint32_t)(32 * quarter) << 16);
+  int64_t di = 0;
+  for (int64_t it = blockIdx.x; it < n_items; it += gridDim.x) {
+    const Item im = item_of<MODE>(P, it, mtiles);
+    // the item's columns: route id (-1 past cnt) and factor (gate_up: the token's 2^s;
+    // down: the routed weight, 1 for the shared expert); loaded before the D wait so the
+    // latency overlaps the MMAs
+    for (int n = lane; n < im.n; n += kWarp) {
+      int r = -1;
+      float f = 1.f;
+      if (n < im.cnt) {
+        r = P.sorted[im.off + n];
+        if (MODE == kGateUp)
+          f = P.xscale[im.sh ? (int64_t)r - P.R : (int64_t)r / P.top_k];
+        else if (!im.sh)
+          f = P.topk_w[r];
+      }
+      col_r[n] = r;
+      col_f[n] = f;
+    }
+    __syncwarp();
+    const int buf = (int)(di & 1);
+    if (!sy.wait(&sh->full_d[buf], (uint32_t)(di / 2) & 1u)) return;
+    tc_fence_after();
+    const uint32_t taddr = tbase + (uint32_t)(buf * kPrefillSegRoutes);
+    if (MODE == kGateUp) {
+      const int I = P.I;
+      const int j = 64 * im.mt + 16 * quarter + (lane & 15);  // gate/up row pair of lanes l, l^16
+      const uint16_t* glob = im.sh ? P.gu.s_global : P.gu.global + (int64_t)im.e * 2 * I;
+      const float glg = __half2float(__ushort_as_half(glob[j]));
+      const float glu = __half2float(__ushort_as_half(glob[I + j]));
+      // lane l (< 16) holds gate row j, lane l + 16 up row j, for all columns. Per column
+      // pair (2p, 2p+1) lane l computes column 2p and lane l + 16 column 2p + 1, each
+      // receiving the partner's value with one shuffle, so all 32 lanes do useful work.
+      const bool upper = (lane & 16) != 0;
+      const bool dbg = P.dbg_ic1 || P.dbg_h || P.dbg_sic1 || P.dbg_sh;
+      for (int c0 = 0; c0 < im.n; c0 += 16) {
+        float v[16];
+        tmem_ld16(taddr + (uint32_t)c0, v);
+#pragma unroll
+        for (int p2 = 0; p2 < 8; ++p2) {
+          const float send = upper ? v[2 * p2] : v[2 * p2 + 1];
+          const float recv = __shfl_xor_sync(0xffffffffu, send, 16);
+          const float own = upper ? v[2 * p2 + 1] : v[2 * p2];
+          const float g = upper ? recv : own, u = upper ? own : recv;
+          const int n = c0 + 2 * p2 + (upper ? 1 : 0);
+          const int r = col_r[n];
+          if (r < 0) continue;
+          const float xs = col_f[n];
+          const float gv = bf16_round((g * xs) * glg);
+          const float uv = bf16_round((u * xs) * glu);
+          const float hv = bf16_round(swiglu_fast(gv, uv, P.limit));
+          if (fabsf(hv) > 65504.f) atomicOr(P.status, kStatusF16Overflow);
+          P.h16[(int64_t)(im.off + n) * I + j] = __float2half_rn(hv);
+          if (dbg) {
+            if (im.sh) {
+              const int64_t tok = (int64_t)r - P.R;
+              if (P.dbg_sic1) {
+                P.dbg_sic1[tok * 2 * I + j] = f32_to_bf16_bits(gv);
+                P.dbg_sic1[tok * 2 * I + I + j] = f32_to_bf16_bits(uv);
+              }
+              if (P.dbg_sh) P.dbg_sh[tok * I + j] = f32_to_bf16_bits(hv);
+            } else {
+              if (P.dbg_ic1) {
+                P.dbg_ic1[(int64_t)r * 2 * I + j] = f32_to_bf16_bits(gv);
+                P.dbg_ic1[(int64_t)r * 2 * I + I + j] = f32_to_bf16_bits(uv);
+              }
+              if (P.dbg_h) P.dbg_h[(int64_t)r * I + j] = f32_to_bf16_bits(hv);
+            }
+          }
+        }
+      }
+    } else {
+      const int H = P.H;
+      const int row = kPfRows * im.mt + m;
+      const uint16_t* glob = im.sh ? P.dn.s_global : P.dn.global + (int64_t)im.e * H;
+      const float gl = __half2float(__ushort_as_half(glob[row]));
+      for (int c0 = 0; c0 < im.n; c0 += 16) {
+        float v[16];
+        tmem_ld16(taddr + (uint32_t)c0, v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int n = c0 + i;
+          const int r = col_r[n];
+          if (r < 0) continue;
+          if (im.sh)
+            P.ic3s[((int64_t)r - P.R) * H + row] = f32_to_bf16_bits(v[i] * gl);
+          else
+            P.ic3[(int64_t)r * H + row] = f32_to_bf16_bits((v[i] * gl) * col_f[n]);
+        }
+      }
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sh->empty_d[buf]);
+    ++di;
+  }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kPfThreads, 1)
+    k_prefill_gemm(const __grid_constant__ DecodeParams P, const __grid_constant__ PfMaps M) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  PfShared* sh = reinterpret_cast<PfShared*>(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_launch_dependents();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPStages; ++s)
+      mbar_init(&sh->full_p[s], 1), mbar_init(&sh->empty_p[s], kDqWarps);
+    for (int s = 0; s < kAStages; ++s)
+      mbar_init(&sh->full_a[s], kDqWarps), mbar_init(&sh->empty_a[s], 1);
+    for (int s = 0; s < kBStages; ++s) mbar_init(&sh->full_b[s], 1), mbar_init(&sh->empty_b[s], 1);
+    for (int s = 0; s < 2; ++s) mbar_init(&sh->full_d[s], 1), mbar_init(&sh->empty_d[s], 4);
+    mbar_init(&sh->drain, 1);
+    sh->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == kWarpMma) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&sh->tmem_base)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (warp == kWarpTma && lane == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&M.w)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&M.s)) : "memory");
+  }
+  if (warp == kWarpTmaB && lane == 0)
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&M.act)) : "memory");
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  pdl_wait();  // segment table, activations and counters come from earlier launches
+  const PfSync sy{sh, P.status};
+  const int K = MODE == kGateUp ? P.H : P.I;
+  const int nk = K / kStgK;
+  const int mtiles = MODE == kGateUp ? P.I / 64 : P.H / kPfRows;
+  const int64_t n_items = (int64_t)(*P.n_seg) * mtiles;
+  if (warp == kWarpTma) {
+    pf_producer_w<MODE>(P, M, smem, sy, n_items, mtiles, nk);
+  } else if (warp == kWarpTmaB) {
+    pf_producer_b<MODE>(P, M, smem, sy, n_items, mtiles, nk);
+  } else if (warp == kWarpMma) {
+    if (lane == 0) pf_mma<MODE>(P, smem, sy, n_items, mtiles, nk);
+    __syncwarp();
+  } else if (warp < kWarpEpi) {
+    pf_dequant<MODE>(smem, sy, n_items, nk);
+  } else {
+    pf_epilogue<MODE>(P, sy, n_items, mtiles);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kWarpMma) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(sh->tmem_base),
+                 "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+// xs[pos] = x16[token of the route at sorted position pos] (routed rows, then the shared
+// expert's rows), so that the gate_up GEMM reads its B tiles as 2D boxes.
+__global__ void __launch_bounds__(256) k_permute_rows(const DecodeParams P, __half* xs) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t nrows = P.R + (P.has_shared ? P.Ts : 0);
+  const int64_t nv = P.H / 8;
+  const uint4* src = reinterpret_cast<const uint4*>(P.x16);
+  uint4* dst = reinterpret_cast<uint4*>(xs);
+  for (int64_t row = blockIdx.x; row < nrows; row += gridDim.x) {
+    const int r = P.sorted[row];
+    const int64_t tok = r >= P.R ? (int64_t)r - P.R : (int64_t)r / P.top_k;
+    for (int64_t v = threadIdx.x; v < nv; v += blockDim.x) dst[row * nv + v] = src[tok * nv + v];
+  }
+}
+
+template <int MODE>
+int make_pf_maps(const DecodeParams& P, PfMaps* M) {
+  const BankView& b = MODE == kGateUp ? P.gu : P.dn;
+  const uint64_t K = MODE == kGateUp ? P.H : P.I;
+  const uint64_t rows_e = MODE == kGateUp ? 2 * (uint64_t)P.I : (uint64_t)P.H;
+  const uint32_t box_rows = MODE == kGateUp ? 64 : kPfRows;
+  const CUtensorMapDataType u8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  int st = get_map_2d(&M->w, b.packed, u8, 1, K / 2, rows_e * P.E, 128, box_rows, true);
+  if (!st) st = get_map_2d(&M->s, b.scale, u8, 1, K / 16, rows_e * P.E, 16, box_rows, false);
+  if (st) return st;
+  if (P.has_shared) {
+    st = get_map_2d(&M->sw, b.s_packed, u8, 1, K / 2, rows_e, 128, box_rows, true);
+    if (!st) st = get_map_2d(&M->ss, b.s_scale, u8, 1, K / 16, rows_e, 16, box_rows, false);
+    if (st) return st;
+  } else {
+    M->sw = M->w;
+    M->ss = M->s;
+  }
+  // activation rows in sorted order: xs [R + Ts, H] (gate_up) or h16 [R + Ts, I] (down), f16,
+  // boxes of 64 rows x 64 k
+  const void* act = MODE == kGateUp ? (const void*)P.xs : (const void*)P.h16;
+  const uint64_t act_rows = (uint64_t)(P.R + (P.has_shared ? P.Ts : 0));
+  return get_map_2d(&M->act, act, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, K, act_rows, kBlkK,
+                    kBoxRows, true);
+}
+
+template <int MODE>
+int launch_pf(const DecodeParams& P, int64_t max_items, cudaStream_t stream) {
+  PfMaps M;
+  int st = make_pf_maps<MODE>(P, &M);
+  if (st) return st;
+  cudaError_t err = cudaFuncSetAttribute(k_prefill_gemm<MODE>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem);
+  if (err != cudaSuccess) return cuda_status(err);
+  int64_t grid = sm_count();
+  if (max_items < grid) grid = max_items;
+  if (grid < 1) grid = 1;
+  return cuda_status(launch_pdl(k_prefill_gemm<MODE>, dim3((unsigned)grid), dim3(kPfThreads),
+                                (size_t)kPfSmem, stream, P, M));
+}
+
+}  // namespace
+
+int launch_prefill_gemms(const DecodeParams& P, cudaStream_t stream) {
+  if (P.H % 256 || P.I % 256 || !P.xs) return FTB_ERR_SHAPE;
+  const int64_t max_seg = max_segments(P.R, P.E, P.Ts, P.has_shared, kPrefillSegRoutes);
+  const int64_t nrows = P.R + (P.has_shared ? P.Ts : 0);
+  int64_t gp = nrows < 4 * (int64_t)sm_count() ? nrows : 4 * (int64_t)sm_count();
+  if (gp < 1) gp = 1;
+  prof_mark(FTB_KERNEL_PERMUTE, true, stream);
+  int st = cuda_status(launch_pdl(k_permute_rows, dim3((unsigned)gp), dim3(256), 0, stream, P,
+                                  P.xs));
+  prof_mark(FTB_KERNEL_PERMUTE, false, stream);
+  if (st) return st;
+  prof_mark(FTB_KERNEL_GATE_UP, true, stream);
+  st = launch_pf<kGateUp>(P, max_seg * (P.I / 64), stream);
+  prof_mark(FTB_KERNEL_GATE_UP, false, stream);
+  if (st) return st;
+  prof_mark(FTB_KERNEL_DOWN, true, stream);
+  st = launch_pf<kDown>(P, max_seg * (P.H / kPfRows), stream);
+  prof_mark(FTB_KERNEL_DOWN, false, stream);
+  return st;
+}
+
+}  // namespace ftb

@@ -100,8 +100,9 @@ __device__ void sort_block(const SortParams& P, int* hist /* [32][E] */) {
     run_off += tot;
     const int poff = run_pad + block_exclusive_scan(P.block_m > 0 ? pad : 0, sm_scan, &tot);
     run_pad += tot;
-    // an expert's routes become ceil(cnt / kSegRoutes) segments of <= kSegRoutes routes
-    const int nsub = (int)ceil_div(cnt, kSegRoutes);
+    // an expert's routes become ceil(cnt / seg_cap) segments of <= seg_cap routes
+    const int cap = P.seg_cap;
+    const int nsub = (int)ceil_div(cnt, cap);
     const int aidx = run_act + block_exclusive_scan(nsub, sm_scan, &tot);
     run_act += tot;
     if (e < E) {
@@ -109,8 +110,8 @@ __device__ void sort_block(const SortParams& P, int* hist /* [32][E] */) {
       if (P.seg_expert) {
         for (int k = 0; k < nsub; ++k) {
           P.seg_expert[aidx + k] = e;
-          P.seg_off[aidx + k] = off + k * kSegRoutes;
-          P.seg_cnt[aidx + k] = min(kSegRoutes, cnt - k * kSegRoutes);
+          P.seg_off[aidx + k] = off + k * cap;
+          P.seg_cnt[aidx + k] = min(cap, cnt - k * cap);
         }
       }
       // turn hist[w][e] into the base position of warp w's first route of expert e
@@ -135,10 +136,10 @@ __device__ void sort_block(const SortParams& P, int* hist /* [32][E] */) {
     if (P.seg_expert) {
       int n = run_act;
       if (P.has_shared && P.Ts > 0) {
-        for (int64_t t0 = 0; t0 < P.Ts; t0 += kSegRoutes, ++n) {
+        for (int64_t t0 = 0; t0 < P.Ts; t0 += P.seg_cap, ++n) {
           P.seg_expert[n] = E;  // marker: the shared expert
           P.seg_off[n] = (int)(R + t0);
-          P.seg_cnt[n] = (int)min((int64_t)kSegRoutes, P.Ts - t0);
+          P.seg_cnt[n] = (int)min((int64_t)P.seg_cap, P.Ts - t0);
         }
       }
       *P.n_seg = n;
@@ -232,7 +233,7 @@ __device__ void stage_token(const SortParams& P, int64_t t, const uint16_t* src)
                                           __uint_as_float(w[j] & 0xffff0000u) * down);
       o[j] = *reinterpret_cast<const uint32_t*>(&h);
     }
-    yr[ri_chunk(i)] = make_uint4(o[0], o[1], o[2], o[3]);
+    yr[P.x_plain ? i : ri_chunk(i)] = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 

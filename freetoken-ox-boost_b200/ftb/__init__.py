@@ -6,11 +6,11 @@ C ABI in ``include/ftb.h``), loaded through ctypes. There is no CPU or Triton fa
 from .banks import Nvfp4Bank, bank_bytes_per_expert
 from .experts import B200Nvfp4Experts, Nvfp4MoELayer, select_nvfp4_backend
 from .fused_nvfp4 import (fused_experts_decode_nvfp4_marlin, fused_experts_nvfp4,
-                          moe_align_block_size, moe_decode)
+                          moe_align_block_size, moe_decode, moe_prefill)
 from .fused_route import fused_route, fused_topk, router_logits
 
 __all__ = [
     "Nvfp4Bank", "bank_bytes_per_expert", "B200Nvfp4Experts", "Nvfp4MoELayer",
     "select_nvfp4_backend", "fused_experts_decode_nvfp4_marlin", "fused_experts_nvfp4",
-    "moe_align_block_size", "moe_decode", "fused_route", "fused_topk", "router_logits",
+    "moe_align_block_size", "moe_decode", "moe_prefill", "fused_route", "fused_topk", "router_logits",
 ]

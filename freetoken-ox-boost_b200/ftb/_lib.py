@@ -64,6 +64,11 @@ SIGNATURES = {
     "ftb_moe_decode_debug": (_i32, [_vp, _BP, _BP, _vp, _vp, _i64, _i32, _i32, _i32, _f32, _vp,
                                     _vp, _sz, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "ftb_moe_combine": (_i32, [_vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp]),
+    "ftb_moe_prefill_workspace_bytes": (_sz, [_i64, _i32, _i32, _i32, _i32, _i32]),
+    "ftb_moe_prefill": (_i32, [_vp, _BP, _BP, _vp, _vp, _i64, _i32, _i32, _i32, _f32, _vp, _vp,
+                               _sz, _vp]),
+    "ftb_moe_prefill_debug": (_i32, [_vp, _BP, _BP, _vp, _vp, _i64, _i32, _i32, _i32, _f32, _vp,
+                                     _vp, _sz, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "ftb_moe_decode_noalloc": (_i32, [_vp, _BP, _BP, _vp, _vp, _i64, _i32, _i32, _i32, _f32,
                                       _vp, _vp]),
     "ftb_ep_region_bytes": (_sz, [_i32, _i64, _i32, _i32]),
@@ -80,7 +85,7 @@ SIGNATURES = {
 }
 
 KERNEL_NAMES = {0: "sort_stage", 1: "gate_up_gemv", 2: "down_gemv", 3: "combine", 4: "route_topk",
-                5: "ep_publish", 6: "ep_combine"}
+                5: "ep_publish", 6: "ep_combine", 7: "permute_rows"}
 
 
 class FtbLibraryError(RuntimeError):

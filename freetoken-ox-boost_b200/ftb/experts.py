@@ -16,7 +16,7 @@ from __future__ import annotations
 import torch
 
 from .banks import FP8, Nvfp4Bank
-from .fused_nvfp4 import _ACTS, moe_decode
+from .fused_nvfp4 import _ACTS, PREFILL_MIN_TOKENS, moe_decode, moe_prefill
 from .fused_route import fused_route, fused_topk, router_logits
 
 DECODE_MAX_TOKENS = 64  # routed_forward treats larger batches as prefill when not told
@@ -83,8 +83,13 @@ class B200Nvfp4Experts:
         if overlap_fn is not None:
             overlap_fn()
         shared = self.shared if include_shared else None
-        return moe_decode(hidden_states, self.bank, topk_weights, topk_ids,
-                          activation=self.activation, act_limit=self._limit(), shared=shared)
+        # the resident reference routes prefill and decode to different drivers
+        # (experts_resident.py:69-83); is_prefill=None picks by the token count
+        if is_prefill is None:
+            is_prefill = hidden_states.shape[0] >= PREFILL_MIN_TOKENS
+        layer = moe_prefill if is_prefill else moe_decode
+        return layer(hidden_states, self.bank, topk_weights, topk_ids,
+                     activation=self.activation, act_limit=self._limit(), shared=shared)
 
 
 class Nvfp4MoELayer:

@@ -56,8 +56,17 @@ def _check_inputs(x, bank: Nvfp4Bank, topk_weights, topk_ids, shared):
     return dev
 
 
+# Token counts from which fused_experts_nvfp4 runs the tensor-core grouped GEMMs.
+PREFILL_MIN_TOKENS = 256
+
+
 def decode_workspace_bytes(T: int, bank: Nvfp4Bank, top_k: int, has_shared: bool) -> int:
     return int(_lib.load().ftb_moe_decode_workspace_bytes(
+        T, bank.hidden, bank.inter, bank.num_experts, top_k, 1 if has_shared else 0))
+
+
+def prefill_workspace_bytes(T: int, bank: Nvfp4Bank, top_k: int, has_shared: bool) -> int:
+    return int(_lib.load().ftb_moe_prefill_workspace_bytes(
         T, bank.hidden, bank.inter, bank.num_experts, top_k, 1 if has_shared else 0))
 
 
@@ -66,6 +75,22 @@ def moe_decode(x: torch.Tensor, bank: Nvfp4Bank, topk_weights: torch.Tensor,
                shared: Nvfp4Bank | None = None, out: torch.Tensor | None = None,
                debug: bool = False, check_status: bool = False):
     """Decode layer on a bank object. ``debug=True`` returns (out, intermediates dict)."""
+    return _layer(False, x, bank, topk_weights, topk_ids, activation, act_limit, shared, out,
+                  debug, check_status)
+
+
+def moe_prefill(x: torch.Tensor, bank: Nvfp4Bank, topk_weights: torch.Tensor,
+                topk_ids: torch.Tensor, *, activation: str = "silu", act_limit: float = 7.0,
+                shared: Nvfp4Bank | None = None, out: torch.Tensor | None = None,
+                debug: bool = False, check_status: bool = False):
+    """The same layer on the tensor-core grouped GEMMs (large T). Same contract and result
+    as ``moe_decode``; ``debug=True`` returns (out, intermediates dict)."""
+    return _layer(True, x, bank, topk_weights, topk_ids, activation, act_limit, shared, out,
+                  debug, check_status)
+
+
+def _layer(prefill: bool, x, bank, topk_weights, topk_ids, activation, act_limit, shared, out,
+           debug, check_status):
     dev = _check_inputs(x, bank, topk_weights, topk_ids, shared)
     limit = _act_limit(activation, act_limit)
     T, H = x.shape
@@ -73,17 +98,23 @@ def moe_decode(x: torch.Tensor, bank: Nvfp4Bank, topk_weights: torch.Tensor,
     I = bank.inter
     if out is None:
         out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
-    nbytes = decode_workspace_bytes(T, bank, K, shared is not None)
+    lib = _lib.load()
+    if prefill:
+        nbytes = prefill_workspace_bytes(T, bank, K, shared is not None)
+        run, run_dbg = lib.ftb_moe_prefill, lib.ftb_moe_prefill_debug
+        name = "ftb_moe_prefill"
+    else:
+        nbytes = decode_workspace_bytes(T, bank, K, shared is not None)
+        run, run_dbg = lib.ftb_moe_decode, lib.ftb_moe_decode_debug
+        name = "ftb_moe_decode"
     ws = workspace(nbytes, dev)
     b = bank.struct()
     s = shared.struct() if shared is not None else None
-    lib = _lib.load()
     sp = ctypes.byref(s) if s is not None else None
     if not debug:
-        st = lib.ftb_moe_decode(ptr(x), ctypes.byref(b), sp, ptr(topk_weights), ptr(topk_ids),
-                                T, H, I, K, limit, ptr(out), ptr(ws), ws.numel(),
-                                stream_handle(dev))
-        _lib.check("ftb_moe_decode", st)
+        st = run(ptr(x), ctypes.byref(b), sp, ptr(topk_weights), ptr(topk_ids), T, H, I, K,
+                 limit, ptr(out), ptr(ws), ws.numel(), stream_handle(dev))
+        _lib.check(name, st)
         inter = None
     else:
         bf = torch.bfloat16
@@ -95,12 +126,11 @@ def moe_decode(x: torch.Tensor, bank: Nvfp4Bank, topk_weights: torch.Tensor,
                          shared_h=torch.zeros(T, I, dtype=bf, device=dev),
                          shared_out=torch.zeros(T, H, dtype=bf, device=dev))
         g = inter.get
-        st = lib.ftb_moe_decode_debug(ptr(x), ctypes.byref(b), sp, ptr(topk_weights),
-                                      ptr(topk_ids), T, H, I, K, limit, ptr(out), ptr(ws),
-                                      ws.numel(), ptr(g("ic1")), ptr(g("h")), ptr(g("ic3")),
-                                      ptr(g("shared_ic1")), ptr(g("shared_h")),
-                                      ptr(g("shared_out")), stream_handle(dev))
-        _lib.check("ftb_moe_decode_debug", st)
+        st = run_dbg(ptr(x), ctypes.byref(b), sp, ptr(topk_weights), ptr(topk_ids), T, H, I, K,
+                     limit, ptr(out), ptr(ws), ws.numel(), ptr(g("ic1")), ptr(g("h")),
+                     ptr(g("ic3")), ptr(g("shared_ic1")), ptr(g("shared_h")),
+                     ptr(g("shared_out")), stream_handle(dev))
+        _lib.check(name + "_debug", st)
     if check_status or debug:
         status = read_status(ws)
         if inter is not None:
@@ -157,7 +187,9 @@ def fused_experts_nvfp4(
     *,
     shared: Nvfp4Bank | None = None,
 ) -> torch.Tensor:
-    """Prefill driver. Same contract and result as the decode driver."""
+    """Prefill driver. Same contract and result as the decode driver; from
+    PREFILL_MIN_TOKENS tokens it runs the tensor-core grouped GEMMs, below that the decode
+    GEMVs (which are faster for few routes per expert)."""
     bank = Nvfp4Bank(gate_up_packed, gate_up_scale, gate_up_global, down_packed, down_scale,
                      down_global)
     if num_experts != bank.num_experts:
@@ -165,8 +197,9 @@ def fused_experts_nvfp4(
     if apply_router_weight_on_input:
         raise NotImplementedError("apply_router_weight_on_input=True is not built")
     del act_alpha
-    return moe_decode(hidden_states, bank, topk_weights, topk_ids, activation=activation,
-                      act_limit=act_limit, shared=shared)
+    layer = moe_prefill if hidden_states.shape[0] >= PREFILL_MIN_TOKENS else moe_decode
+    return layer(hidden_states, bank, topk_weights, topk_ids, activation=activation,
+                 act_limit=act_limit, shared=shared)
 
 
 def moe_sum_reduce(ic3: torch.Tensor, topk_ids: torch.Tensor, num_experts: int,

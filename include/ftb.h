@@ -137,6 +137,31 @@ FTB_API int ftb_moe_decode_debug(const uint16_t* x, const ftb_nvfp4_bank* bank,
                          uint16_t* shared_h, uint16_t* shared_out, ftb_stream_t stream);
 
 /*
+ * Prefill (large T) fused MoE on the tensor cores: the same contract and result as
+ * ftb_moe_decode(), replacing the prefill driver fused_experts_nvfp4(...)
+ * (overlay/freetoken/models/glm5_next/experts_resident.py:69-75; kernel
+ * patches/kernel_triton_nvfp4_fused_moe.patch:73-106). Weight tiles are dequantised exactly
+ * to f16 and multiplied by tcgen05.mma (kind::f16, fp32 accumulation in tensor memory) against
+ * segments of up to 256 routes of one expert. Same shape rules and status word as decode;
+ * ftb_moe_prefill_workspace_bytes() bytes of workspace.
+ */
+FTB_API size_t ftb_moe_prefill_workspace_bytes(int64_t T, int H, int I, int E, int top_k,
+                                               int has_shared);
+FTB_API int ftb_moe_prefill(const uint16_t* x, const ftb_nvfp4_bank* bank,
+                            const ftb_nvfp4_bank* shared, const float* topk_w,
+                            const int32_t* topk_ids, int64_t T, int H, int I, int top_k,
+                            float act_limit, uint16_t* out, void* workspace,
+                            size_t workspace_bytes, ftb_stream_t stream);
+/* The prefill layer with its intermediates exposed (as ftb_moe_decode_debug). */
+FTB_API int ftb_moe_prefill_debug(const uint16_t* x, const ftb_nvfp4_bank* bank,
+                                  const ftb_nvfp4_bank* shared, const float* topk_w,
+                                  const int32_t* topk_ids, int64_t T, int H, int I, int top_k,
+                                  float act_limit, uint16_t* out, void* workspace,
+                                  size_t workspace_bytes, uint16_t* ic1, uint16_t* h,
+                                  uint16_t* ic3, uint16_t* shared_ic1, uint16_t* shared_h,
+                                  uint16_t* shared_out, ftb_stream_t stream);
+
+/*
  * Fixed-order combine, replacing moe_sum_reduce_triton(ic3, out)
  * (patches/moe_fused_nvfp4.patch:147-148) plus the model block's shared add
  * (patches/models_glm_moe_dsa_moe.patch:203-206): out[t] = bf16(sum over k of ic3[t,k]
@@ -212,7 +237,8 @@ enum {
   FTB_KERNEL_COMBINE = 3,
   FTB_KERNEL_ROUTE = 4,
   FTB_KERNEL_EP_PUBLISH = 5,
-  FTB_KERNEL_EP_COMBINE = 6
+  FTB_KERNEL_EP_COMBINE = 6,
+  FTB_KERNEL_PERMUTE = 7
 };
 FTB_API int ftb_profile_begin(void);
 FTB_API int ftb_profile_end(int32_t* kernel_ids, float* ms, int max_n);

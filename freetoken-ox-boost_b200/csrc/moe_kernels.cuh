@@ -14,8 +14,8 @@ constexpr int kStatusTimeout = 4;       // a bounded device-side wait gave up
 // an expert with more routes is split into several segments.
 constexpr int kSegRoutes = 16;
 // Prefill (tensor-core) segments hold up to this many routes: the MMA's N (two accumulators
-// of this many fp32 columns and two A tiles share the 512 tensor-memory columns).
-constexpr int kPrefillSegRoutes = 192;
+// of this many fp32 columns and three 128-k A tiles share the 512 tensor-memory columns).
+constexpr int kPrefillSegRoutes = 160;
 
 // Activation rows (x16, h16) are stored "round-interleaved": in each 128-k round, the 16-byte
 // chunk holding k = 32*tig + 8q .. +8 sits at chunk position 4q + tig, the order in which a

@@ -27,10 +27,10 @@
 //   warp 1     allocates the 512 tensor-memory columns (two D buffers of up to 192 columns
 //              and four 32-column A tiles) and, on one lane, issues the MMAs and the
 //              tcgen05.commit arrivals;
-//   warps 2-9  dequantise: warp group h (0/1) writes k 32h .. 32h+31 of each 64-k A tile;
-//              a thread owns the A row of its tensor-memory lane, reads 16 packed bytes and 2
-//              scales and stores 32 f16 values (cvt.rn.f16x2.e2m1x2, exact f16x2 scale
-//              multiply) with tcgen05.st;
+//   warps 2-9  dequantise: the two warp groups take alternate 64-k A tiles (so one group's
+//              tensor-memory stores overlap the other's conversions); a thread owns the A row
+//              of its tensor-memory lane, reads 32 packed bytes and 4 scales and stores 64 f16
+//              values (cvt.rn.f16x2.e2m1x2, exact f16x2 scale multiply) with tcgen05.st;
 //   warps 10-13 epilogue: tcgen05.ld of D (each warp reads its 32-lane quarter), then the
 //              decode path's arithmetic: gate_up -> bf16 ic1, SwiGLU -> f16 h (sorted order);
 //              down -> bf16(acc x global x routed weight) per route.
@@ -62,29 +62,30 @@ int get_map_2d(CUtensorMap* out, const void* base, CUtensorMapDataType dtype, in
 namespace {
 
 constexpr int kPfRows = 128;                 // MMA M
-constexpr int kBlkK = 64;                    // k per operand tile
+constexpr int kBlkK = 64;                    // k per 128-byte-swizzled operand sub-tile
+constexpr int kAbK = 128;                    // k per A/B stage: 8 MMAs per hand-off
 constexpr int kStgK = 256;                   // k per packed stage
-constexpr int kPStages = 4, kAStages = 4, kBStages = 4;
+constexpr int kPStages = 4, kAbStages = 3;
 constexpr int kPfWarps = 15;
 constexpr int kPfThreads = kPfWarps * kWarp;
 // warp roles: weights producer, MMA, 8 dequant warps, 4 epilogue warps, activations producer
 constexpr int kWarpTma = 0, kWarpMma = 1, kWarpDq = 2, kDqWarps = 8, kWarpEpi = 10, kWarpTmaB = 14;
 constexpr int kPBytes = kPfRows * 128 + kPfRows * 16;  // 18432
-constexpr int kBoxRows = 64;                 // rows per activation TMA box
-constexpr int kBBytes = (kPrefillSegRoutes + kBoxRows - 1) / kBoxRows * kBoxRows * kBlkK * 2;
+constexpr int kBoxRows = 32;                 // rows per activation TMA box
+static_assert(kPrefillSegRoutes % kBoxRows == 0, "segment cap in whole boxes");
+constexpr int kBSub = kPrefillSegRoutes * 128;  // one 64-k sub-tile of up to cap rows
+constexpr int kBBytes = (kAbK / kBlkK) * kBSub;
 // tensor memory (512 columns x 128 lanes of 32 bit): two D buffers of up to
-// kPrefillSegRoutes fp32 columns, then kAStages A tiles of 64 k (32 columns of f16 pairs);
-// four A tiles keep the dequantisation far enough ahead of the MMAs (two measured
-// latency-bound)
+// kPrefillSegRoutes fp32 columns, then kAbStages A tiles of 128 k (64 columns of f16 pairs)
 constexpr int kTmemCols = 512;
 constexpr int kTmemA = 2 * kPrefillSegRoutes;
-constexpr int kACols = kBlkK / 2;
-static_assert(kTmemA + kAStages * kACols <= kTmemCols, "tensor memory budget");
+constexpr int kACols = kAbK / 2;
+static_assert(kTmemA + kAbStages * kACols <= kTmemCols, "tensor memory budget");
 constexpr int kPfHeader = 12288;
 constexpr int kPOff = kPfHeader;
 constexpr int kBOff = kPOff + kPStages * kPBytes;
-constexpr int kPfSmem = kBOff + kBStages * kBBytes;
-static_assert(kPBytes % 1024 == 0 && kBOff % 1024 == 0 && kBBytes % 1024 == 0, "1024-B atoms");
+constexpr int kPfSmem = kBOff + kAbStages * kBBytes;
+static_assert(kPBytes % 1024 == 0 && kBOff % 1024 == 0 && kBSub % 1024 == 0, "1024-B atoms");
 static_assert(kPfSmem <= 227 * 1024, "shared memory");
 
 enum { kGateUp = 0, kDown = 1 };
@@ -97,8 +98,7 @@ struct PfMaps {
 // header layout
 struct PfShared {
   uint64_t full_p[kPStages], empty_p[kPStages];
-  uint64_t full_a[kAStages], empty_a[kAStages];
-  uint64_t full_b[kBStages], empty_b[kBStages];
+  uint64_t full_ab[kAbStages], empty_ab[kAbStages];
   uint64_t full_d[2], empty_d[2];
   uint64_t drain;
   uint32_t tmem_base;
@@ -109,15 +109,21 @@ struct PfShared {
 };
 static_assert(sizeof(PfShared) <= kPfHeader, "header");
 
+// Polls before a wait starts to back off: try_wait suspends in hardware, so spinning on it
+// costs no issue slots, and a sleeping MMA warp would leave the tensor pipe idle.
+constexpr uint32_t kFastPolls = 1u << 16;
+
 struct PfSync {
   PfShared* sh;
   int32_t* status;
   __device__ bool wait(uint64_t* bar, uint32_t parity) const {
+    // the completed case costs one try_wait: the MMA warp pays every wait in its issue stream
+    if (mbar_try_wait(bar, parity)) return true;
     volatile int* ab = &sh->abort;
     for (uint32_t i = 0; i < kSpinLimit; ++i) {
       if (*ab) return false;
       if (mbar_try_wait(bar, parity)) return true;
-      if (i > 16) __nanosleep(64);
+      if (i > kFastPolls) __nanosleep(64);
     }
     *ab = 1;
     atomicOr(status, kStatusTimeout);
@@ -147,30 +153,42 @@ __device__ __forceinline__ uint32_t f16_idesc(int n) {
   return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kPfRows >> 4) << 24);
 }
 
-// D += A (tensor memory, lanes = rows, f16 pairs per column) x B (shared memory).
+// D += A (tensor memory, lanes = rows, f16 pairs per column) x B (shared memory), issued by
+// one elected lane of the converged MMA warp (a measured 15% cheaper per instruction than a
+// lone lane in a divergent branch).
 __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b,
                                            uint32_t idesc, uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "{\n\t.reg .pred p, e;\n\tsetp.ne.b32 p, %4, 0;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+// Stores 32 columns of this warp's 32 lanes; tmem_st_wait() completes them.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
   asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-      "%11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
+      "%29, %30, %31, %32};" ::"r"(taddr),
       "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
-      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+      "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]),
+      "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
+      "r"(v[29]), "r"(v[30]), "r"(v[31])
       : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// Arrives on `bar` once the MMAs this warp's elected lane issued have completed.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   smem_u32(bar))
-               : "memory");
+  asm volatile(
+      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
+          smem_u32(bar))
+      : "memory");
 }
 
 __device__ __forceinline__ void tc_fence_before() {
@@ -289,21 +307,23 @@ __device__ void pf_producer_b(const DecodeParams& P, const PfMaps& M, uint8_t* s
   bool aborted = false;
   for (int64_t it = blockIdx.x; it < n_items && !aborted; it += gridDim.x) {
     const Item im = item_of<MODE>(P, it, mtiles);
-    const int nblk = nk * (kStgK / kBlkK);
-    for (int blk = 0; blk < nblk; ++blk) {  // rows off .. off+n of the sorted rows, 64 k
-      const int s = (int)(bi % kBStages);
+    const int nst = nk * (kStgK / kAbK);
+    // boxes of 32 rows: rows past n (the next segment's, or zero fill) are never read
+    const int nbox = (im.n + kBoxRows - 1) / kBoxRows;
+    for (int j = 0; j < nst; ++j) {  // rows off .. off+n of the sorted rows, 128 k
+      const int s = (int)(bi % kAbStages);
       int go = 1;
       if (lane == 0) {
-        if (bi >= kBStages && !sy.wait(&sh->empty_b[s], (uint32_t)((bi / kBStages) - 1) & 1u))
+        if (bi >= kAbStages && !sy.wait(&sh->empty_ab[s], (uint32_t)((bi / kAbStages) - 1) & 1u))
           go = 0;
         if (go) {
-          // 64-row boxes: rows past n (the next segment's, or zero fill) are never read
-          const int nbox = (im.n + kBoxRows - 1) / kBoxRows;
-          mbar_arrive_expect_tx(&sh->full_b[s], (uint32_t)(nbox * kBoxRows * 128));
+          const uint32_t bar = smem_u32(&sh->full_ab[s]);
+          mbar_arrive_expect_tx(&sh->full_ab[s], (uint32_t)((kAbK / kBlkK) * nbox * kBoxRows * 128));
           uint8_t* bt = smem + kBOff + s * kBBytes;
-          for (int g = 0; g < nbox; ++g)
-            tma_2d(smem_u32(bt + g * kBoxRows * 128), &M.act, blk * kBlkK, im.off + kBoxRows * g,
-                   smem_u32(&sh->full_b[s]));
+          for (int h = 0; h < kAbK / kBlkK; ++h)
+            for (int g = 0; g < nbox; ++g)
+              tma_2d(smem_u32(bt + h * kBSub + g * kBoxRows * 128), &M.act,
+                     j * kAbK + h * kBlkK, im.off + kBoxRows * g, bar);
         }
       }
       go = __shfl_sync(0xffffffffu, go, 0);
@@ -314,10 +334,11 @@ __device__ void pf_producer_b(const DecodeParams& P, const PfMaps& M, uint8_t* s
       ++bi;
     }
   }
+  // copies in flight must land before the CTA exits (only after an abort can any be pending)
   if (lane != 0 || !sh->abort) return;
-  for (int64_t j = bi - kBStages > 0 ? bi - kBStages : 0; j < bi; ++j)
+  for (int64_t j = bi - kAbStages > 0 ? bi - kAbStages : 0; j < bi; ++j)
     for (uint32_t k = 0; k < kSpinLimit; ++k) {
-      if (mbar_try_wait(&sh->full_b[j % kBStages], (uint32_t)(j / kBStages) & 1u)) break;
+      if (mbar_try_wait(&sh->full_ab[j % kAbStages], (uint32_t)(j / kAbStages) & 1u)) break;
       __nanosleep(64);
     }
 }
@@ -326,95 +347,107 @@ template <int MODE>
 __device__ void pf_dequant(uint8_t* smem, const PfSync& sy, int64_t n_items, int nk) {
   PfShared* sh = sy.sh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int half = (warp - kWarpDq) >> 2;  // k 32*half .. 32*half+31 of each A tile
-  const int t = 32 * (warp & 3) + lane;    // A row = the tensor-memory lane this warp may write
+  // warp group g dequantises the k half g of every packed stage (A stages ai, ai % 2 == g),
+  // so one group's tensor-memory stores overlap the other's conversions
+  const int grp = (warp - kWarpDq) >> 2;
+  const int t = 32 * (warp & 3) + lane;  // A row = the tensor-memory lane this warp may write
   // packed-stage line of A row t. gate_up: lane l < 16 of a warp holds gate row 16q + l and
   // lane l + 16 the matching up row (lines 0..63 gate, 64..127 up), so that an 8-lane phase
   // reads 8 distinct swizzle lines (no bank conflicts) and SwiGLU pairs lanes l, l ^ 16.
   const int line = MODE == kGateUp ? 16 * (warp & 3) + (lane & 15) + 64 * (lane >> 4) : t;
-  const uint32_t a_base = sh->tmem_base + ((uint32_t)(32 * (warp & 3)) << 16) +
-                          (uint32_t)(kTmemA + 16 * half);
+  const uint32_t a_base = sh->tmem_base + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)kTmemA;
   int64_t pi = 0, ai = 0;
   for (int64_t it = blockIdx.x; it < n_items; it += gridDim.x) {
     for (int kc = 0; kc < nk; ++kc) {
       const int s = (int)(pi % kPStages);
       if (!sy.wait(&sh->full_p[s], (uint32_t)(pi / kPStages) & 1u)) return;
       const uint8_t* st = smem + kPOff + s * kPBytes;
-      for (int j = 0; j < kStgK / kBlkK; ++j) {
-        const int sa = (int)(ai % kAStages);
-        if (ai >= kAStages && !sy.wait(&sh->empty_a[sa], (uint32_t)((ai / kAStages) - 1) & 1u))
-          return;
-        tc_fence_after();
-        // 16 packed bytes = k 64j + 32half .. +32 of the stage; scales of its two 16-k blocks
-        const uint4 w = *reinterpret_cast<const uint4*>(st + swz(line, 2 * j + half));
-        const uint16_t sc =
-            *reinterpret_cast<const uint16_t*>(st + kPfRows * 128 + line * 16 + 4 * j + 2 * half);
-        const uint32_t s01 = e4m3x2_to_f16x2(sc);
-        const uint32_t sb[2] = {f16x2_bcast_lo(s01), f16x2_bcast_hi(s01)};
-        const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-        uint32_t o[16];  // 32 f16 in k order: column c holds k (2c, 2c+1) of this half
+      const int64_t my = ai + grp;  // this group's A stage of the packed stage
+      ai += kStgK / kAbK;
+      const int sa = (int)(my % kAbStages);
+      if (my >= kAbStages && !sy.wait(&sh->empty_ab[sa], (uint32_t)((my / kAbStages) - 1) & 1u))
+        return;
+      tc_fence_after();
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+      for (int q = 0; q < kAbK / kBlkK; ++q) {
+        // 32 packed bytes = k 128g + 64q .. +63 of the stage, and the scales of its 4 16-k
+        // blocks
+        const int c = 4 * grp + 2 * q;  // 16-byte chunk of the 128-byte packed line
+        const uint4 w0 = *reinterpret_cast<const uint4*>(st + swz(line, c));
+        const uint4 w1 = *reinterpret_cast<const uint4*>(st + swz(line, c + 1));
+        const uint32_t sc =
+            *reinterpret_cast<const uint32_t*>(st + kPfRows * 128 + line * 16 + 4 * (c >> 1));
+        const uint32_t s01 = e4m3x2_to_f16x2((uint16_t)(sc & 0xffffu));
+        const uint32_t s23 = e4m3x2_to_f16x2((uint16_t)(sc >> 16));
+        const uint32_t sb[4] = {f16x2_bcast_lo(s01), f16x2_bcast_hi(s01), f16x2_bcast_lo(s23),
+                                f16x2_bcast_hi(s23)};
+        const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        uint32_t o[32];  // 64 f16 in k order: column cc holds k (2cc, 2cc+1)
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
           uint32_t h[4];
-          e2m1x8_to_f16x2x4(words[c], h);
-          const uint32_t s16 = sb[c >> 1];
+          e2m1x8_to_f16x2x4(words[cc], h);
+          const uint32_t s16 = sb[cc >> 1];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) o[4 * c + q] = hmul2(h[q], s16);
+          for (int e = 0; e < 4; ++e) o[4 * cc + e] = hmul2(h[e], s16);
         }
-        tmem_st16(a_base + (uint32_t)(sa * kACols), o);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sh->full_a[sa]);
-        ++ai;
+        tmem_st32(a_base + (uint32_t)(sa * kACols + q * (kBlkK / 2)), o);
       }
+      tmem_st_wait();
+      tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sh->empty_p[s]);
+      if (lane == 0) {
+        mbar_arrive(&sh->full_ab[sa]);
+        mbar_arrive(&sh->empty_p[s]);
+      }
       ++pi;
     }
   }
 }
 
+// The whole MMA warp runs this loop (waits on every lane, a vote to reconverge, then one
+// elected lane issues): per 128-k stage one wait, 8 MMAs and one commit. Per-instruction
+// costs measured on this loop's shape: ~90 cycles per MMA issue, ~170 per bounded wait that
+// checks the abort flag first, ~50 per commit, against N/2 cycles of tensor work per MMA, so
+// the hand-offs are amortised over 8 MMAs.
 template <int MODE>
 __device__ void pf_mma(const DecodeParams& P, uint8_t* smem, const PfSync& sy, int64_t n_items,
                        int mtiles, int nk) {
   PfShared* sh = sy.sh;
   const uint32_t tbase = sh->tmem_base;
-  int64_t ai = 0, bi = 0, di = 0;
+  int64_t ai = 0, di = 0;
   bool issued = false;
   for (int64_t it = blockIdx.x; it < n_items; it += gridDim.x) {
     const Item im = item_of<MODE>(P, it, mtiles);
     const int buf = (int)(di & 1);
-    if (di >= 2 && !sy.wait(&sh->empty_d[buf], (uint32_t)((di / 2) - 1) & 1u)) break;
+    // every wait's outcome is voted on, so the warp stays converged for elect.sync
+    bool ok = __all_sync(0xffffffffu,
+                         di < 2 || sy.wait(&sh->empty_d[buf], (uint32_t)((di / 2) - 1) & 1u));
+    if (!ok) break;
     tc_fence_after();
     const uint32_t d = tbase + (uint32_t)(buf * kPrefillSegRoutes);
     const uint32_t idesc = f16_idesc(im.n);
-    const int nblk = nk * (kStgK / kBlkK);
-    bool ok = true;
-    for (int b = 0; b < nblk; ++b) {
-      const int sa = (int)(ai % kAStages), sb = (int)(bi % kBStages);
-      if (!sy.wait(&sh->full_a[sa], (uint32_t)(ai / kAStages) & 1u) ||
-          !sy.wait(&sh->full_b[sb], (uint32_t)(bi / kBStages) & 1u)) {
-        ok = false;
-        break;
-      }
+    const int nst = nk * (kStgK / kAbK);
+    for (int j = 0; j < nst; ++j) {
+      const int s = (int)(ai % kAbStages);
+      ok = __all_sync(0xffffffffu, sy.wait(&sh->full_ab[s], (uint32_t)(ai / kAbStages) & 1u));
+      if (!ok) break;
       tc_fence_after();
-      const uint32_t a0 = tbase + (uint32_t)(kTmemA + sa * kACols);
-      const uint32_t b0 = smem_u32(smem + kBOff + sb * kBBytes);
+      const uint32_t a0 = tbase + (uint32_t)(kTmemA + s * kACols);
+      const uint32_t b0 = smem_u32(smem + kBOff + s * kBBytes);
 #pragma unroll
-      for (int kk = 0; kk < kBlkK / 16; ++kk)
-        mma_f16_ts(d, a0 + (uint32_t)(kk * 8), sw128_desc(b0 + kk * 32), idesc,
-                   (b > 0 || kk > 0) ? 1u : 0u);
+      for (int kk = 0; kk < kAbK / 16; ++kk)
+        mma_f16_ts(d, a0 + (uint32_t)(kk * 8), sw128_desc(b0 + (kk >> 2) * kBSub + (kk & 3) * 32),
+                   idesc, (j > 0 || kk > 0) ? 1u : 0u);
       issued = true;
-      mma_commit(&sh->empty_a[sa]);
-      mma_commit(&sh->empty_b[sb]);
+      mma_commit(&sh->empty_ab[s]);
       ++ai;
-      ++bi;
     }
     if (!ok) break;
     mma_commit(&sh->full_d[buf]);
     ++di;
   }
-  // every MMA this thread issued has finished once the drain barrier completes
+  // every MMA this warp issued has finished once the drain barrier completes
   if (issued) {
     mma_commit(&sh->drain);
     for (uint32_t k = 0; k < kSpinLimit; ++k) {
@@ -542,9 +575,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kPStages; ++s)
       mbar_init(&sh->full_p[s], 1), mbar_init(&sh->empty_p[s], kDqWarps);
-    for (int s = 0; s < kAStages; ++s)
-      mbar_init(&sh->full_a[s], kDqWarps), mbar_init(&sh->empty_a[s], 1);
-    for (int s = 0; s < kBStages; ++s) mbar_init(&sh->full_b[s], 1), mbar_init(&sh->empty_b[s], 1);
+    // an A/B stage is full once its dequant warp group and the activation producer arrived
+    for (int s = 0; s < kAbStages; ++s)
+      mbar_init(&sh->full_ab[s], kDqWarps / 2 + 1), mbar_init(&sh->empty_ab[s], 1);
     for (int s = 0; s < 2; ++s) mbar_init(&sh->full_d[s], 1), mbar_init(&sh->empty_d[s], 4);
     mbar_init(&sh->drain, 1);
     sh->abort = 0;
@@ -577,8 +610,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   } else if (warp == kWarpTmaB) {
     pf_producer_b<MODE>(P, M, smem, sy, n_items, mtiles, nk);
   } else if (warp == kWarpMma) {
-    if (lane == 0) pf_mma<MODE>(P, smem, sy, n_items, mtiles, nk);
-    __syncwarp();
+    pf_mma<MODE>(P, smem, sy, n_items, mtiles, nk);
   } else if (warp < kWarpEpi) {
     pf_dequant<MODE>(smem, sy, n_items, nk);
   } else {

@@ -65,7 +65,11 @@ constexpr int kPfRows = 128;                 // MMA M
 constexpr int kBlkK = 64;                    // k per 128-byte-swizzled operand sub-tile
 constexpr int kAbK = 128;                    // k per A/B stage: 8 MMAs per hand-off
 constexpr int kStgK = 256;                   // k per packed stage
-constexpr int kPStages = 4, kAbStages = 3;
+// A tiles live in tensor memory (3 fit beside two accumulators), B tiles in shared memory (4,
+// so that three stay queued while a slot's TMA refill is in flight); the barrier ring follows
+// the B slots: stage i is announced on full_ab[i % kBStages] once its A tile (slot i % kAStages)
+// and its B tile are in place, and the MMAs' commit of stage i arrives on empty_ab[i % kBStages].
+constexpr int kPStages = 3, kAStages = 3, kBStages = 4;
 constexpr int kPfWarps = 15;
 constexpr int kPfThreads = kPfWarps * kWarp;
 // warp roles: weights producer, MMA, 8 dequant warps, 4 epilogue warps, activations producer
@@ -76,15 +80,15 @@ static_assert(kPrefillSegRoutes % kBoxRows == 0, "segment cap in whole boxes");
 constexpr int kBSub = kPrefillSegRoutes * 128;  // one 64-k sub-tile of up to cap rows
 constexpr int kBBytes = (kAbK / kBlkK) * kBSub;
 // tensor memory (512 columns x 128 lanes of 32 bit): two D buffers of up to
-// kPrefillSegRoutes fp32 columns, then kAbStages A tiles of 128 k (64 columns of f16 pairs)
+// kPrefillSegRoutes fp32 columns, then kAStages A tiles of 128 k (64 columns of f16 pairs)
 constexpr int kTmemCols = 512;
 constexpr int kTmemA = 2 * kPrefillSegRoutes;
 constexpr int kACols = kAbK / 2;
-static_assert(kTmemA + kAbStages * kACols <= kTmemCols, "tensor memory budget");
-constexpr int kPfHeader = 12288;
+static_assert(kTmemA + kAStages * kACols <= kTmemCols, "tensor memory budget");
+constexpr int kPfHeader = 6144;
 constexpr int kPOff = kPfHeader;
 constexpr int kBOff = kPOff + kPStages * kPBytes;
-constexpr int kPfSmem = kBOff + kAbStages * kBBytes;
+constexpr int kPfSmem = kBOff + kBStages * kBBytes;
 static_assert(kPBytes % 1024 == 0 && kBOff % 1024 == 0 && kBSub % 1024 == 0, "1024-B atoms");
 static_assert(kPfSmem <= 227 * 1024, "shared memory");
 
@@ -98,7 +102,7 @@ struct PfMaps {
 // header layout
 struct PfShared {
   uint64_t full_p[kPStages], empty_p[kPStages];
-  uint64_t full_ab[kAbStages], empty_ab[kAbStages];
+  uint64_t full_ab[kBStages], empty_ab[kBStages];
   uint64_t full_d[2], empty_d[2];
   uint64_t drain;
   uint32_t tmem_base;
@@ -311,10 +315,10 @@ __device__ void pf_producer_b(const DecodeParams& P, const PfMaps& M, uint8_t* s
     // boxes of 32 rows: rows past n (the next segment's, or zero fill) are never read
     const int nbox = (im.n + kBoxRows - 1) / kBoxRows;
     for (int j = 0; j < nst; ++j) {  // rows off .. off+n of the sorted rows, 128 k
-      const int s = (int)(bi % kAbStages);
+      const int s = (int)(bi % kBStages);
       int go = 1;
       if (lane == 0) {
-        if (bi >= kAbStages && !sy.wait(&sh->empty_ab[s], (uint32_t)((bi / kAbStages) - 1) & 1u))
+        if (bi >= kBStages && !sy.wait(&sh->empty_ab[s], (uint32_t)((bi / kBStages) - 1) & 1u))
           go = 0;
         if (go) {
           const uint32_t bar = smem_u32(&sh->full_ab[s]);
@@ -336,9 +340,9 @@ __device__ void pf_producer_b(const DecodeParams& P, const PfMaps& M, uint8_t* s
   }
   // copies in flight must land before the CTA exits (only after an abort can any be pending)
   if (lane != 0 || !sh->abort) return;
-  for (int64_t j = bi - kAbStages > 0 ? bi - kAbStages : 0; j < bi; ++j)
+  for (int64_t j = bi - kBStages > 0 ? bi - kBStages : 0; j < bi; ++j)
     for (uint32_t k = 0; k < kSpinLimit; ++k) {
-      if (mbar_try_wait(&sh->full_ab[j % kAbStages], (uint32_t)(j / kAbStages) & 1u)) break;
+      if (mbar_try_wait(&sh->full_ab[j % kBStages], (uint32_t)(j / kBStages) & 1u)) break;
       __nanosleep(64);
     }
 }
@@ -364,8 +368,10 @@ __device__ void pf_dequant(uint8_t* smem, const PfSync& sy, int64_t n_items, int
       const uint8_t* st = smem + kPOff + s * kPBytes;
       const int64_t my = ai + grp;  // this group's A stage of the packed stage
       ai += kStgK / kAbK;
-      const int sa = (int)(my % kAbStages);
-      if (my >= kAbStages && !sy.wait(&sh->empty_ab[sa], (uint32_t)((my / kAbStages) - 1) & 1u))
+      const int sa = (int)(my % kAStages);
+      // A slot sa last held stage my - kAStages: wait for that stage's commit
+      const int64_t prev = my - kAStages;
+      if (prev >= 0 && !sy.wait(&sh->empty_ab[prev % kBStages], (uint32_t)(prev / kBStages) & 1u))
         return;
       tc_fence_after();
 #pragma unroll
@@ -397,7 +403,7 @@ __device__ void pf_dequant(uint8_t* smem, const PfSync& sy, int64_t n_items, int
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&sh->full_ab[sa]);
+        mbar_arrive(&sh->full_ab[my % kBStages]);
         mbar_arrive(&sh->empty_p[s]);
       }
       ++pi;
@@ -429,11 +435,11 @@ __device__ void pf_mma(const DecodeParams& P, uint8_t* smem, const PfSync& sy, i
     const uint32_t idesc = f16_idesc(im.n);
     const int nst = nk * (kStgK / kAbK);
     for (int j = 0; j < nst; ++j) {
-      const int s = (int)(ai % kAbStages);
-      ok = __all_sync(0xffffffffu, sy.wait(&sh->full_ab[s], (uint32_t)(ai / kAbStages) & 1u));
+      const int s = (int)(ai % kBStages);
+      ok = __all_sync(0xffffffffu, sy.wait(&sh->full_ab[s], (uint32_t)(ai / kBStages) & 1u));
       if (!ok) break;
       tc_fence_after();
-      const uint32_t a0 = tbase + (uint32_t)(kTmemA + s * kACols);
+      const uint32_t a0 = tbase + (uint32_t)(kTmemA + (int)(ai % kAStages) * kACols);
       const uint32_t b0 = smem_u32(smem + kBOff + s * kBBytes);
 #pragma unroll
       for (int kk = 0; kk < kAbK / 16; ++kk)
@@ -576,7 +582,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     for (int s = 0; s < kPStages; ++s)
       mbar_init(&sh->full_p[s], 1), mbar_init(&sh->empty_p[s], kDqWarps);
     // an A/B stage is full once its dequant warp group and the activation producer arrived
-    for (int s = 0; s < kAbStages; ++s)
+    for (int s = 0; s < kBStages; ++s)
       mbar_init(&sh->full_ab[s], kDqWarps / 2 + 1), mbar_init(&sh->empty_ab[s], 1);
     for (int s = 0; s < 2; ++s) mbar_init(&sh->full_d[s], 1), mbar_init(&sh->empty_d[s], 4);
     mbar_init(&sh->drain, 1);

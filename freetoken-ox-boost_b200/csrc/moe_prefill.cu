@@ -214,21 +214,6 @@ __device__ __forceinline__ float swiglu_fast(float g, float u, float limit) {
   return (g * sg) * u;
 }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
-      "%12, %13, %14, %15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr)
-      : "memory");
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
 struct Item {
   int e, off, cnt, mt, n;  // expert (E = shared), segment start/size, weight tile, MMA N
   bool sh;
@@ -463,6 +448,61 @@ __device__ void pf_mma(const DecodeParams& P, uint8_t* smem, const PfSync& sy, i
   }
 }
 
+// Route metadata of one item, column n = lane + 32 k of the segment: route id (-1 past cnt)
+// and factor (gate_up: the token's 2^s; down: the routed weight, 1 for the shared expert).
+constexpr int kMetaK = kPrefillSegRoutes / kWarp;
+static_assert(kPrefillSegRoutes % kWarp == 0, "metadata slots");
+struct Meta {
+  int r[kMetaK];
+  float f[kMetaK];
+};
+
+__device__ __forceinline__ void meta_routes(const DecodeParams& P, const Item& im, int lane,
+                                            Meta& m) {
+#pragma unroll
+  for (int k = 0; k < kMetaK; ++k) {
+    const int n = lane + kWarp * k;
+    m.r[k] = n < im.cnt ? P.sorted[im.off + n] : -1;
+  }
+}
+
+template <int MODE>
+__device__ __forceinline__ void meta_factors(const DecodeParams& P, const Item& im, Meta& m) {
+#pragma unroll
+  for (int k = 0; k < kMetaK; ++k) {
+    const int r = m.r[k];
+    float f = 1.f;
+    if (r >= 0) {
+      if (MODE == kGateUp)
+        f = P.xscale[im.sh ? (int64_t)r - P.R : (int64_t)r / P.top_k];
+      else if (!im.sh)
+        f = P.topk_w[r];
+    }
+    m.f[k] = f;
+  }
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+      "%30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Epilogue warps. The next item's route ids are loaded before this item's D wait and its
+// factors right after it, so both global round trips overlap this item's D work; D is read
+// 32 columns per tensor-memory wait.
 template <int MODE>
 __device__ void pf_epilogue(const DecodeParams& P, const PfSync& sy, int64_t n_items, int mtiles) {
   PfShared* sh = sy.sh;
@@ -474,28 +514,32 @@ __device__ void pf_epilogue(const DecodeParams& P, const PfSync& sy, int64_t n_i
   float* col_f = sh->col_f[ew];
   const uint32_t tbase = sh->tmem_base + ((uint32_t)(32 * quarter) << 16);
   int64_t di = 0;
-  for (int64_t it = blockIdx.x; it < n_items; it += gridDim.x) {
-    const Item im = item_of<MODE>(P, it, mtiles);
-    // the item's columns: route id (-1 past cnt) and factor (gate_up: the token's 2^s;
-    // down: the routed weight, 1 for the shared expert); loaded before the D wait so the
-    // latency overlaps the MMAs
-    for (int n = lane; n < im.n; n += kWarp) {
-      int r = -1;
-      float f = 1.f;
-      if (n < im.cnt) {
-        r = P.sorted[im.off + n];
-        if (MODE == kGateUp)
-          f = P.xscale[im.sh ? (int64_t)r - P.R : (int64_t)r / P.top_k];
-        else if (!im.sh)
-          f = P.topk_w[r];
-      }
-      col_r[n] = r;
-      col_f[n] = f;
+  Meta nx;
+  int64_t it = blockIdx.x;
+  Item im{};
+  if (it < n_items) {
+    im = item_of<MODE>(P, it, mtiles);
+    meta_routes(P, im, lane, nx);
+    meta_factors<MODE>(P, im, nx);
+  }
+  for (; it < n_items; it += gridDim.x) {
+#pragma unroll
+    for (int k = 0; k < kMetaK; ++k) {
+      col_r[lane + kWarp * k] = nx.r[k];
+      col_f[lane + kWarp * k] = nx.f[k];
     }
     __syncwarp();
+    const int64_t it2 = it + gridDim.x;
+    const bool has_next = it2 < n_items;
+    Item im2{};
+    if (has_next) {
+      im2 = item_of<MODE>(P, it2, mtiles);
+      meta_routes(P, im2, lane, nx);
+    }
     const int buf = (int)(di & 1);
     if (!sy.wait(&sh->full_d[buf], (uint32_t)(di / 2) & 1u)) return;
     tc_fence_after();
+    if (has_next) meta_factors<MODE>(P, im2, nx);
     const uint32_t taddr = tbase + (uint32_t)(buf * kPrefillSegRoutes);
     if (MODE == kGateUp) {
       const int I = P.I;
@@ -508,16 +552,17 @@ __device__ void pf_epilogue(const DecodeParams& P, const PfSync& sy, int64_t n_i
       // receiving the partner's value with one shuffle, so all 32 lanes do useful work.
       const bool upper = (lane & 16) != 0;
       const bool dbg = P.dbg_ic1 || P.dbg_h || P.dbg_sic1 || P.dbg_sh;
-      for (int c0 = 0; c0 < im.n; c0 += 16) {
-        float v[16];
-        tmem_ld16(taddr + (uint32_t)c0, v);
+      for (int c0 = 0; c0 < im.n; c0 += 32) {
+        float v[32];
+        tmem_ld32(taddr + (uint32_t)c0, v);
 #pragma unroll
-        for (int p2 = 0; p2 < 8; ++p2) {
+        for (int p2 = 0; p2 < 16; ++p2) {
           const float send = upper ? v[2 * p2] : v[2 * p2 + 1];
           const float recv = __shfl_xor_sync(0xffffffffu, send, 16);
           const float own = upper ? v[2 * p2 + 1] : v[2 * p2];
           const float g = upper ? recv : own, u = upper ? own : recv;
           const int n = c0 + 2 * p2 + (upper ? 1 : 0);
+          if (n >= im.n) continue;
           const int r = col_r[n];
           if (r < 0) continue;
           const float xs = col_f[n];
@@ -549,18 +594,19 @@ __device__ void pf_epilogue(const DecodeParams& P, const PfSync& sy, int64_t n_i
       const int row = kPfRows * im.mt + m;
       const uint16_t* glob = im.sh ? P.dn.s_global : P.dn.global + (int64_t)im.e * H;
       const float gl = __half2float(__ushort_as_half(glob[row]));
-      for (int c0 = 0; c0 < im.n; c0 += 16) {
-        float v[16];
-        tmem_ld16(taddr + (uint32_t)c0, v);
+      uint16_t* out = (im.sh ? P.ic3s : P.ic3) + row;
+      const int64_t r0 = im.sh ? P.R : 0;  // shared-expert routes R + t are rows t of ic3s
+      for (int c0 = 0; c0 < im.n; c0 += 32) {
+        float v[32];
+        tmem_ld32(taddr + (uint32_t)c0, v);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
+        for (int i = 0; i < 32; ++i) {
           const int n = c0 + i;
+          if (n >= im.n) break;
           const int r = col_r[n];
           if (r < 0) continue;
-          if (im.sh)
-            P.ic3s[((int64_t)r - P.R) * H + row] = f32_to_bf16_bits(v[i] * gl);
-          else
-            P.ic3[(int64_t)r * H + row] = f32_to_bf16_bits((v[i] * gl) * col_f[n]);
+          out[((int64_t)r - r0) * H] =
+              f32_to_bf16_bits(im.sh ? v[i] * gl : (v[i] * gl) * col_f[n]);
         }
       }
     }
@@ -568,6 +614,7 @@ __device__ void pf_epilogue(const DecodeParams& P, const PfSync& sy, int64_t n_i
     __syncwarp();
     if (lane == 0) mbar_arrive(&sh->empty_d[buf]);
     ++di;
+    im = im2;
   }
 }
 

@@ -13,6 +13,9 @@ sharded contiguously; tokens and outputs move over NVLink peer memory inside the
 kernels (--ep-transport p2p, default) or by NCCL all_to_all (--ep-transport nccl, the
 collective-library baseline); value = tokens/s of the whole box.
 Timed steps replay one CUDA graph per layer (--no-graphs: eager launches).
+The line's "prefill" object is BASELINE config 2 on one GPU: a T=4096 prefill chunk through
+the tcgen05 grouped GEMMs (ftb.moe_prefill), with its own tensor-pipe roofline (--no-prefill
+skips it).
 
 Prints one JSON line (rank 0). `--impl reference` times the reference's CPU MoE executor
 semantics (the C++ restatement in oracle/, the reference's own executor being unbuildable)
@@ -51,6 +54,9 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="skip the T=1/4/16 decode sweep")
+    ap.add_argument("--no-prefill", action="store_true",
+                    help="skip the config 2 prefill measurement (T=--prefill-tokens)")
+    ap.add_argument("--prefill-tokens", type=int, default=4096)
     ap.add_argument("--no-graphs", dest="graphs", action="store_false",
                     help="time eager launches instead of CUDA-graph replay")
     ap.add_argument("--ep-transport", choices=["p2p", "nccl"], default="p2p",
@@ -73,6 +79,18 @@ def measured_peaks():
         return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs, copy)"
     except (OSError, KeyError, ValueError):
         return FALLBACK_HBM_GBS, "fallback (6.65 TB/s, earlier measurement on this pool)"
+
+
+def measured_tensor_peaks():
+    """(burst, sustained) dense bf16 TFLOP/s and where they come from."""
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return (float(d["bf16_tflops"]), float(d["bf16_tflops_sustained"]),
+                "measured (MEASURED_PEAKS.json bf16_tflops / bf16_tflops_sustained, cuBLAS)")
+    except (OSError, KeyError, ValueError):
+        return 1590.0, 1400.0, "fallback (1.59 / 1.4 PFLOP/s, earlier measurement on this pool)"
 
 
 class ClockSampler:
@@ -360,6 +378,8 @@ def run_ftb_single(args, torch):
     }
     if not args.no_sweep:
         out["decode_sweep"] = sweep_decode(torch, ftb, layers, args)
+    if not args.no_prefill:
+        out["prefill"] = bench_prefill(torch, ftb, layers, args)
     if not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(torch, layers, args.cpu_seconds)
     return out
@@ -394,6 +414,84 @@ def sweep_decode(torch, ftb, layers: "Layers", args):
                          "host_issue_ms_per_step": round(host_ms, 4),
                          "kernels_ms": {k: round(statistics.mean(v), 4) for k, v in kt.items()}}
     return res
+
+
+def bench_prefill(torch, ftb, layers: "Layers", args):
+    """one prefill chunk of T tokens (flat N(0,1) router logits) through
+    ftb.moe_prefill on the same rotated layer banks, eager launches (route, sort, permute,
+    gate_up, down, combine). The tensor roofline is taken per GEMM: useful FLOPs per launch =
+    2 x rows x (output rows) x K with rows = T x (top_k + 1) (routed + shared routes)."""
+    from ftb import _lib, synth
+
+    T = args.prefill_tokens
+    nl = len(layers.banks)
+    inps = [synth.make_inputs(T, H, E, seed=3000 + l, device="cuda") for l in range(nl)]
+    outs = [torch.empty(T, H, dtype=torch.bfloat16, device="cuda") for _ in range(nl)]
+
+    def step(i):
+        l = i % nl
+        w, ids = ftb.fused_topk(None, inps[l].logits, TOPK, True)
+        ftb.moe_prefill(inps[l].x, layers.banks[l], w, ids, shared=layers.shared[l],
+                        out=outs[l])
+
+    for i in range(max(3, args.warmup)):
+        step(i)
+    steps = min(max(8, args.steps // 4), 60)
+    clocks = ClockSampler(torch, 0)
+    clocks.start()
+    ms = time_steps(torch, step, steps)
+    clk = clocks.stop()
+    kt = kernel_times(_lib, torch, step, 8)
+    rows = T * (TOPK + 1)
+    flops = {"gate_up_gemv": 2.0 * rows * 2 * I * H, "down_gemv": 2.0 * rows * H * I}
+    burst, sustained, src = measured_tensor_peaks()
+    gemms = {}
+    for k, f in flops.items():
+        t = statistics.mean(kt[k])
+        ach = f / (t * 1e-3) / 1e12
+        gemms[k] = {"avg_launch_ms": round(t, 4), "tflops": round(ach, 1),
+                    "frac_burst": round(ach / burst, 4), "frac_sustained": round(ach / sustained, 4)}
+    gemm_ms = sum(statistics.mean(kt[k]) for k in flops)
+    ach = sum(flops.values()) / (gemm_ms * 1e-3) / 1e12
+    hx = [inp.x.cpu().pin_memory() for inp in inps]
+    hl = [inp.logits.cpu().pin_memory() for inp in inps]
+    hout = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+    dx = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    dl = torch.empty(T, E, dtype=torch.float32, device="cuda")
+    dout = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+
+    def e2e_one(i):
+        l = i % nl
+        dx.copy_(hx[l], non_blocking=True)
+        dl.copy_(hl[l], non_blocking=True)
+        w, ids = ftb.fused_topk(dx, dl, TOPK, True)
+        ftb.moe_prefill(dx, layers.banks[l], w, ids, shared=layers.shared[l], out=dout)
+        hout.copy_(dout, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    for i in range(3):
+        e2e_one(i)
+    n_e2e = min(steps, 20)
+    t0 = time.perf_counter()
+    for i in range(n_e2e):
+        e2e_one(i)
+    e2e_dt = (time.perf_counter() - t0) / n_e2e
+    return {
+        "workload": f"config 2 prefill T={T}: H{H} I{I} E{E} top{TOPK} +1 shared expert, "
+                    "flat N(0,1) router logits, layers rotated",
+        "tokens_per_s": round(T * 1e3 / ms, 1), "ms_per_step": round(ms, 4), "steps": steps,
+        "layer_tflops": round(sum(flops.values()) / (ms * 1e-3) / 1e12, 1),
+        "kernels_ms": {k: round(statistics.mean(v), 4) for k, v in kt.items()},
+        "roofline": {"kernel": "gate_up + down (k_prefill_gemm<0>, <1>), tcgen05 kind::f16",
+                     "bound": "tensor", "achieved": round(ach, 1), "peak": burst,
+                     "unit": "TFLOP/s", "frac": round(ach / burst, 4),
+                     "frac_sustained": round(ach / sustained, 4), "peak_source": src,
+                     "flops_per_step": sum(flops.values()), "per_gemm": gemms},
+        "e2e": {"value": round(T / e2e_dt, 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": T * H * 2 + T * E * 4, "d2h_bytes_per_step": T * H * 2},
+        "gpu_launches_per_step": 6,  # route_topk, sort, permute, gate_up, down, combine
+        "clocks": clk,
+    }
 
 
 def run_reference(args, torch):

@@ -58,26 +58,33 @@ namespace ftb {
 int get_map_2d(CUtensorMap* out, const void* base, CUtensorMapDataType dtype, int esize,
                uint64_t inner, uint64_t rows, uint32_t box_inner, uint32_t box_rows,
                bool swizzle128);
+int get_map_3d(CUtensorMap* out, const void* base, CUtensorMapDataType dtype,
+               const uint64_t (&dims)[3], const uint64_t (&strides)[2],
+               const uint32_t (&box)[3], bool swizzle128);
 
 namespace {
 
-constexpr int kPfRows = 128;                 // MMA M
+constexpr int kPair = 2;                     // CTAs per cluster: one MMA of M = 256 per pair
+constexpr int kPfRows = 128;                 // weight rows (MMA M) per CTA
 constexpr int kBlkK = 64;                    // k per 128-byte-swizzled operand sub-tile
 constexpr int kAbK = 128;                    // k per A/B stage: 8 MMAs per hand-off
 constexpr int kStgK = 256;                   // k per packed stage
-// A tiles live in tensor memory (3 fit beside two accumulators), B tiles in shared memory (4,
-// so that three stay queued while a slot's TMA refill is in flight); the barrier ring follows
+// A tiles live in tensor memory (3 fit beside two accumulators), B tiles in shared memory (6,
+// so that five stay queued while a slot's TMA refill is in flight); the barrier ring follows
 // the B slots: stage i is announced on full_ab[i % kBStages] once its A tile (slot i % kAStages)
 // and its B tile are in place, and the MMAs' commit of stage i arrives on empty_ab[i % kBStages].
-constexpr int kPStages = 3, kAStages = 3, kBStages = 4;
+constexpr int kPStages = 4, kAStages = 3, kBStages = 6;
 constexpr int kPfWarps = 15;
 constexpr int kPfThreads = kPfWarps * kWarp;
 // warp roles: weights producer, MMA, 8 dequant warps, 4 epilogue warps, activations producer
 constexpr int kWarpTma = 0, kWarpMma = 1, kWarpDq = 2, kDqWarps = 8, kWarpEpi = 10, kWarpTmaB = 14;
 constexpr int kPBytes = kPfRows * 128 + kPfRows * 16;  // 18432
-constexpr int kBoxRows = 32;                 // rows per activation TMA box
-static_assert(kPrefillSegRoutes % kBoxRows == 0, "segment cap in whole boxes");
-constexpr int kBSub = kPrefillSegRoutes * 128;  // one 64-k sub-tile of up to cap rows
+// Each CTA of a pair holds half of the segment's N routes (N % 16 == 0, so a multiple of 8
+// rows: whole 8-row swizzle atoms), loaded as boxes of 16 rows.
+constexpr int kBoxRows = 16;
+constexpr int kHalfRoutes = kPrefillSegRoutes / kPair;
+static_assert(kHalfRoutes % kBoxRows == 0, "half segment in whole boxes");
+constexpr int kBSub = kHalfRoutes * 128;  // one 64-k sub-tile of up to cap / 2 rows
 constexpr int kBBytes = (kAbK / kBlkK) * kBSub;
 // tensor memory (512 columns x 128 lanes of 32 bit): two D buffers of up to
 // kPrefillSegRoutes fp32 columns, then kAStages A tiles of 128 k (64 columns of f16 pairs)
@@ -94,12 +101,20 @@ static_assert(kPfSmem <= 227 * 1024, "shared memory");
 
 enum { kGateUp = 0, kDown = 1 };
 
+// One TMA instruction per operand tile where it fits (per-SM TMA throughput grows with the
+// bytes per instruction): gate_up weights as 3D views [gate/up half][row][k] whose box holds a
+// tile's 64 gate and 64 up rows; activations as a 3D view [64-k block][row][64 k] whose box
+// holds a stage's two 64-k sub-tiles of kHalfRoutes rows (act3), with 16-row 2D boxes (act)
+// for halves of at most 48 rows.
 struct PfMaps {
   CUtensorMap w, s, sw, ss;  // packed weights / scales: routed bank, shared expert
   CUtensorMap act;           // activation rows in sorted order (xs or h16), f16, 64 x 16 boxes
+  CUtensorMap act3;          // the same rows, boxes of 2 x kHalfRoutes x 64
 };
+constexpr int kBigBoxMin = 48;  // halves of more rows than this load as one act3 box
 
-// header layout
+// header layout (the same offsets in both CTAs of a pair: the leader's barriers are addressed
+// from the peer through mapa)
 struct PfShared {
   uint64_t full_p[kPStages], empty_p[kPStages];
   uint64_t full_ab[kBStages], empty_ab[kBStages];
@@ -120,6 +135,7 @@ constexpr uint32_t kFastPolls = 1u << 16;
 struct PfSync {
   PfShared* sh;
   int32_t* status;
+  int rank;  // CTA rank in the pair; rank 0 issues the MMAs
   __device__ bool wait(uint64_t* bar, uint32_t parity) const {
     // the completed case costs one try_wait: the MMA warp pays every wait in its issue stream
     if (mbar_try_wait(bar, parity)) return true;
@@ -135,6 +151,32 @@ struct PfSync {
   }
 };
 
+// Address of the same shared-memory object in the pair's leader CTA (rank 0).
+__device__ __forceinline__ uint32_t leader_addr(const void* p) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(r) : "r"(smem_u32(p)));
+  return r;
+}
+
+// Arrival on a barrier of the leader CTA. Default (CTA-scope release) semantics: what the
+// leader consumes after it is tensor memory ordered by tcgen05.fence::before_thread_sync, so a
+// cluster-scope release, whose fence measured 13% of the peer's stall samples, is not needed.
+__device__ __forceinline__ void mbar_arrive_leader(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(leader_addr(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ int cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return (int)r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+
 __device__ __forceinline__ int swz(int line, int c) { return line * 128 + ((c ^ (line & 7)) << 4); }
 
 __device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
@@ -145,6 +187,33 @@ __device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap* map, int
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
       : "memory");
 }
+__device__ __forceinline__ void tma_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z,
+                                       uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
+}
+
+// Tile loads into this CTA's shared memory whose bytes complete on the leader's barrier
+// `bar_leader` (a shared::cluster address), so one barrier covers both halves of a B tile.
+__device__ __forceinline__ void tma_2d_pair(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            uint32_t bar_leader) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_leader)
+      : "memory");
+}
+__device__ __forceinline__ void tma_3d_pair(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            int z, uint32_t bar_leader) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar_leader)
+      : "memory");
+}
 
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms 1024 B apart.
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
@@ -152,19 +221,22 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
-// Instruction descriptor, kind::f16: D fp32, A and B f16, both K-major, M = 128, N.
+// Instruction descriptor, kind::f16: D fp32, A and B f16, both K-major, M = 256 (128 rows in
+// each CTA of the pair), N.
 __device__ __forceinline__ uint32_t f16_idesc(int n) {
-  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kPfRows >> 4) << 24);
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)((kPair * kPfRows) >> 4) << 24);
 }
 
-// D += A (tensor memory, lanes = rows, f16 pairs per column) x B (shared memory), issued by
-// one elected lane of the converged MMA warp (a measured 15% cheaper per instruction than a
-// lone lane in a divergent branch).
+// D += A x B^T for the pair: A rows 0..127 from the leader's tensor memory, 128..255 from the
+// peer's (same address, f16 pairs per column), B rows 0..N/2-1 from the leader's shared
+// memory and N/2..N-1 from the peer's (same descriptor), D rows split like A. Issued by one
+// elected lane of the leader's converged MMA warp (a measured 15% cheaper per instruction
+// than a lone lane in a divergent branch).
 __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b,
                                            uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p, e;\n\tsetp.ne.b32 p, %4, 0;\n\telect.sync _|e, 0xffffffff;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
       : "memory");
 }
@@ -186,11 +258,21 @@ __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
-// Arrives on `bar` once the MMAs this warp's elected lane issued have completed.
+// Arrives on `bar` in both CTAs of the pair once the MMAs this warp's elected lane issued
+// have completed.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster"
+      ".multicast::cluster.b64 [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
+      "h"((uint16_t)0x3)
+      : "memory");
+}
+// The same, arriving on this CTA's `bar` only.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile(
       "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
-      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
           smem_u32(bar))
       : "memory");
 }
@@ -219,11 +301,13 @@ struct Item {
   bool sh;
 };
 
+// Pair item `it`: segment it / mpairs against weight tiles 2 (it % mpairs) and +1 (this CTA's
+// rank picks one); both CTAs of a pair walk the same item sequence.
 template <int MODE>
-__device__ __forceinline__ Item item_of(const DecodeParams& P, int64_t it, int mtiles) {
+__device__ __forceinline__ Item item_of(const DecodeParams& P, int64_t it, int mpairs, int rank) {
   Item r;
-  const int a = (int)(it / mtiles);
-  r.mt = (int)(it % mtiles);
+  const int a = (int)(it / mpairs);
+  r.mt = kPair * (int)(it % mpairs) + rank;
   r.e = P.seg_expert[a];
   r.off = P.seg_off[a];
   r.cnt = P.seg_cnt[a];
@@ -236,17 +320,18 @@ __device__ __forceinline__ Item item_of(const DecodeParams& P, int64_t it, int m
 
 template <int MODE>
 __device__ void pf_producer_w(const DecodeParams& P, const PfMaps& M, uint8_t* smem,
-                              const PfSync& sy, int64_t n_items, int mtiles, int nk) {
+                              const PfSync& sy, int64_t n_items, int mpairs, int nk) {
   PfShared* sh = sy.sh;
   const int lane = threadIdx.x & 31;
   const int rows_e = MODE == kGateUp ? 2 * P.I : P.H;
   int64_t pi = 0;
   bool aborted = false;
-  for (int64_t it = blockIdx.x; it < n_items && !aborted; it += gridDim.x) {
-    const Item im = item_of<MODE>(P, it, mtiles);
+  for (int64_t it = blockIdx.x / kPair; it < n_items && !aborted; it += gridDim.x / kPair) {
+    const Item im = item_of<MODE>(P, it, mpairs, sy.rank);
     const CUtensorMap* wm = im.sh ? &M.sw : &M.w;
     const CUtensorMap* sm = im.sh ? &M.ss : &M.s;
     const int ebase = im.sh ? 0 : im.e * rows_e;
+    const int half0 = im.sh ? 0 : 2 * im.e;  // gate_up: the expert's gate half in the 3D views
     for (int kc = 0; kc < nk; ++kc) {  // packed weights + scales of 128 rows x 256 k
       const int s = (int)(pi % kPStages);
       int go = 1;
@@ -258,11 +343,9 @@ __device__ void pf_producer_w(const DecodeParams& P, const PfMaps& M, uint8_t* s
           const uint32_t bar = smem_u32(&sh->full_p[s]);
           mbar_arrive_expect_tx(&sh->full_p[s], (uint32_t)kPBytes);
           if (MODE == kGateUp) {
-            const int y0 = ebase + 64 * im.mt, y1 = ebase + P.I + 64 * im.mt;
-            tma_2d(smem_u32(st), wm, kc * 128, y0, bar);
-            tma_2d(smem_u32(st + 64 * 128), wm, kc * 128, y1, bar);
-            tma_2d(smem_u32(st + kPfRows * 128), sm, kc * 16, y0, bar);
-            tma_2d(smem_u32(st + kPfRows * 128 + 64 * 16), sm, kc * 16, y1, bar);
+            // gate rows 64 mt .. +63, then the matching up rows (lines 0..63, 64..127)
+            tma_3d(smem_u32(st), wm, kc * 128, 64 * im.mt, half0, bar);
+            tma_3d(smem_u32(st + kPfRows * 128), sm, kc * 16, 64 * im.mt, half0, bar);
           } else {
             const int y = ebase + kPfRows * im.mt;
             tma_2d(smem_u32(st), wm, kc * 128, y, bar);
@@ -289,30 +372,41 @@ __device__ void pf_producer_w(const DecodeParams& P, const PfMaps& M, uint8_t* s
 
 template <int MODE>
 __device__ void pf_producer_b(const DecodeParams& P, const PfMaps& M, uint8_t* smem,
-                              const PfSync& sy, int64_t n_items, int mtiles, int nk) {
+                              const PfSync& sy, int64_t n_items, int mpairs, int nk) {
   PfShared* sh = sy.sh;
   const int lane = threadIdx.x & 31;
   int64_t bi = 0;
   bool aborted = false;
-  for (int64_t it = blockIdx.x; it < n_items && !aborted; it += gridDim.x) {
-    const Item im = item_of<MODE>(P, it, mtiles);
+  for (int64_t it = blockIdx.x / kPair; it < n_items && !aborted; it += gridDim.x / kPair) {
+    const Item im = item_of<MODE>(P, it, mpairs, sy.rank);
     const int nst = nk * (kStgK / kAbK);
-    // boxes of 32 rows: rows past n (the next segment's, or zero fill) are never read
-    const int nbox = (im.n + kBoxRows - 1) / kBoxRows;
-    for (int j = 0; j < nst; ++j) {  // rows off .. off+n of the sorted rows, 128 k
+    // this CTA's half of the segment: rows off + rank n/2 .. +n/2 of the sorted rows, as one
+    // 3D box of kHalfRoutes rows x both sub-tiles, or for small halves 16-row boxes per
+    // sub-tile (rows past n/2, the peer's or zero fill, are never read)
+    const bool big = im.n / kPair > kBigBoxMin;
+    const int nbox = big ? 1 : (im.n / kPair + kBoxRows - 1) / kBoxRows;
+    const uint32_t bytes = big ? (uint32_t)((kAbK / kBlkK) * kBSub)
+                               : (uint32_t)((kAbK / kBlkK) * nbox * kBoxRows * 128);
+    const int row0 = im.off + sy.rank * (im.n / kPair);
+    for (int j = 0; j < nst; ++j) {  // 128 k per stage
       const int s = (int)(bi % kBStages);
       int go = 1;
       if (lane == 0) {
         if (bi >= kBStages && !sy.wait(&sh->empty_ab[s], (uint32_t)((bi / kBStages) - 1) & 1u))
           go = 0;
         if (go) {
-          const uint32_t bar = smem_u32(&sh->full_ab[s]);
-          mbar_arrive_expect_tx(&sh->full_ab[s], (uint32_t)((kAbK / kBlkK) * nbox * kBoxRows * 128));
+          // both halves complete on the leader's barrier, which expects the pair's bytes
+          const uint32_t bar = leader_addr(&sh->full_ab[s]);
+          if (sy.rank == 0) mbar_arrive_expect_tx(&sh->full_ab[s], kPair * bytes);
           uint8_t* bt = smem + kBOff + s * kBBytes;
-          for (int h = 0; h < kAbK / kBlkK; ++h)
-            for (int g = 0; g < nbox; ++g)
-              tma_2d(smem_u32(bt + h * kBSub + g * kBoxRows * 128), &M.act,
-                     j * kAbK + h * kBlkK, im.off + kBoxRows * g, bar);
+          if (big) {
+            tma_3d_pair(smem_u32(bt), &M.act3, 0, row0, j * (kAbK / kBlkK), bar);
+          } else {
+            for (int h = 0; h < kAbK / kBlkK; ++h)
+              for (int g = 0; g < nbox; ++g)
+                tma_2d_pair(smem_u32(bt + h * kBSub + g * kBoxRows * 128), &M.act,
+                            j * kAbK + h * kBlkK, row0 + kBoxRows * g, bar);
+          }
         }
       }
       go = __shfl_sync(0xffffffffu, go, 0);
@@ -323,13 +417,11 @@ __device__ void pf_producer_b(const DecodeParams& P, const PfMaps& M, uint8_t* s
       ++bi;
     }
   }
-  // copies in flight must land before the CTA exits (only after an abort can any be pending)
+  // copies in flight must land before the CTA exits (only after an abort can any be pending).
+  // They complete on the leader's barriers, which the peer cannot poll: both CTAs give them a
+  // fixed grace time (a tile load takes microseconds) before the pair's final cluster barrier.
   if (lane != 0 || !sh->abort) return;
-  for (int64_t j = bi - kBStages > 0 ? bi - kBStages : 0; j < bi; ++j)
-    for (uint32_t k = 0; k < kSpinLimit; ++k) {
-      if (mbar_try_wait(&sh->full_ab[j % kBStages], (uint32_t)(j / kBStages) & 1u)) break;
-      __nanosleep(64);
-    }
+  for (int k = 0; k < 1000; ++k) __nanosleep(1000);
 }
 
 template <int MODE>
@@ -346,7 +438,7 @@ __device__ void pf_dequant(uint8_t* smem, const PfSync& sy, int64_t n_items, int
   const int line = MODE == kGateUp ? 16 * (warp & 3) + (lane & 15) + 64 * (lane >> 4) : t;
   const uint32_t a_base = sh->tmem_base + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)kTmemA;
   int64_t pi = 0, ai = 0;
-  for (int64_t it = blockIdx.x; it < n_items; it += gridDim.x) {
+  for (int64_t it = blockIdx.x / kPair; it < n_items; it += gridDim.x / kPair) {
     for (int kc = 0; kc < nk; ++kc) {
       const int s = (int)(pi % kPStages);
       if (!sy.wait(&sh->full_p[s], (uint32_t)(pi / kPStages) & 1u)) return;
@@ -388,7 +480,10 @@ __device__ void pf_dequant(uint8_t* smem, const PfSync& sy, int64_t n_items, int
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&sh->full_ab[my % kBStages]);
+        if (sy.rank == 0)
+          mbar_arrive(&sh->full_ab[my % kBStages]);
+        else
+          mbar_arrive_leader(&sh->full_ab[my % kBStages]);
         mbar_arrive(&sh->empty_p[s]);
       }
       ++pi;
@@ -403,13 +498,13 @@ __device__ void pf_dequant(uint8_t* smem, const PfSync& sy, int64_t n_items, int
 // the hand-offs are amortised over 8 MMAs.
 template <int MODE>
 __device__ void pf_mma(const DecodeParams& P, uint8_t* smem, const PfSync& sy, int64_t n_items,
-                       int mtiles, int nk) {
+                       int mpairs, int nk) {
   PfShared* sh = sy.sh;
   const uint32_t tbase = sh->tmem_base;
   int64_t ai = 0, di = 0;
   bool issued = false;
-  for (int64_t it = blockIdx.x; it < n_items; it += gridDim.x) {
-    const Item im = item_of<MODE>(P, it, mtiles);
+  for (int64_t it = blockIdx.x / kPair; it < n_items; it += gridDim.x / kPair) {
+    const Item im = item_of<MODE>(P, it, mpairs, sy.rank);
     const int buf = (int)(di & 1);
     // every wait's outcome is voted on, so the warp stays converged for elect.sync
     bool ok = __all_sync(0xffffffffu,
@@ -421,7 +516,8 @@ __device__ void pf_mma(const DecodeParams& P, uint8_t* smem, const PfSync& sy, i
     const int nst = nk * (kStgK / kAbK);
     for (int j = 0; j < nst; ++j) {
       const int s = (int)(ai % kBStages);
-      ok = __all_sync(0xffffffffu, sy.wait(&sh->full_ab[s], (uint32_t)(ai / kBStages) & 1u));
+      ok = __all_sync(0xffffffffu,
+                      sy.wait(&sh->full_ab[s], (uint32_t)(ai / kBStages) & 1u));
       if (!ok) break;
       tc_fence_after();
       const uint32_t a0 = tbase + (uint32_t)(kTmemA + (int)(ai % kAStages) * kACols);
@@ -431,11 +527,11 @@ __device__ void pf_mma(const DecodeParams& P, uint8_t* smem, const PfSync& sy, i
         mma_f16_ts(d, a0 + (uint32_t)(kk * 8), sw128_desc(b0 + (kk >> 2) * kBSub + (kk & 3) * 32),
                    idesc, (j > 0 || kk > 0) ? 1u : 0u);
       issued = true;
-      mma_commit(&sh->empty_ab[s]);
+      mma_commit_pair(&sh->empty_ab[s]);
       ++ai;
     }
     if (!ok) break;
-    mma_commit(&sh->full_d[buf]);
+    mma_commit_pair(&sh->full_d[buf]);
     ++di;
   }
   // every MMA this warp issued has finished once the drain barrier completes
@@ -504,7 +600,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 // factors right after it, so both global round trips overlap this item's D work; D is read
 // 32 columns per tensor-memory wait.
 template <int MODE>
-__device__ void pf_epilogue(const DecodeParams& P, const PfSync& sy, int64_t n_items, int mtiles) {
+__device__ void pf_epilogue(const DecodeParams& P, const PfSync& sy, int64_t n_items, int mpairs) {
   PfShared* sh = sy.sh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int quarter = warp & 3;       // tensor-memory lanes this warp may read
@@ -515,25 +611,25 @@ __device__ void pf_epilogue(const DecodeParams& P, const PfSync& sy, int64_t n_i
   const uint32_t tbase = sh->tmem_base + ((uint32_t)(32 * quarter) << 16);
   int64_t di = 0;
   Meta nx;
-  int64_t it = blockIdx.x;
+  int64_t it = blockIdx.x / kPair;
   Item im{};
   if (it < n_items) {
-    im = item_of<MODE>(P, it, mtiles);
+    im = item_of<MODE>(P, it, mpairs, sy.rank);
     meta_routes(P, im, lane, nx);
     meta_factors<MODE>(P, im, nx);
   }
-  for (; it < n_items; it += gridDim.x) {
+  for (; it < n_items; it += gridDim.x / kPair) {
 #pragma unroll
     for (int k = 0; k < kMetaK; ++k) {
       col_r[lane + kWarp * k] = nx.r[k];
       col_f[lane + kWarp * k] = nx.f[k];
     }
     __syncwarp();
-    const int64_t it2 = it + gridDim.x;
+    const int64_t it2 = it + gridDim.x / kPair;
     const bool has_next = it2 < n_items;
     Item im2{};
     if (has_next) {
-      im2 = item_of<MODE>(P, it2, mtiles);
+      im2 = item_of<MODE>(P, it2, mpairs, sy.rank);
       meta_routes(P, im2, lane, nx);
     }
     const int buf = (int)(di & 1);
@@ -612,68 +708,85 @@ __device__ void pf_epilogue(const DecodeParams& P, const PfSync& sy, int64_t n_i
     }
     tc_fence_before();
     __syncwarp();
-    if (lane == 0) mbar_arrive(&sh->empty_d[buf]);
+    if (lane == 0) {
+      if (sy.rank == 0)
+        mbar_arrive(&sh->empty_d[buf]);
+      else
+        mbar_arrive_leader(&sh->empty_d[buf]);
+    }
     ++di;
     im = im2;
   }
 }
 
+// Launched in clusters of kPair CTAs. Barriers that the leader's MMA warp waits on (full_ab,
+// empty_d) collect both CTAs' arrivals in the leader; the leader's commits arrive on empty_ab
+// and full_d in both CTAs. The peer's full_ab / empty_d are initialised but unused.
 template <int MODE>
 __global__ void __launch_bounds__(kPfThreads, 1)
     k_prefill_gemm(const __grid_constant__ DecodeParams P, const __grid_constant__ PfMaps M) {
   extern __shared__ __align__(1024) uint8_t smem[];
   PfShared* sh = reinterpret_cast<PfShared*>(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rank = cluster_rank();
   pdl_launch_dependents();
   if (threadIdx.x == 0) {
     for (int s = 0; s < kPStages; ++s)
       mbar_init(&sh->full_p[s], 1), mbar_init(&sh->empty_p[s], kDqWarps);
-    // an A/B stage is full once its dequant warp group and the activation producer arrived
+    // an A/B stage is full once both CTAs' dequant warp groups and the leader's activation
+    // producer (expecting both CTAs' bytes) arrived
     for (int s = 0; s < kBStages; ++s)
-      mbar_init(&sh->full_ab[s], kDqWarps / 2 + 1), mbar_init(&sh->empty_ab[s], 1);
-    for (int s = 0; s < 2; ++s) mbar_init(&sh->full_d[s], 1), mbar_init(&sh->empty_d[s], 4);
+      mbar_init(&sh->full_ab[s], kPair * (kDqWarps / 2) + 1), mbar_init(&sh->empty_ab[s], 1);
+    for (int s = 0; s < 2; ++s)
+      mbar_init(&sh->full_d[s], 1), mbar_init(&sh->empty_d[s], kPair * 4);
     mbar_init(&sh->drain, 1);
     sh->abort = 0;
     fence_mbar_init();
   }
-  if (warp == kWarpMma) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+  if (warp == kWarpMma) {  // the same columns in both CTAs of the pair
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(&sh->tmem_base)),
                  "r"(kTmemCols)
                  : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
   }
   if (warp == kWarpTma && lane == 0) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&M.w)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&M.s)) : "memory");
   }
-  if (warp == kWarpTmaB && lane == 0)
+  if (warp == kWarpTmaB && lane == 0) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&M.act)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&M.act3)) : "memory");
+  }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();  // both CTAs' barriers are initialised before any cross-CTA arrival
   tc_fence_after();
   pdl_wait();  // segment table, activations and counters come from earlier launches
-  const PfSync sy{sh, P.status};
+  const PfSync sy{sh, P.status, rank};
   const int K = MODE == kGateUp ? P.H : P.I;
   const int nk = K / kStgK;
   const int mtiles = MODE == kGateUp ? P.I / 64 : P.H / kPfRows;
-  const int64_t n_items = (int64_t)(*P.n_seg) * mtiles;
+  const int mpairs = mtiles / kPair;
+  const int64_t n_items = (int64_t)(*P.n_seg) * mpairs;
   if (warp == kWarpTma) {
-    pf_producer_w<MODE>(P, M, smem, sy, n_items, mtiles, nk);
+    pf_producer_w<MODE>(P, M, smem, sy, n_items, mpairs, nk);
   } else if (warp == kWarpTmaB) {
-    pf_producer_b<MODE>(P, M, smem, sy, n_items, mtiles, nk);
+    pf_producer_b<MODE>(P, M, smem, sy, n_items, mpairs, nk);
   } else if (warp == kWarpMma) {
-    pf_mma<MODE>(P, smem, sy, n_items, mtiles, nk);
+    if (rank == 0) pf_mma<MODE>(P, smem, sy, n_items, mpairs, nk);
   } else if (warp < kWarpEpi) {
     pf_dequant<MODE>(smem, sy, n_items, nk);
   } else {
-    pf_epilogue<MODE>(P, sy, n_items, mtiles);
+    pf_epilogue<MODE>(P, sy, n_items, mpairs);
   }
+  // neither CTA leaves (or frees tensor memory) while the leader's MMAs may read the peer's
+  // shared and tensor memory or either CTA may still arrive on the other's barriers
   tc_fence_before();
-  __syncthreads();
+  __syncwarp();  // the cluster barrier is .aligned: warps arrive converged
+  cluster_sync();
   if (warp == kWarpMma) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(sh->tmem_base),
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(sh->tmem_base),
                  "r"(kTmemCols)
                  : "memory");
   }
@@ -695,45 +808,91 @@ __global__ void __launch_bounds__(256) k_permute_rows(const DecodeParams P, __ha
   }
 }
 
+// gate_up packed weights / scales of `experts` experts as [2 experts][I rows][kb bytes]: box
+// {kb_box, 64 rows, 2 halves} = a tile's gate rows and the matching up rows.
+int gu_map(CUtensorMap* out, const void* base, uint64_t I, uint64_t kb, uint32_t kb_box,
+           uint64_t experts, bool swizzle128) {
+  const uint64_t dims[3] = {kb, I, 2 * experts};
+  const uint64_t strides[2] = {kb, I * kb};
+  const uint32_t box[3] = {kb_box, 64, 2};
+  return get_map_3d(out, base, CU_TENSOR_MAP_DATA_TYPE_UINT8, dims, strides, box, swizzle128);
+}
+
 template <int MODE>
 int make_pf_maps(const DecodeParams& P, PfMaps* M) {
   const BankView& b = MODE == kGateUp ? P.gu : P.dn;
   const uint64_t K = MODE == kGateUp ? P.H : P.I;
-  const uint64_t rows_e = MODE == kGateUp ? 2 * (uint64_t)P.I : (uint64_t)P.H;
-  const uint32_t box_rows = MODE == kGateUp ? 64 : kPfRows;
   const CUtensorMapDataType u8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
-  int st = get_map_2d(&M->w, b.packed, u8, 1, K / 2, rows_e * P.E, 128, box_rows, true);
-  if (!st) st = get_map_2d(&M->s, b.scale, u8, 1, K / 16, rows_e * P.E, 16, box_rows, false);
-  if (st) return st;
-  if (P.has_shared) {
-    st = get_map_2d(&M->sw, b.s_packed, u8, 1, K / 2, rows_e, 128, box_rows, true);
-    if (!st) st = get_map_2d(&M->ss, b.s_scale, u8, 1, K / 16, rows_e, 16, box_rows, false);
-    if (st) return st;
+  int st;
+  if (MODE == kGateUp) {
+    const uint64_t I = (uint64_t)P.I;
+    st = gu_map(&M->w, b.packed, I, K / 2, 128, (uint64_t)P.E, true);
+    if (!st) st = gu_map(&M->s, b.scale, I, K / 16, 16, (uint64_t)P.E, false);
+    if (!st && P.has_shared) st = gu_map(&M->sw, b.s_packed, I, K / 2, 128, 1, true);
+    if (!st && P.has_shared) st = gu_map(&M->ss, b.s_scale, I, K / 16, 16, 1, false);
   } else {
+    const uint64_t rows_e = (uint64_t)P.H;
+    st = get_map_2d(&M->w, b.packed, u8, 1, K / 2, rows_e * P.E, 128, kPfRows, true);
+    if (!st) st = get_map_2d(&M->s, b.scale, u8, 1, K / 16, rows_e * P.E, 16, kPfRows, false);
+    if (!st && P.has_shared)
+      st = get_map_2d(&M->sw, b.s_packed, u8, 1, K / 2, rows_e, 128, kPfRows, true);
+    if (!st && P.has_shared)
+      st = get_map_2d(&M->ss, b.s_scale, u8, 1, K / 16, rows_e, 16, kPfRows, false);
+  }
+  if (st) return st;
+  if (!P.has_shared) {
     M->sw = M->w;
     M->ss = M->s;
   }
-  // activation rows in sorted order: xs [R + Ts, H] (gate_up) or h16 [R + Ts, I] (down), f16,
-  // boxes of 64 rows x 64 k
+  // activation rows in sorted order: xs [R + Ts, H] (gate_up) or h16 [R + Ts, I] (down), f16
   const void* act = MODE == kGateUp ? (const void*)P.xs : (const void*)P.h16;
   const uint64_t act_rows = (uint64_t)(P.R + (P.has_shared ? P.Ts : 0));
-  return get_map_2d(&M->act, act, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, K, act_rows, kBlkK,
-                    kBoxRows, true);
+  st = get_map_2d(&M->act, act, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, K, act_rows, kBlkK,
+                  kBoxRows, true);
+  if (st) return st;
+  const uint64_t dims[3] = {(uint64_t)kBlkK, act_rows, K / kBlkK};
+  const uint64_t strides[2] = {K * 2, (uint64_t)kBlkK * 2};
+  const uint32_t box[3] = {(uint32_t)kBlkK, (uint32_t)kHalfRoutes, (uint32_t)(kAbK / kBlkK)};
+  return get_map_3d(&M->act3, act, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, dims, strides, box, true);
 }
 
+// Persistent grid of CTA pairs: as many clusters as can be resident at once (clusters are
+// placed within a GPC, so this can be below half the SM count), at most one per pair item.
 template <int MODE>
 int launch_pf(const DecodeParams& P, int64_t max_items, cudaStream_t stream) {
   PfMaps M;
   int st = make_pf_maps<MODE>(P, &M);
   if (st) return st;
-  cudaError_t err = cudaFuncSetAttribute(k_prefill_gemm<MODE>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem);
+  auto kern = k_prefill_gemm<MODE>;
+  cudaError_t err =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem);
   if (err != cudaSuccess) return cuda_status(err);
-  int64_t grid = sm_count();
-  if (max_items < grid) grid = max_items;
-  if (grid < 1) grid = 1;
-  return cuda_status(launch_pdl(k_prefill_gemm<MODE>, dim3((unsigned)grid), dim3(kPfThreads),
-                                (size_t)kPfSmem, stream, P, M));
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(kPfThreads);
+  cfg.dynamicSmemBytes = kPfSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kPair;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  static int max_clusters[2] = {0, 0};
+  if (!max_clusters[MODE]) {
+    cfg.gridDim = dim3((unsigned)(sm_count() / kPair * kPair));
+    int n = 0;
+    err = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+    if (err != cudaSuccess) return cuda_status(err);
+    max_clusters[MODE] = n > 0 ? n : 1;
+  }
+  int64_t pairs = max_clusters[MODE];
+  if (max_items < pairs) pairs = max_items;
+  if (pairs < 1) pairs = 1;
+  cfg.gridDim = dim3((unsigned)(pairs * kPair));
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, P, M));
 }
 
 }  // namespace
@@ -750,11 +909,11 @@ int launch_prefill_gemms(const DecodeParams& P, cudaStream_t stream) {
   prof_mark(FTB_KERNEL_PERMUTE, false, stream);
   if (st) return st;
   prof_mark(FTB_KERNEL_GATE_UP, true, stream);
-  st = launch_pf<kGateUp>(P, max_seg * (P.I / 64), stream);
+  st = launch_pf<kGateUp>(P, max_seg * (P.I / 64 / kPair), stream);
   prof_mark(FTB_KERNEL_GATE_UP, false, stream);
   if (st) return st;
   prof_mark(FTB_KERNEL_DOWN, true, stream);
-  st = launch_pf<kDown>(P, max_seg * (P.H / kPfRows), stream);
+  st = launch_pf<kDown>(P, max_seg * (P.H / kPfRows / kPair), stream);
   prof_mark(FTB_KERNEL_DOWN, false, stream);
   return st;
 }

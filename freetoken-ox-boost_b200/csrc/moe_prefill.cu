@@ -445,12 +445,9 @@ __device__ void pf_dequant(uint8_t* smem, const PfSync& sy, int64_t n_items, int
       const uint8_t* st = smem + kPOff + s * kPBytes;
       const int64_t my = ai + grp;  // this group's A stage of the packed stage
       ai += kStgK / kAbK;
-      const int sa = (int)(my % kAStages);
-      // A slot sa last held stage my - kAStages: wait for that stage's commit
-      const int64_t prev = my - kAStages;
-      if (prev >= 0 && !sy.wait(&sh->empty_ab[prev % kBStages], (uint32_t)(prev / kBStages) & 1u))
-        return;
-      tc_fence_after();
+      // convert first (registers), so that once the A slot frees only the tensor-memory
+      // stores stand between the slot's release and the stage's arrival
+      uint32_t o[kAbK / kBlkK][32];  // per 64-k half: 64 f16, column cc holds k (2cc, 2cc+1)
 #pragma unroll
       for (int q = 0; q < kAbK / kBlkK; ++q) {
         // 32 packed bytes = k 128g + 64q .. +63 of the stage, and the scales of its 4 16-k
@@ -465,17 +462,28 @@ __device__ void pf_dequant(uint8_t* smem, const PfSync& sy, int64_t n_items, int
         const uint32_t sb[4] = {f16x2_bcast_lo(s01), f16x2_bcast_hi(s01), f16x2_bcast_lo(s23),
                                 f16x2_bcast_hi(s23)};
         const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-        uint32_t o[32];  // 64 f16 in k order: column cc holds k (2cc, 2cc+1)
 #pragma unroll
         for (int cc = 0; cc < 8; ++cc) {
           uint32_t h[4];
           e2m1x8_to_f16x2x4(words[cc], h);
           const uint32_t s16 = sb[cc >> 1];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) o[4 * cc + e] = hmul2(h[e], s16);
+          for (int e = 0; e < 4; ++e) o[q][4 * cc + e] = hmul2(h[e], s16);
         }
-        tmem_st32(a_base + (uint32_t)(sa * kACols + q * (kBlkK / 2)), o);
       }
+      // the packed stage is consumed (both groups' halves are in registers once all 8 warps
+      // arrived)
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh->empty_p[s]);
+      const int sa = (int)(my % kAStages);
+      // A slot sa last held stage my - kAStages: wait for that stage's commit
+      const int64_t prev = my - kAStages;
+      if (prev >= 0 && !sy.wait(&sh->empty_ab[prev % kBStages], (uint32_t)(prev / kBStages) & 1u))
+        return;
+      tc_fence_after();
+#pragma unroll
+      for (int q = 0; q < kAbK / kBlkK; ++q)
+        tmem_st32(a_base + (uint32_t)(sa * kACols + q * (kBlkK / 2)), o[q]);
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
@@ -484,7 +492,6 @@ __device__ void pf_dequant(uint8_t* smem, const PfSync& sy, int64_t n_items, int
           mbar_arrive(&sh->full_ab[my % kBStages]);
         else
           mbar_arrive_leader(&sh->full_ab[my % kBStages]);
-        mbar_arrive(&sh->empty_p[s]);
       }
       ++pi;
     }

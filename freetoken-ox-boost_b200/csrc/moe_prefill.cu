@@ -74,10 +74,12 @@ constexpr int kStgK = 256;                   // k per packed stage
 // the B slots: stage i is announced on full_ab[i % kBStages] once its A tile (slot i % kAStages)
 // and its B tile are in place, and the MMAs' commit of stage i arrives on empty_ab[i % kBStages].
 constexpr int kPStages = 4, kAStages = 3, kBStages = 6;
-constexpr int kPfWarps = 15;
+constexpr int kPfWarps = 19;
 constexpr int kPfThreads = kPfWarps * kWarp;
-// warp roles: weights producer, MMA, 8 dequant warps, 4 epilogue warps, activations producer
-constexpr int kWarpTma = 0, kWarpMma = 1, kWarpDq = 2, kDqWarps = 8, kWarpEpi = 10, kWarpTmaB = 14;
+// warp roles: weights producer, MMA, 8 dequant warps, 8 epilogue warps (two per tensor-memory
+// lane quarter, alternate 16-column chunks of D), activations producer
+constexpr int kWarpTma = 0, kWarpMma = 1, kWarpDq = 2, kDqWarps = 8, kWarpEpi = 10, kEpiWarps = 8,
+              kWarpTmaB = 18;
 constexpr int kPBytes = kPfRows * 128 + kPfRows * 16;  // 18432
 // Each CTA of a pair holds half of the segment's N routes (N % 16 == 0, so a multiple of 8
 // rows: whole 8-row swizzle atoms), loaded as boxes of 16 rows.
@@ -92,7 +94,7 @@ constexpr int kTmemCols = 512;
 constexpr int kTmemA = 2 * kPrefillSegRoutes;
 constexpr int kACols = kAbK / 2;
 static_assert(kTmemA + kAStages * kACols <= kTmemCols, "tensor memory budget");
-constexpr int kPfHeader = 6144;
+constexpr int kPfHeader = 12288;
 constexpr int kPOff = kPfHeader;
 constexpr int kBOff = kPOff + kPStages * kPBytes;
 constexpr int kPfSmem = kBOff + kBStages * kBBytes;
@@ -123,8 +125,8 @@ struct PfShared {
   uint32_t tmem_base;
   int abort;
   // epilogue warp w (0..3): route id and factor of each column of its current item
-  int col_r[4][kPrefillSegRoutes];
-  float col_f[4][kPrefillSegRoutes];
+  int col_r[kEpiWarps][kPrefillSegRoutes];
+  float col_f[kEpiWarps][kPrefillSegRoutes];
 };
 static_assert(sizeof(PfShared) <= kPfHeader, "header");
 
@@ -585,27 +587,25 @@ __device__ __forceinline__ void meta_factors(const DecodeParams& P, const Item& 
   }
 }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
-      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
-      "%30, %31}, [%32];"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
         "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        "=r"(r[14]), "=r"(r[15])
       : "r"(taddr)
       : "memory");
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Epilogue warps. The next item's route ids are loaded before this item's D wait and its
-// factors right after it, so both global round trips overlap this item's D work; D is read
-// 32 columns per tensor-memory wait.
+// Epilogue warps, two per tensor-memory lane quarter, each taking alternate 16-column chunks
+// of D (one warp per quarter measured latency-bound: its per-element SwiGLU chains left the
+// MMA waiting for the accumulator). The next item's route ids are loaded before this item's
+// D wait and its factors right after it, so both global round trips overlap this item's work.
 template <int MODE>
 __device__ void pf_epilogue(const DecodeParams& P, const PfSync& sy, int64_t n_items, int mpairs) {
   PfShared* sh = sy.sh;
@@ -613,6 +613,7 @@ __device__ void pf_epilogue(const DecodeParams& P, const PfSync& sy, int64_t n_i
   const int quarter = warp & 3;       // tensor-memory lanes this warp may read
   const int m = 32 * quarter + lane;  // D row (A row) of this thread
   const int ew = warp - kWarpEpi;     // this warp's metadata slice
+  const int half = ew >> 2;           // this warp's 16-column chunks: c0 = 16 half + 32 i
   int* col_r = sh->col_r[ew];
   float* col_f = sh->col_f[ew];
   const uint32_t tbase = sh->tmem_base + ((uint32_t)(32 * quarter) << 16);
@@ -655,17 +656,17 @@ __device__ void pf_epilogue(const DecodeParams& P, const PfSync& sy, int64_t n_i
       // receiving the partner's value with one shuffle, so all 32 lanes do useful work.
       const bool upper = (lane & 16) != 0;
       const bool dbg = P.dbg_ic1 || P.dbg_h || P.dbg_sic1 || P.dbg_sh;
-      for (int c0 = 0; c0 < im.n; c0 += 32) {
-        float v[32];
-        tmem_ld32(taddr + (uint32_t)c0, v);
+      // chunks of 16 columns (im.n % 16 == 0: every column of a chunk is below n)
+      for (int c0 = 16 * half; c0 < im.n; c0 += 32) {
+        float v[16];
+        tmem_ld16(taddr + (uint32_t)c0, v);
 #pragma unroll
-        for (int p2 = 0; p2 < 16; ++p2) {
+        for (int p2 = 0; p2 < 8; ++p2) {
           const float send = upper ? v[2 * p2] : v[2 * p2 + 1];
           const float recv = __shfl_xor_sync(0xffffffffu, send, 16);
           const float own = upper ? v[2 * p2 + 1] : v[2 * p2];
           const float g = upper ? recv : own, u = upper ? own : recv;
           const int n = c0 + 2 * p2 + (upper ? 1 : 0);
-          if (n >= im.n) continue;
           const int r = col_r[n];
           if (r < 0) continue;
           const float xs = col_f[n];
@@ -699,13 +700,12 @@ __device__ void pf_epilogue(const DecodeParams& P, const PfSync& sy, int64_t n_i
       const float gl = __half2float(__ushort_as_half(glob[row]));
       uint16_t* out = (im.sh ? P.ic3s : P.ic3) + row;
       const int64_t r0 = im.sh ? P.R : 0;  // shared-expert routes R + t are rows t of ic3s
-      for (int c0 = 0; c0 < im.n; c0 += 32) {
-        float v[32];
-        tmem_ld32(taddr + (uint32_t)c0, v);
+      for (int c0 = 16 * half; c0 < im.n; c0 += 32) {
+        float v[16];
+        tmem_ld16(taddr + (uint32_t)c0, v);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
+        for (int i = 0; i < 16; ++i) {
           const int n = c0 + i;
-          if (n >= im.n) break;
           const int r = col_r[n];
           if (r < 0) continue;
           out[((int64_t)r - r0) * H] =
@@ -745,7 +745,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     for (int s = 0; s < kBStages; ++s)
       mbar_init(&sh->full_ab[s], kPair * (kDqWarps / 2) + 1), mbar_init(&sh->empty_ab[s], 1);
     for (int s = 0; s < 2; ++s)
-      mbar_init(&sh->full_d[s], 1), mbar_init(&sh->empty_d[s], kPair * 4);
+      mbar_init(&sh->full_d[s], 1), mbar_init(&sh->empty_d[s], kPair * kEpiWarps);
     mbar_init(&sh->drain, 1);
     sh->abort = 0;
     fence_mbar_init();
@@ -781,7 +781,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     pf_producer_b<MODE>(P, M, smem, sy, n_items, mpairs, nk);
   } else if (warp == kWarpMma) {
     if (rank == 0) pf_mma<MODE>(P, smem, sy, n_items, mpairs, nk);
-  } else if (warp < kWarpEpi) {
+  } else if (warp < kWarpEpi) {  // dequant warps
     pf_dequant<MODE>(smem, sy, n_items, nk);
   } else {
     pf_epilogue<MODE>(P, sy, n_items, mpairs);

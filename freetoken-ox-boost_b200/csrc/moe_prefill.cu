@@ -501,47 +501,57 @@ __device__ void pf_dequant(uint8_t* smem, const PfSync& sy, int64_t n_items, int
 }
 
 // The whole MMA warp runs this loop (waits on every lane, a vote to reconverge, then one
-// elected lane issues): per 128-k stage one wait, 8 MMAs and one commit. Per-instruction
-// costs measured on this loop's shape: ~90 cycles per MMA issue, ~170 per bounded wait that
-// checks the abort flag first, ~50 per commit, against N/2 cycles of tensor work per MMA, so
-// the hand-offs are amortised over 8 MMAs.
+// elected lane issues): per 128-k stage one wait, 8 MMAs and one commit. The tensor pipe
+// queues only a few MMAs (an issue blocks about as long as the MMA it waits behind runs), so
+// everything else in the loop is kept short: ring slots and phases are counted in registers,
+// descriptors are formed once per stage, and the next item's segment is read while this one
+// runs.
 template <int MODE>
 __device__ void pf_mma(const DecodeParams& P, uint8_t* smem, const PfSync& sy, int64_t n_items,
                        int mpairs, int nk) {
   PfShared* sh = sy.sh;
   const uint32_t tbase = sh->tmem_base;
-  int64_t ai = 0, di = 0;
-  bool issued = false;
-  for (int64_t it = blockIdx.x / kPair; it < n_items; it += gridDim.x / kPair) {
-    const Item im = item_of<MODE>(P, it, mpairs, sy.rank);
-    const int buf = (int)(di & 1);
+  const uint64_t bdesc0 = sw128_desc(smem_u32(smem + kBOff));
+  const int nst = nk * (kStgK / kAbK);
+  int sb = 0, sa = 0;        // B slot / barrier ring index, A slot
+  uint32_t ph = 0;           // phase parity of ring slot sb
+  uint32_t di = 0;           // items issued (D buffer di & 1)
+  bool issued = false, ok = true;
+  int64_t it = blockIdx.x / kPair;
+  Item im{};
+  if (it < n_items) im = item_of<MODE>(P, it, mpairs, sy.rank);
+  for (; it < n_items; it += gridDim.x / kPair) {
+    const int64_t it2 = it + gridDim.x / kPair;
+    Item im2{};
+    if (it2 < n_items) im2 = item_of<MODE>(P, it2, mpairs, sy.rank);  // loads in flight
+    const uint32_t buf = di & 1u;
     // every wait's outcome is voted on, so the warp stays converged for elect.sync
-    bool ok = __all_sync(0xffffffffu,
-                         di < 2 || sy.wait(&sh->empty_d[buf], (uint32_t)((di / 2) - 1) & 1u));
+    ok = __all_sync(0xffffffffu, di < 2 || sy.wait(&sh->empty_d[buf], ((di >> 1) - 1) & 1u));
     if (!ok) break;
     tc_fence_after();
-    const uint32_t d = tbase + (uint32_t)(buf * kPrefillSegRoutes);
+    const uint32_t d = tbase + buf * (uint32_t)kPrefillSegRoutes;
     const uint32_t idesc = f16_idesc(im.n);
-    const int nst = nk * (kStgK / kAbK);
     for (int j = 0; j < nst; ++j) {
-      const int s = (int)(ai % kBStages);
-      ok = __all_sync(0xffffffffu,
-                      sy.wait(&sh->full_ab[s], (uint32_t)(ai / kBStages) & 1u));
+      ok = __all_sync(0xffffffffu, sy.wait(&sh->full_ab[sb], ph));
       if (!ok) break;
       tc_fence_after();
-      const uint32_t a0 = tbase + (uint32_t)(kTmemA + (int)(ai % kAStages) * kACols);
-      const uint32_t b0 = smem_u32(smem + kBOff + s * kBBytes);
+      const uint32_t a0 = tbase + (uint32_t)(kTmemA + sa * kACols);
+      // descriptor start addresses advance in 16-byte units in the low bits
+      const uint64_t b0 = bdesc0 + (uint64_t)((sb * kBBytes) >> 4);
 #pragma unroll
       for (int kk = 0; kk < kAbK / 16; ++kk)
-        mma_f16_ts(d, a0 + (uint32_t)(kk * 8), sw128_desc(b0 + (kk >> 2) * kBSub + (kk & 3) * 32),
-                   idesc, (j > 0 || kk > 0) ? 1u : 0u);
+        mma_f16_ts(d, a0 + (uint32_t)(kk * 8),
+                   b0 + (uint64_t)((((kk >> 2) * kBSub) + (kk & 3) * 32) >> 4), idesc,
+                   (j > 0 || kk > 0) ? 1u : 0u);
       issued = true;
-      mma_commit_pair(&sh->empty_ab[s]);
-      ++ai;
+      mma_commit_pair(&sh->empty_ab[sb]);
+      if (++sb == kBStages) sb = 0, ph ^= 1u;
+      if (++sa == kAStages) sa = 0;
     }
     if (!ok) break;
     mma_commit_pair(&sh->full_d[buf]);
     ++di;
+    im = im2;
   }
   // every MMA this warp issued has finished once the drain barrier completes
   if (issued) {

@@ -151,7 +151,7 @@ static int layer_impl(bool prefill, const uint16_t* x, const ftb_nvfp4_bank* ban
                       void* workspace, size_t workspace_bytes, uint16_t* dbg_ic1, uint16_t* dbg_h,
                       uint16_t* dbg_ic3, uint16_t* dbg_sic1, uint16_t* dbg_sh,
                       uint16_t* dbg_sout, cudaStream_t stream) {
-  if (T < 0 || H <= 0 || I <= 0 || top_k < 1) return FTB_ERR_SHAPE;
+  if (T < 0 || H <= 0 || I <= 0 || top_k < 1 || top_k > 32) return FTB_ERR_SHAPE;
   if (H % 256 || I % 256) return FTB_ERR_SHAPE;
   if (!bank_ok(bank) || (shared && !bank_ok(shared))) return FTB_ERR_ARG;
   const int64_t E = bank->num_experts;

@@ -66,6 +66,8 @@ struct SortParams {
   int has_shared;
   int seg_cap;         // routes per segment at most (kSegRoutes for the decode GEMVs)
   int x_plain;         // stage x16 in natural k order (prefill) instead of round-interleaved
+  int stage_tpb;       // tokens staged per block (1: the whole block per row; 32: a warp each),
+                       // set by launch_sort_stage
   int block_m;         // > 0: also emit the padded (moe_align) outputs
   // outputs (decode segment table); seg_expert may be null
   int32_t* offsets;    // [E+1] unpadded, required

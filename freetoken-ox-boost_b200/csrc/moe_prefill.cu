@@ -810,18 +810,25 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 }
 
 // xs[pos] = x16[token of the route at sorted position pos] (routed rows, then the shared
-// expert's rows), so that the gate_up GEMM reads its B tiles as 2D boxes.
+// expert's rows), so that the gate_up GEMM reads its B tiles as 2D boxes. One warp per row
+// (H % 256 == 0: whole rounds of 32 16-byte chunks), all of a row's loads in flight at once.
 __global__ void __launch_bounds__(256) k_permute_rows(const DecodeParams P, __half* xs) {
   pdl_launch_dependents();
   pdl_wait();
   const int64_t nrows = P.R + (P.has_shared ? P.Ts : 0);
-  const int64_t nv = P.H / 8;
+  const int nv = P.H / 8;
+  const int lane = threadIdx.x & 31;
   const uint4* src = reinterpret_cast<const uint4*>(P.x16);
   uint4* dst = reinterpret_cast<uint4*>(xs);
-  for (int64_t row = blockIdx.x; row < nrows; row += gridDim.x) {
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < nrows;
+       row += warps) {
     const int r = P.sorted[row];
     const int64_t tok = r >= P.R ? (int64_t)r - P.R : (int64_t)r / P.top_k;
-    for (int64_t v = threadIdx.x; v < nv; v += blockDim.x) dst[row * nv + v] = src[tok * nv + v];
+    const uint4* s0 = src + tok * nv;
+    uint4* d0 = dst + row * nv;
+#pragma unroll 8
+    for (int v = lane; v < nv; v += kWarp) d0[v] = s0[v];
   }
 }
 
@@ -918,7 +925,9 @@ int launch_prefill_gemms(const DecodeParams& P, cudaStream_t stream) {
   if (P.H % 256 || P.I % 256 || !P.xs) return FTB_ERR_SHAPE;
   const int64_t max_seg = max_segments(P.R, P.E, P.Ts, P.has_shared, kPrefillSegRoutes);
   const int64_t nrows = P.R + (P.has_shared ? P.Ts : 0);
-  int64_t gp = nrows < 4 * (int64_t)sm_count() ? nrows : 4 * (int64_t)sm_count();
+  // 8 rows (warps) per block, up to 8 blocks per SM resident
+  int64_t gp = ceil_div(nrows, (int64_t)8);
+  if (gp > 8 * (int64_t)sm_count()) gp = 8 * (int64_t)sm_count();
   if (gp < 1) gp = 1;
   prof_mark(FTB_KERNEL_PERMUTE, true, stream);
   int st = cuda_status(launch_pdl(k_permute_rows, dim3((unsigned)gp), dim3(256), 0, stream, P,

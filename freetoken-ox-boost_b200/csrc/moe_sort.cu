@@ -4,10 +4,11 @@
 //   block 0      stable counting sort of the T*top_k routes by expert (ties by route index),
 //                the per-expert segment table the GEMV kernels walk, and (align mode) the
 //                BLOCK_M-padded sorted_ids / expert_ids of moe_align_block_size;
-//   blocks 1..T  one token each: bf16 row -> f16 row scaled by 2^-s (s from the row's max
-//                exponent so that max|x|*2^-s lies in [2^14, 2^15): the f16 tensor-core
-//                operand is then exact for every element within 2^-31 of the row max),
-//                stored round-interleaved (ri_chunk) for the GEMV's fragment loads.
+//   blocks 1..   one token per warp (32 per block): bf16 row -> f16 row scaled by 2^-s (s
+//                from the row's max exponent so that max|x|*2^-s lies in [2^14, 2^15): the
+//                f16 tensor-core operand is then exact for every element within 2^-31 of the
+//                row max), stored round-interleaved (ri_chunk) for the GEMV's fragment loads
+//                (plain order for the prefill GEMMs).
 //
 // The sort is single-CTA: 32 warps each own a contiguous chunk of routes; __match_any_sync
 // ranks equal experts inside a 32-route group, so the result is the same on every run
@@ -22,6 +23,13 @@ namespace {
 
 constexpr int kSortThreads = 1024;
 constexpr int kSortWarps = kSortThreads / kWarp;
+// Large route counts load kSortBatch groups of 32 routes per warp at once and match equal
+// experts with ballots (the passes are latency-bound on those loads, and the hardware match
+// takes a pass per distinct expert); small ones keep a single group per step and the hardware
+// match, whose shorter code measured faster on this once-per-layer path (T=1: 12.5 vs 23 us;
+// T=4096: 91 vs 67 us).
+constexpr int kSortBatch = 8;
+constexpr int64_t kBatchedSortRoutes = 8192;
 
 // Exclusive block-wide scan of one value per thread (blockDim.x == 1024). Returns the
 // exclusive prefix; *total receives the sum over the block.
@@ -53,7 +61,23 @@ __device__ int block_exclusive_scan(int v, int* sm_warp, int* total) {
   return r;
 }
 
-__device__ void sort_block(const SortParams& P, int* hist /* [32][E] */) {
+// Lanes holding the same value e (in [-1, 2^nbits)), as __match_any_sync(full, e) returns,
+// from one ballot per bit plus one for validity: the hardware match takes about one pass per
+// distinct value, and a warp of routes over hundreds of experts holds ~32 distinct ones.
+__device__ __forceinline__ unsigned match_peers(int e, int nbits) {
+  const bool valid = e >= 0;
+  const unsigned vm = __ballot_sync(0xffffffffu, valid);
+  unsigned peers = valid ? vm : ~vm;
+  for (int b = 0; b < nbits; ++b) {
+    const bool bit = valid && ((e >> b) & 1);
+    const unsigned m = __ballot_sync(0xffffffffu, bit);
+    peers &= bit ? m : ~m;
+  }
+  return peers;
+}
+
+template <int BATCH, bool BALLOT>
+__device__ void sort_block_t(const SortParams& P, int* hist /* [32][E] */) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int E = P.E;
   const int64_t R = P.R;
@@ -64,24 +88,32 @@ __device__ void sort_block(const SortParams& P, int* hist /* [32][E] */) {
   for (int i = tid; i < kSortWarps * E; i += kSortThreads) hist[i] = 0;
   __syncthreads();
 
+  const int nbits = E > 1 ? 32 - __clz(E - 1) : 0;
   const int64_t chunk = ceil_div(ceil_div(R, kSortWarps), 32) * 32;
   const int64_t beg = warp * chunk;
   const int64_t end = (beg + chunk < R) ? beg + chunk : R;
   const unsigned lt_mask = (1u << lane) - 1u;
 
-  // pass 1: per-warp histograms
-  for (int64_t base = beg; base < end; base += 32) {
-    const int64_t r = base + lane;
-    int e = -1;
-    if (r < end) {
-      e = P.ids[r];
-      if (e < 0 || e >= E) {
+  // pass 1: per-warp histograms (kSortBatch groups of 32 routes loaded at once: the passes are
+  // latency-bound on these loads)
+  for (int64_t base = beg; base < end; base += 32 * BATCH) {
+    int ev[BATCH];
+#pragma unroll
+    for (int u = 0; u < BATCH; ++u) {
+      const int64_t r = base + 32 * u + lane;
+      ev[u] = r < end ? P.ids[r] : -1;
+    }
+#pragma unroll
+    for (int u = 0; u < BATCH; ++u) {
+      const int64_t r = base + 32 * u + lane;
+      int e = ev[u];
+      if (r < end && (e < 0 || e >= E)) {
         if (!(P.skip_neg && e < 0)) atomicOr(P.status, kStatusBadId);
         e = -1;
       }
+      const unsigned peers = BALLOT ? match_peers(e, nbits) : __match_any_sync(0xffffffffu, e);
+      if (e >= 0 && lane == __ffs(peers) - 1) hist[warp * E + e] += __popc(peers);
     }
-    const unsigned peers = __match_any_sync(0xffffffffu, e);
-    if (e >= 0 && lane == __ffs(peers) - 1) hist[warp * E + e] += __popc(peers);
   }
   __syncthreads();
 
@@ -149,22 +181,27 @@ __device__ void sort_block(const SortParams& P, int* hist /* [32][E] */) {
   __syncthreads();
 
   // pass 2: stable scatter
-  for (int64_t base = beg; base < end; base += 32) {
-    const int64_t r = base + lane;
-    int e = -1;
-    if (r < end) {
-      e = P.ids[r];
-      if (e < 0 || e >= E) e = -1;
+  for (int64_t base = beg; base < end; base += 32 * BATCH) {
+    int ev[BATCH];
+#pragma unroll
+    for (int u = 0; u < BATCH; ++u) {
+      const int64_t r = base + 32 * u + lane;
+      ev[u] = r < end ? P.ids[r] : -1;
     }
-    const unsigned peers = __match_any_sync(0xffffffffu, e);
-    int pos = 0;
-    if (e >= 0) pos = hist[warp * E + e] + __popc(peers & lt_mask);
-    __syncwarp();
-    if (e >= 0) {
-      P.sorted[pos] = (int)r;
-      if (lane == __ffs(peers) - 1) hist[warp * E + e] += __popc(peers);
+#pragma unroll
+    for (int u = 0; u < BATCH; ++u) {
+      const int64_t r = base + 32 * u + lane;
+      const int e = (ev[u] < 0 || ev[u] >= E) ? -1 : ev[u];
+      const unsigned peers = BALLOT ? match_peers(e, nbits) : __match_any_sync(0xffffffffu, e);
+      int pos = 0;
+      if (e >= 0) pos = hist[warp * E + e] + __popc(peers & lt_mask);
+      __syncwarp();
+      if (e >= 0) {
+        P.sorted[pos] = (int)r;
+        if (lane == __ffs(peers) - 1) hist[warp * E + e] += __popc(peers);
+      }
+      __syncwarp();
     }
-    __syncwarp();
   }
   if (P.has_shared && P.sorted)
     for (int64_t t = tid; t < P.Ts; t += kSortThreads) P.sorted[R + t] = (int)(R + t);
@@ -185,8 +222,16 @@ __device__ void sort_block(const SortParams& P, int* hist /* [32][E] */) {
   }
 }
 
-// Stages token t (x16 row t, xscale[t]) from the bf16 row `src`.
-__device__ void stage_token(const SortParams& P, int64_t t, const uint16_t* src) {
+__device__ void sort_block(const SortParams& P, int* hist) {
+  if (P.R >= kBatchedSortRoutes)
+    sort_block_t<kSortBatch, true>(P, hist);
+  else
+    sort_block_t<1, false>(P, hist);
+}
+
+// Stages token t (x16 row t, xscale[t]) from the bf16 row `src` with the whole block (small T:
+// few tokens, each spread over all threads).
+__device__ void stage_token_block(const SortParams& P, int64_t t, const uint16_t* src) {
   __shared__ float sm_max[32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint4* xr = reinterpret_cast<const uint4*>(src);
@@ -237,6 +282,50 @@ __device__ void stage_token(const SortParams& P, int64_t t, const uint16_t* src)
   }
 }
 
+// The same with one warp per token (large T; H % 256 == 0: 16-byte chunks in whole rounds of
+// 32 lanes).
+__device__ void stage_token_warp(const SortParams& P, int64_t t, const uint16_t* src) {
+  const int lane = threadIdx.x & 31;
+  const uint4* xr = reinterpret_cast<const uint4*>(src);
+  const int nv = P.H / 8;
+  float m = 0.f;
+#pragma unroll 4
+  for (int i = lane; i < nv; i += kWarp) {
+    const uint4 v = xr[i];
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      m = fmaxf(m, fabsf(__uint_as_float(w[j] << 16)));
+      m = fmaxf(m, fabsf(__uint_as_float(w[j] & 0xffff0000u)));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  int s = 0;
+  if (m > 0.f && m <= 3.0e38f) {
+    int ex;
+    frexpf(m, &ex);  // m = f * 2^ex, f in [0.5, 1)
+    s = ex - 1 - 14;
+    s = s < -100 ? -100 : (s > 100 ? 100 : s);
+  }
+  const float down = exp2f((float)-s);
+  if (lane == 0) P.xscale[t] = exp2f((float)s);
+  uint4* yr = reinterpret_cast<uint4*>(P.x16 + t * P.H);
+#pragma unroll 4
+  for (int i = lane; i < nv; i += kWarp) {
+    const uint4 v = xr[i];
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const __half2 h = __floats2half2_rn(__uint_as_float(w[j] << 16) * down,
+                                          __uint_as_float(w[j] & 0xffff0000u) * down);
+      o[j] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    yr[P.x_plain ? i : ri_chunk(i)] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 // Expert-parallel front (P.ep.world > 0). Token slots are ordered by rank starting with this
 // one: slot block b (tokens b*tblk .. b*tblk+tblk-1) holds rank (rank + b) % world's tokens,
 // so this rank's own tokens are rows 0..tblk-1 (the shared expert's rows).
@@ -247,23 +336,48 @@ __device__ void stage_token(const SortParams& P, int64_t t, const uint16_t* src)
 //   block 1+t:   stages token slot t from its home rank's published row (a peer load).
 __device__ void ep_front(const SortParams& P, int* hist) {
   const EpLinks& L = P.ep;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t epoch = *L.epoch + 1;
+  if (blockIdx.x != 0 && P.stage_tpb == 1) {  // staging: block 1 + t stages token slot t
+    __shared__ int sm_ok1;
+    const int64_t t = (int64_t)blockIdx.x - 1;
+    const int b = (int)(t / L.tblk);
+    if (threadIdx.x == 0) {
+      ep_signal(L.in_sig, L.world, epoch);
+      const bool ok = ep_wait(L.in_flag + (L.rank + b) % L.world, epoch, L.wait_ns);
+      if (!ok) atomicOr(P.status, kStatusTimeout);
+      sm_ok1 = ok;
+    }
+    __syncthreads();
+    if (sm_ok1) stage_token_block(P, t, L.x[(L.rank + b) % L.world] + (t - b * L.tblk) * P.H);
+    return;
+  }
+  if (blockIdx.x != 0) {  // staging: warp w stages token slot 32 (block - 1) + w
+    const int64_t t = ((int64_t)blockIdx.x - 1) * kSortWarps + warp;
+    if (t >= P.T) return;
+    const int b = (int)(t / L.tblk);
+    int ok = 1;
+    if (lane == 0) {
+      if (threadIdx.x == 0) ep_signal(L.in_sig, L.world, epoch);
+      ok = ep_wait(L.in_flag + (L.rank + b) % L.world, epoch, L.wait_ns);
+      if (!ok) atomicOr(P.status, kStatusTimeout);
+    }
+    if (!__shfl_sync(0xffffffffu, ok, 0)) return;
+    const uint16_t* src = L.x[(L.rank + b) % L.world] + (t - b * L.tblk) * P.H;
+    stage_token_warp(P, t, src);
+    return;
+  }
   __shared__ int sm_ok;
   if (threadIdx.x == 0) {
-    const uint32_t epoch = *L.epoch + 1;
     ep_signal(L.in_sig, L.world, epoch);
     bool ok = true;
-    if (blockIdx.x == 0) {
-      for (int p = 0; p < L.world && ok; ++p) ok = ep_wait(L.in_flag + p, epoch, L.wait_ns);
-    } else {
-      const int b = (int)(((int64_t)blockIdx.x - 1) / L.tblk);
-      ok = ep_wait(L.in_flag + (L.rank + b) % L.world, epoch, L.wait_ns);
-    }
+    for (int p = 0; p < L.world && ok; ++p) ok = ep_wait(L.in_flag + p, epoch, L.wait_ns);
     if (!ok) atomicOr(P.status, kStatusTimeout);
     sm_ok = ok;
   }
   __syncthreads();
   const bool ok = sm_ok != 0;
-  if (blockIdx.x == 0) {
+  {
     const int64_t per_rank = L.tblk * L.top_k;
     const int64_t n = (int64_t)L.world * per_rank;
     for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
@@ -283,11 +397,6 @@ __device__ void ep_front(const SortParams& P, int* hist) {
     }
     __syncthreads();
     sort_block(P, hist);  // P.ids == L.ids_all, P.skip_neg set
-  } else if (ok) {
-    const int64_t t = (int64_t)blockIdx.x - 1;
-    const int b = (int)(t / L.tblk);
-    const uint16_t* src = L.x[(L.rank + b) % L.world] + (t - b * L.tblk) * P.H;
-    stage_token(P, t, src);
   }
 }
 
@@ -299,9 +408,12 @@ __global__ void __launch_bounds__(kSortThreads) k_sort_stage(SortParams P) {
     ep_front(P, hist);
   } else if (blockIdx.x == 0) {
     sort_block(P, hist);
-  } else {
+  } else if (P.stage_tpb == 1) {
     const int64_t t = (int64_t)blockIdx.x - 1;
-    stage_token(P, t, P.x + t * P.H);
+    stage_token_block(P, t, P.x + t * P.H);
+  } else {
+    const int64_t t = ((int64_t)blockIdx.x - 1) * kSortWarps + (threadIdx.x >> 5);
+    if (t < P.T) stage_token_warp(P, t, P.x + t * P.H);
   }
 }
 
@@ -309,14 +421,18 @@ __global__ void __launch_bounds__(kSortThreads) k_sort_stage(SortParams P) {
 
 size_t sort_smem_bytes(int E) { return (size_t)kSortWarps * E * sizeof(int); }
 
-int launch_sort_stage(const SortParams& P, cudaStream_t stream) {
+int launch_sort_stage(const SortParams& P0, cudaStream_t stream) {
+  // up to two tokens per SM: a block per token (all threads on one row, the shortest latency);
+  // beyond, a warp per token (T=4096: 128 staging blocks instead of 4096, no block barriers)
+  SortParams P = P0;
+  P.stage_tpb = P.T <= 2 * (int64_t)sm_count() ? 1 : kSortWarps;
   const size_t smem = sort_smem_bytes(P.E);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(k_sort_stage, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return cuda_status(e);
   }
-  const int64_t blocks = 1 + (P.x16 ? P.T : 0);
+  const int64_t blocks = 1 + (P.x16 ? ceil_div(P.T, (int64_t)P.stage_tpb) : 0);
   prof_mark(FTB_KERNEL_SORT, true, stream);
   const cudaError_t err =
       launch_pdl(k_sort_stage, dim3((unsigned)blocks), dim3(kSortThreads), smem, stream, P);

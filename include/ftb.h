@@ -110,8 +110,8 @@ FTB_API int ftb_moe_align(const int32_t* topk_ids, int64_t T, int top_k, int E, 
  * followed by "out + shared_experts(x)" (patches/models_glm_moe_dsa_moe.patch:203-206)
  * when shared != NULL (one expert, weight 1.0).
  * act_limit: +inf = silu(g)*u; finite L > 0 = swiglu_clamp silu(min(g,L))*clamp(u,+-L).
- * Requires H % 256 == 0, I % 256 == 0 (TMA row strides of the scale banks), 16-byte aligned
- * pointers.
+ * Requires H % 256 == 0, I % 256 == 0 (TMA row strides of the scale banks), 1 <= top_k <= 32,
+ * 16-byte aligned pointers.
  * Workspace: ftb_moe_decode_workspace_bytes() bytes of device memory, 256-byte aligned.
  * Bytes [0, 4) of every workspace hold the device status word, cleared at each call:
  * bit 0 = a top-k id outside [0, E) was skipped (its route contributes 0);

@@ -3,46 +3,50 @@
 // The reference's prefill driver (fused_experts_nvfp4 -> _prefill_nvfp4_moe_kernel,
 // patches/kernel_triton_nvfp4_fused_moe.patch:73-106, patches/moe_fused_nvfp4.patch:153-179)
 // builds each weight tile as e2m1 x scale in bf16 (exact) and runs a dense dot per sorted
-// token block. Here one work item is a 128-row weight tile of one expert against one segment
-// of up to 192 of its routes (the MMA's N), full K:
-//   D[128 x N] (fp32, tensor memory) += A[128 x 64] (dequantised weights, f16, tensor memory)
-//                                      x B[N x 64]^T (the routes' f16 activation rows, smem)
-// with tcgen05.mma kind::f16 (M=128, K=16 per instruction, issued by one thread). B is a
-// K-major tile in the canonical 128-byte-swizzled layout (8-row atoms of 128-byte rows, the
-// 16-byte chunk c of row r stored at chunk c ^ (r & 7)). A lives in tensor memory (lane = row,
-// two f16 per 32-bit column): written there with tcgen05.st it costs no shared-memory
-// bandwidth, which the MMA's B reads and the TMA writes already use up (a first version with
-// A in shared memory measured 3-4x slower, every role stalled on shared memory). e2m1 x e4m3
-// products are exact in f16, so A is the reference's weight tile exactly.
+// token block. Here a work item is a 256-row weight tile of one expert (gate_up: 128 gate rows
+// and the matching 128 up rows) against one segment of up to kPrefillSegRoutes (160) of the
+// expert's routes, full K, computed by a pair of CTAs (a cluster of 2) with
+//   D[256 x N] (fp32, tensor memory) += A[256 x 16] (dequantised weights, f16, tensor memory)
+//                                      x B[N x 16]^T (the routes' f16 activation rows, smem)
+// tcgen05.mma.cta_group::2.kind::f16 (M = 256, K = 16, N = the segment's routes rounded up to
+// 16), issued by one elected lane of the leader CTA's MMA warp. Each CTA holds 128 rows of A
+// in its own tensor memory (lane = row, two f16 per 32-bit column; written with tcgen05.st,
+// so the dequantised weights cost no shared-memory bandwidth), half of B's rows in its own
+// shared memory (K-major, canonical 128-byte swizzle: the 16-byte chunk c of row r stored at
+// chunk c ^ (r & 7)), and D for its 128 rows. e2m1 x e4m3 products are exact in f16, so A is
+// the reference's weight tile exactly; the routes' rows are the f16 staging of x (gate_up)
+// or h (down) with a per-token power-of-2 scale.
 //
-// One persistent CTA per SM, warp roles (items assigned round-robin: CTA b takes items
-// b, b + grid, ...; every role walks the same sequence):
-//   warp 0     TMA producer of the packed weights and scales, 256 k per stage (2D boxes,
-//              the decode GEMV's tensor maps), no multicast;
-//   warp 14    TMA producer of the routes' activation rows, per 64-k block: 2D boxes of
-//              64 rows x 64 k over the rows in sorted order (gate_up: k_permute_rows copies
-//              each route's x row to its sorted position first; down: h is written in sorted
-//              order), no multicast; tile::gather4 straight from the token rows measured 7x
-//              fewer rows per microsecond than these boxes;
-//   warp 1     allocates the 512 tensor-memory columns (two D buffers of up to 192 columns
-//              and four 32-column A tiles) and, on one lane, issues the MMAs and the
-//              tcgen05.commit arrivals;
-//   warps 2-9  dequantise: the two warp groups take alternate 64-k A tiles (so one group's
-//              tensor-memory stores overlap the other's conversions); a thread owns the A row
-//              of its tensor-memory lane, reads 32 packed bytes and 4 scales and stores 64 f16
-//              values (cvt.rn.f16x2.e2m1x2, exact f16x2 scale multiply) with tcgen05.st;
-//   warps 10-13 epilogue: tcgen05.ld of D (each warp reads its 32-lane quarter), then the
-//              decode path's arithmetic: gate_up -> bf16 ic1, SwiGLU -> f16 h (sorted order);
-//              down -> bf16(acc x global x routed weight) per route.
+// One persistent CTA per SM; both CTAs of a pair walk the same item sequence (pair p takes
+// items p, p + pairs, ...). Warp roles per CTA:
+//   warp 0      TMA producer of this CTA's 128 packed weight rows and their scales, 256 k per
+//               stage (gate_up: one 3D box holds the 64 gate and 64 up rows), no multicast;
+//   warp 18     TMA producer of this CTA's half of the segment's activation rows, 128 k per
+//               stage, as one 3D box (both 64-k sub-tiles, up to 80 rows) completing on the
+//               leader's barrier (.cta_group::2 form, no multicast); halves of <= 48 rows
+//               take 16-row 2D boxes. gate_up reads xs, the x16 rows permuted into sorted
+//               order by k_permute_rows; down reads h16, written in sorted order;
+//   warp 1      allocates the 512 tensor-memory columns (cta_group::2: the same columns in
+//               both CTAs; two D buffers of 160 columns and three 128-k A tiles of 64) and, in
+//               the leader, issues the MMAs and the tcgen05.commit arrivals (multicast to both
+//               CTAs' barriers);
+//   warps 2-9   dequantise: warp group g converts the k half g of each packed stage into
+//               registers (cvt.rn.f16x2.e2m1x2, exact f16x2 scale multiply), releases the
+//               packed slot, waits for its A slot and stores it with tcgen05.st;
+//   warps 10-17 epilogue, two warps per tensor-memory lane quarter on alternate 16-column
+//               chunks of D: tcgen05.ld, then the decode path's arithmetic: gate_up -> bf16
+//               ic1, SwiGLU -> f16 h (sorted order); down -> bf16(acc x global x routed
+//               weight) per route.
 // gate_up's A rows pair gate and up rows 16 lanes apart (A row 32q + l = gate row 16q + l,
-// A row 32q + 16 + l = up row 16q + l of the tile, l < 16), so SwiGLU pairs tensor-memory
-// lanes l and l ^ 16 of a warp with one shuffle.
+// A row 32q + 16 + l = up row 16q + l of the CTA's tile, l < 16), so SwiGLU pairs
+// tensor-memory lanes l and l ^ 16 of a warp with one shuffle.
 //
-// Rings, each an mbarrier pair: packed stages (producer -> dequant), A tiles (dequant ->
-// MMA, released by tcgen05.commit), B tiles (producer -> MMA, released by commit), D buffers
-// (MMA -> epilogue). Every wait is bounded; a timeout raises the CTA abort flag and
-// kStatusTimeout, every role stops, the MMA lane waits for its MMAs to finish, the producer
-// for its copies, and the tensor memory is released before the CTA exits.
+// Rings, each an mbarrier pair: packed stages (producer -> dequant, per CTA), A/B stages
+// (dequant + activation producer of both CTAs -> the leader's MMA warp; released by the
+// leader's commit in both CTAs), D buffers (MMA -> both CTAs' epilogues). Every wait is
+// bounded; a timeout raises the CTA abort flag and kStatusTimeout, every role stops, the
+// leader's MMA warp waits for its MMAs to finish, the producers for their copies, and both
+// CTAs meet at a cluster barrier before the tensor memory is released.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 

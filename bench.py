@@ -61,6 +61,11 @@ def parse_args():
                     help="time eager launches instead of CUDA-graph replay")
     ap.add_argument("--ep-transport", choices=["p2p", "nccl"], default="p2p",
                     help="expert-parallel transport for --gpus > 1")
+    ap.add_argument("--stack", type=int, default=0,
+                    help="BASELINE config 4 (--gpus > 1): a step runs this many distinct stacked "
+                         "layers (60 in the config) back to back, --tokens per GPU")
+    ap.add_argument("--routing", choices=["flat", "zipf"], default="flat",
+                    help="config 4 routing: flat N(0,1) logits, or + log Zipf(1.1) popularity")
     return ap.parse_args()
 
 
@@ -224,7 +229,7 @@ def graph_steps(torch, fn, n: int):
     return step
 
 
-def kernel_times(ftb_lib, torch, fn, steps: int):
+def kernel_times(ftb_lib, torch, fn, steps: int, launches_per_step: int = 64):
     """Per-launch durations of the library's kernels over `steps` calls (CUDA events on the
     launching stream, recorded by the library around each launch)."""
     import ctypes
@@ -235,7 +240,7 @@ def kernel_times(ftb_lib, torch, fn, steps: int):
     for i in range(steps):
         fn(i)
     torch.cuda.synchronize()
-    cap = 64 * steps + 64
+    cap = launches_per_step * steps + 64
     ids = (ctypes.c_int32 * cap)()
     ms = (ctypes.c_float * cap)()
     n = lib.ftb_profile_end(ids, ms, cap)
@@ -453,6 +458,13 @@ def bench_prefill(torch, ftb, layers: "Layers", args):
                     "frac_burst": round(ach / burst, 4), "frac_sustained": round(ach / sustained, 4)}
     gemm_ms = sum(statistics.mean(kt[k]) for k in flops)
     ach = sum(flops.values()) / (gemm_ms * 1e-3) / 1e12
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "prefill_gemm_traffic.json")
+    if os.path.exists(tpath) and T == 4096:
+        # ncu DRAM bytes of one gate_up and one down launch at this workload
+        with open(tpath) as f:
+            d = json.load(f)
+        traffic = d["gate_up_dram_bytes_per_launch"] + d["down_dram_bytes_per_launch"]
     hx = [inp.x.cpu().pin_memory() for inp in inps]
     hl = [inp.logits.cpu().pin_memory() for inp in inps]
     hout = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
@@ -486,7 +498,8 @@ def bench_prefill(torch, ftb, layers: "Layers", args):
                      "bound": "tensor", "achieved": round(ach, 1), "peak": burst,
                      "unit": "TFLOP/s", "frac": round(ach / burst, 4),
                      "frac_sustained": round(ach / sustained, 4), "peak_source": src,
-                     "flops_per_step": sum(flops.values()), "per_gemm": gemms},
+                     "flops_per_step": sum(flops.values()), "traffic": traffic,
+                     "per_gemm": gemms},
         "e2e": {"value": round(T / e2e_dt, 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": T * H * 2 + T * E * 4, "d2h_bytes_per_step": T * H * 2},
         "gpu_launches_per_step": 6,  # route_topk, sort, permute, gate_up, down, combine
@@ -684,6 +697,114 @@ def run_ep(args, torch, rank: int, world: int, local: int):
     }
 
 
+def run_ep_stack(args, torch, rank: int, world: int, local: int):
+    """--stack distinct layers of the config 1 shape resident and sharded
+    expert-parallel (experts [r E/W, (r+1) E/W) of every layer on rank r, the shared expert
+    replicated), run back to back in one step over the peer-memory transport, --tokens per
+    GPU, flat or Zipf(1.1)-skewed routing. Each layer takes its own seeded input rows (the
+    layers are timed as a stack; no norm or attention sits between them). value = tokens/s
+    of the whole box through the stack = W T / (max over ranks of the step's device time)."""
+    import datetime
+
+    import torch.distributed as dist
+
+    import ftb
+    from ftb import _lib, synth
+    from ftb.ep import EpGroup, ExpertParallelMoE, shard_range
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    per_gpu_bytes = args.stack * (E // world + 1) * ftb.bank_bytes_per_expert(H, I)
+    free, _ = torch.cuda.mem_get_info(dev)
+    if per_gpu_bytes > 0.8 * free:
+        raise SystemExit(f"config 4 needs {per_gpu_bytes / 1e9:.1f} GB per GPU at {world} GPUs; "
+                         f"{free / 1e9:.1f} GB free")
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    e0, e1 = shard_range(E, rank, world)
+    zipf = 1.1 if args.routing == "zipf" else None
+    group = EpGroup(args.tokens, H, I, E, TOPK, True, rank, world)
+    layers, hits = [], []
+    for l in range(args.stack):
+        # this rank's shard only, drawn directly (the values do not enter the timing)
+        bank = synth.make_bank(e1 - e0, H, I, seed=100000 + 1000 * l + rank, device=dev)
+        shared = synth.make_shared(H, I, seed=200000 + l, device=dev)
+        inp = synth.make_inputs(args.tokens, H, E, seed=3000 + l, stream=rank, device=dev,
+                                zipf_s=zipf)
+        layers.append((ExpertParallelMoE(bank, shared, E, TOPK, rank, world,
+                                         transport="p2p", ep_group=group), inp))
+        ids = torch.cat([ftb.fused_topk(r.x, r.logits, TOPK, True)[1].flatten() for r in
+                         (synth.make_inputs(args.tokens, H, E, seed=3000 + l, stream=q,
+                                            device=dev, zipf_s=zipf) for q in range(world))])
+        hits.append(int(torch.unique(ids[(ids >= e0) & (ids < e1)]).numel()))
+    # busiest rank: max over ranks of the owned experts hit, summed over the stack
+    t_hits = torch.tensor([sum(hits)], dtype=torch.float64, device=dev)
+    dist.all_reduce(t_hits, op=dist.ReduceOp.MAX)
+
+    def stack_step(i):
+        for ep, inp in layers:
+            ep.forward(inp.x, inp.logits)
+
+    for i in range(max(2, min(args.warmup, 3))):
+        stack_step(i)
+    torch.cuda.synchronize()
+    dist.barrier()
+    timed = graph_steps(torch, stack_step, 1) if args.graphs else stack_step
+    for i in range(2):
+        timed(i)
+    torch.cuda.synchronize()
+    dist.barrier()
+    clocks = ClockSampler(torch, local) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    steps = max(3, min(args.steps, 20))
+    ms = time_steps(torch, timed, steps)
+    dist.barrier()
+    clk = clocks.stop() if clocks else None
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    kt = kernel_times(_lib, torch, stack_step, 1, launches_per_step=8 * args.stack)
+    status = group.status()
+    if args.graphs:
+        del timed
+    dist.barrier()
+    group.close()
+    dist.destroy_process_group()
+    if status:
+        raise RuntimeError(f"EP device status word {status:#x} on rank {rank}")
+    if rank != 0:
+        return None
+    peak, peak_src = measured_peaks()
+    # rank 0's weight bytes per step: its owned experts hit plus the shared expert, per layer
+    r0_bytes = sum((h + 1) * ftb.bank_bytes_per_expert(H, I) for h in hits)
+    return {
+        "metric": METRIC, "value": round(world * args.tokens * 1e3 / ms_max, 1),
+        "unit": "tokens/s", "n_gpus": world, "steps": steps, "warmup": 2,
+        "ms_per_step": round(ms_max, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "nvfp4 (e2m1+e4m3) x bf16 -> fp32 accumulate, bf16 out",
+        "data": "synthetic: seeded NVFP4 banks and N(0,1) logits/activations per BASELINE "
+                f"config 4 ({args.routing} routing)",
+        "config": {"workload": f"config 4 stacked MoE: {args.stack} layers of H{H} I{I} E{E} "
+                               f"top{TOPK} +1 shared, T={args.tokens} tokens per GPU per step, "
+                               f"{E // world} experts per GPU per layer, {args.routing} routing",
+                   "routing": args.routing, "layers": args.stack,
+                   "tokens_per_step_per_gpu": args.tokens,
+                   "resident_expert_bytes_per_gpu": per_gpu_bytes,
+                   "resident_expert_bytes_total": args.stack * (E + world) *
+                                                  ftb.bank_bytes_per_expert(H, I),
+                   "owned_experts_hit_rank0": sum(hits),
+                   "owned_experts_hit_busiest_rank": int(t_hits.item()),
+                   "launch": "one CUDA graph per step" if args.graphs else "eager launches",
+                   "timing": "per-rank CUDA events, max over ranks"},
+        "layer_ms": round(ms_max / args.stack, 4),
+        "rank0_weight_gbs": round(r0_bytes / (ms * 1e-3) / 1e9, 1), "peak_gbs": peak,
+        "peak_source": peak_src,
+        "kernels_ms": {k: round(statistics.mean(v), 4) for k, v in kt.items()},
+        "gpu_launches": 6 * args.stack * steps,
+        "clocks": clk,
+    }
+
+
 def main():
     args = parse_args()
     rank, world, local = dist_env()
@@ -693,6 +814,11 @@ def main():
         if rank != 0:
             return 0  # the reference arm runs on rank 0 only
         print(json.dumps(run_reference(args, torch)), flush=True)
+        return 0
+    if world > 1 and args.stack > 0:
+        out = run_ep_stack(args, torch, rank, world, local)
+        if rank == 0:
+            print(json.dumps(out), flush=True)
         return 0
     if world > 1:
         out = run_ep(args, torch, rank, world, local)

@@ -85,8 +85,9 @@ def make_inputs(tokens: int, hidden: int, experts: int, *, seed: int = 0, stream
         return Inputs(x, logits.contiguous(), G.contiguous())
     logits = torch.randn(tokens, experts, device=device, generator=gen)
     if zipf_s is not None:
-        # expert popularity p_e ~ rank_e^-s, ranks from a seeded permutation, added as log p
-        perm = torch.randperm(experts, device=device, generator=gen)
+        # expert popularity p_e ~ rank_e^-s, ranks from a permutation seeded by `seed` alone
+        # (a property of the layer: the same on every stream / rank), added as log p
+        perm = torch.randperm(experts, device=device, generator=_gen(device, seed + 7919))
         ranks = torch.empty(experts, device=device)
         ranks[perm] = torch.arange(1, experts + 1, device=device, dtype=torch.float32)
         logp = -zipf_s * torch.log(ranks)

@@ -145,21 +145,28 @@ int sm_count() {
 }
 
 // The layer, decode GEMVs (prefill == false) or tensor-core grouped GEMMs (prefill == true).
+// route_mask / phase: one phase of the split decode (routes with mask 0 are not computed; the
+// shared expert only with FTB_PHASE_SHARED; the combine only with FTB_PHASE_COMBINE).
 static int layer_impl(bool prefill, const uint16_t* x, const ftb_nvfp4_bank* bank,
                       const ftb_nvfp4_bank* shared, const float* topk_w, const int32_t* topk_ids,
                       int64_t T, int H, int I, int top_k, float act_limit, uint16_t* out,
                       void* workspace, size_t workspace_bytes, uint16_t* dbg_ic1, uint16_t* dbg_h,
                       uint16_t* dbg_ic3, uint16_t* dbg_sic1, uint16_t* dbg_sh,
-                      uint16_t* dbg_sout, cudaStream_t stream) {
+                      uint16_t* dbg_sout, cudaStream_t stream, const int8_t* route_mask = nullptr,
+                      int phase = FTB_PHASE_SHARED | FTB_PHASE_COMBINE) {
   if (T < 0 || H <= 0 || I <= 0 || top_k < 1 || top_k > 32) return FTB_ERR_SHAPE;
   if (H % 256 || I % 256) return FTB_ERR_SHAPE;
   if (!bank_ok(bank) || (shared && !bank_ok(shared))) return FTB_ERR_ARG;
   const int64_t E = bank->num_experts;
   if (E < 1 || E > 1024 || (shared && shared->num_experts < 1)) return FTB_ERR_SHAPE;
+  if (phase & ~(FTB_PHASE_SHARED | FTB_PHASE_COMBINE)) return FTB_ERR_ARG;
+  const bool combine = (phase & FTB_PHASE_COMBINE) != 0;
   if (T == 0) return FTB_OK;
-  if (!x || !topk_w || !topk_ids || !out) return FTB_ERR_ARG;
-  if (!aligned16(x) || !aligned16(out)) return FTB_ERR_ALIGN;
+  if (!x || !topk_w || !topk_ids || (combine && !out)) return FTB_ERR_ARG;
+  if (!aligned16(x) || (out && !aligned16(out))) return FTB_ERR_ALIGN;
   const int has_shared = shared ? 1 : 0;
+  // this call computes the shared expert's rows (the combine adds them whenever shared != 0)
+  const int run_shared = has_shared && (phase & FTB_PHASE_SHARED) ? 1 : 0;
   const int cap = prefill ? kPrefillSegRoutes : kSegRoutes;
   const DecodeWs need = carve_decode(nullptr, T, H, I, E, top_k, has_shared, cap);
   if (!workspace || workspace_bytes < need.bytes) return FTB_ERR_WORKSPACE;
@@ -171,12 +178,13 @@ static int layer_impl(bool prefill, const uint16_t* x, const ftb_nvfp4_bank* ban
   sp.zero_words = w.status;  // status word and the two GEMV work counters
   sp.n_zero = 4;
   sp.ids = topk_ids;
+  sp.route_mask = route_mask;
   sp.R = R;
   sp.T = T;
-  sp.Ts = T;
+  sp.Ts = run_shared ? T : 0;
   sp.E = (int)E;
   sp.top_k = top_k;
-  sp.has_shared = has_shared;
+  sp.has_shared = run_shared;
   sp.seg_cap = cap;
   sp.x_plain = prefill ? 1 : 0;
   sp.block_m = 0;
@@ -226,12 +234,11 @@ static int layer_impl(bool prefill, const uint16_t* x, const ftb_nvfp4_bank* ban
   dp.dbg_sic1 = dbg_sic1;
   dp.dbg_sh = dbg_sh;
   dp.has_shared = has_shared;
-  if (prefill) {
+  if (prefill)
     st = launch_prefill_gemms(dp, stream);
-    if (!st) st = launch_combine(dp, stream);
-  } else {
-    st = launch_decode_gemvs(dp, stream);
-  }
+  else
+    st = launch_decode_gemvs_tma(dp, stream);
+  if (!st && combine) st = launch_combine(dp, stream);
   if (st) return st;
   if (dbg_ic3) {
     st = cuda_status(cudaMemcpyAsync(dbg_ic3, w.ic3, (size_t)R * H * 2, cudaMemcpyDeviceToDevice,
@@ -431,6 +438,17 @@ int ftb_moe_decode_debug(const uint16_t* x, const ftb_nvfp4_bank* bank,
   return layer_impl(false, x, bank, shared, topk_w, topk_ids, T, H, I, top_k, act_limit, out, workspace,
                      workspace_bytes, ic1, h, ic3, shared_ic1, shared_h, shared_out,
                      (cudaStream_t)stream);
+}
+
+int ftb_moe_decode_phase(const uint16_t* x, const ftb_nvfp4_bank* bank,
+                         const ftb_nvfp4_bank* shared, const float* topk_w,
+                         const int32_t* topk_ids, const int8_t* route_mask, int phase,
+                         int64_t T, int H, int I, int top_k, float act_limit, uint16_t* out,
+                         void* workspace, size_t workspace_bytes, ftb_stream_t stream) {
+  if (!route_mask) return FTB_ERR_ARG;
+  return layer_impl(false, x, bank, shared, topk_w, topk_ids, T, H, I, top_k, act_limit, out,
+                    workspace, workspace_bytes, nullptr, nullptr, nullptr, nullptr, nullptr,
+                    nullptr, (cudaStream_t)stream, route_mask, phase);
 }
 
 }  // extern "C"

@@ -60,6 +60,7 @@ struct SortParams {
   int64_t T;
   int64_t Ts;          // shared-expert tokens: rows 0..Ts-1 (Ts <= T)
   int skip_neg;        // negative ids are skipped without setting kStatusBadId
+  const int8_t* route_mask;  // [R] or null: routes with mask 0 are skipped (split decode)
   EpLinks ep;          // ep.world > 0: ids/x are gathered from the group (block 0 / blocks 1..T)
   int E;
   int top_k;

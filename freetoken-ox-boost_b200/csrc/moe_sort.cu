@@ -98,16 +98,21 @@ __device__ void sort_block_t(const SortParams& P, int* hist /* [32][E] */) {
   // latency-bound on these loads)
   for (int64_t base = beg; base < end; base += 32 * BATCH) {
     int ev[BATCH];
+    bool masked[BATCH];
 #pragma unroll
     for (int u = 0; u < BATCH; ++u) {
       const int64_t r = base + 32 * u + lane;
       ev[u] = r < end ? P.ids[r] : -1;
+      // a masked-out route (split decode) is skipped without a status flag
+      masked[u] = P.route_mask && r < end && P.route_mask[r] == 0;
     }
 #pragma unroll
     for (int u = 0; u < BATCH; ++u) {
       const int64_t r = base + 32 * u + lane;
       int e = ev[u];
-      if (r < end && (e < 0 || e >= E)) {
+      if (masked[u]) {
+        e = -1;
+      } else if (r < end && (e < 0 || e >= E)) {
         if (!(P.skip_neg && e < 0)) atomicOr(P.status, kStatusBadId);
         e = -1;
       }
@@ -187,6 +192,7 @@ __device__ void sort_block_t(const SortParams& P, int* hist /* [32][E] */) {
     for (int u = 0; u < BATCH; ++u) {
       const int64_t r = base + 32 * u + lane;
       ev[u] = r < end ? P.ids[r] : -1;
+      if (P.route_mask && r < end && P.route_mask[r] == 0) ev[u] = -1;
     }
 #pragma unroll
     for (int u = 0; u < BATCH; ++u) {

@@ -30,6 +30,8 @@ STATUS_F16_OVERFLOW = 2
 STATUS_TIMEOUT = 4
 
 EP_HANDLE_BYTES = 64
+PHASE_SHARED = 1   # FTB_PHASE_SHARED: this split-decode phase computes the shared expert
+PHASE_COMBINE = 2  # FTB_PHASE_COMBINE: it ends with the combine of every route
 
 # Every symbol include/ftb.h declares, with (restype, argtypes).
 _vp, _i32, _i64, _f32, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
@@ -64,6 +66,8 @@ SIGNATURES = {
     "ftb_moe_decode_debug": (_i32, [_vp, _BP, _BP, _vp, _vp, _i64, _i32, _i32, _i32, _f32, _vp,
                                     _vp, _sz, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "ftb_moe_combine": (_i32, [_vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp]),
+    "ftb_moe_decode_phase": (_i32, [_vp, _BP, _BP, _vp, _vp, _vp, _i32, _i64, _i32, _i32, _i32,
+                                    _f32, _vp, _vp, _sz, _vp]),
     "ftb_moe_prefill_workspace_bytes": (_sz, [_i64, _i32, _i32, _i32, _i32, _i32]),
     "ftb_moe_prefill": (_i32, [_vp, _BP, _BP, _vp, _vp, _i64, _i32, _i32, _i32, _f32, _vp, _vp,
                                _sz, _vp]),

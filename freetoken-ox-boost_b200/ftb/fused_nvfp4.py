@@ -169,6 +169,81 @@ def fused_experts_decode_nvfp4_marlin(
                       act_limit=act_limit, shared=shared)
 
 
+def _phase_masks(miss_mask, R: int, dev):
+    """(hit, miss) int8 masks over the R routes: a (hit, miss) pair of int8 masks as the
+    reference's ensure kernel hands over, or one miss mask (bool or integer, [T, k] or [R])."""
+    if isinstance(miss_mask, tuple):
+        if len(miss_mask) != 2:
+            raise ValueError("miss_mask tuple must be (hit_mask, miss_mask)")
+        masks = [m.reshape(-1) for m in miss_mask]
+    else:
+        mb = miss_mask.reshape(-1)
+        masks = [(mb == 0), (mb != 0)]
+    out = []
+    for m in masks:
+        if m.numel() != R:
+            raise ValueError(f"route masks must have T*top_k = {R} entries, got {m.numel()}")
+        if m.device != dev:
+            raise ValueError("route masks must be on the hidden states' device")
+        out.append(m.to(torch.int8).contiguous())
+    return out
+
+
+def fused_experts_decode_nvfp4_split(
+    hidden_states: torch.Tensor,
+    gate_up_packed: torch.Tensor,
+    gate_up_scale: torch.Tensor,
+    gate_up_global: torch.Tensor,
+    down_packed: torch.Tensor,
+    down_scale: torch.Tensor,
+    down_global: torch.Tensor,
+    topk_weights: torch.Tensor,
+    topk_ids: torch.Tensor,
+    miss_mask,
+    copy_event: torch.cuda.Event | None,
+    activation: str = "silu",
+    apply_router_weight_on_input: bool = False,
+    act_alpha: float = 1.702,
+    act_limit: float = 7.0,
+    *,
+    shared: Nvfp4Bank | None = None,
+) -> torch.Tensor:
+    """Decode MoE in two phases around an in-flight miss copy, as the reference's
+    ``fused_experts_decode_nvfp4_split`` (patches/moe_fused_nvfp4.patch:189-272): phase A
+    computes the routes whose expert was resident (``~miss_mask``), the stream then waits
+    ``copy_event``, phase B computes the missed routes and one combine closes both. The
+    phases write disjoint route rows of the same workspace, so the result is bit-identical
+    to ``fused_experts_decode_nvfp4_marlin``. ``topk_ids`` may be cache-slot ids of a bank of
+    slots (position == slot). The shared expert (keyword, resident) runs in phase A."""
+    del act_alpha
+    if apply_router_weight_on_input:
+        raise NotImplementedError("apply_router_weight_on_input=True is not built")
+    bank = Nvfp4Bank(gate_up_packed, gate_up_scale, gate_up_global, down_packed, down_scale,
+                     down_global)
+    x = hidden_states
+    dev = _check_inputs(x, bank, topk_weights, topk_ids, shared)
+    limit = _act_limit(activation, act_limit)
+    T, H = x.shape
+    K = topk_ids.shape[1]
+    mask_a, mask_b = _phase_masks(miss_mask, T * K, dev)
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    lib = _lib.load()
+    ws = workspace(decode_workspace_bytes(T, bank, K, shared is not None), dev)
+    b = bank.struct()
+    s = shared.struct() if shared is not None else None
+    sp = ctypes.byref(s) if s is not None else None
+    for phase, mask in ((0, mask_a), (1, mask_b)):
+        if phase == 1 and copy_event is not None:
+            torch.cuda.current_stream(dev).wait_event(copy_event)
+        flags = _lib.PHASE_SHARED if phase == 0 else _lib.PHASE_COMBINE
+        st = lib.ftb_moe_decode_phase(ptr(x), ctypes.byref(b), sp, ptr(topk_weights),
+                                      ptr(topk_ids), ptr(mask), flags, T, H, bank.inter, K,
+                                      limit, ptr(out) if phase == 1 else None, ptr(ws),
+                                      ws.numel(), stream_handle(dev))
+        _lib.check("ftb_moe_decode_phase", st)
+    return out
+
+
 def fused_experts_nvfp4(
     hidden_states: torch.Tensor,
     gate_up_packed: torch.Tensor,

@@ -137,13 +137,34 @@ FTB_API int ftb_moe_decode_debug(const uint16_t* x, const ftb_nvfp4_bank* bank,
                          uint16_t* shared_h, uint16_t* shared_out, ftb_stream_t stream);
 
 /*
+ * One phase of the split (hit/miss) decode, replacing fused_experts_decode_nvfp4_split
+ * (patches/moe_fused_nvfp4.patch:189-272) and the GEMV's route_mask
+ * (patches/kernel_triton_nvfp4_fused_moe.patch:25-29): only routes r with route_mask[r] != 0
+ * (int8 [T*top_k]) are computed into the workspace's per-route rows; the other rows are left
+ * as an earlier phase on the same workspace wrote them. FTB_PHASE_SHARED computes the shared
+ * expert in this call; FTB_PHASE_COMBINE then sums every route (k in order) and, when shared
+ * != NULL, the shared expert into out (out may be NULL without it). With complementary masks
+ * over two calls (the second with FTB_PHASE_COMBINE) the output is bit-identical to
+ * ftb_moe_decode(). Same workspace size as ftb_moe_decode; ids may be cache-slot ids of a
+ * bank of slots (the GEMVs index the bank by id).
+ */
+#define FTB_PHASE_SHARED 1
+#define FTB_PHASE_COMBINE 2
+FTB_API int ftb_moe_decode_phase(const uint16_t* x, const ftb_nvfp4_bank* bank,
+                                 const ftb_nvfp4_bank* shared, const float* topk_w,
+                                 const int32_t* topk_ids, const int8_t* route_mask, int phase,
+                                 int64_t T, int H, int I, int top_k, float act_limit,
+                                 uint16_t* out, void* workspace, size_t workspace_bytes,
+                                 ftb_stream_t stream);
+
+/*
  * Prefill (large T) fused MoE on the tensor cores: the same contract and result as
  * ftb_moe_decode(), replacing the prefill driver fused_experts_nvfp4(...)
  * (overlay/freetoken/models/glm5_next/experts_resident.py:69-75; kernel
  * patches/kernel_triton_nvfp4_fused_moe.patch:73-106). Weight tiles are dequantised exactly
- * to f16 and multiplied by tcgen05.mma (kind::f16, fp32 accumulation in tensor memory) against
- * segments of up to 256 routes of one expert. Same shape rules and status word as decode;
- * ftb_moe_prefill_workspace_bytes() bytes of workspace.
+ * to f16 and multiplied by tcgen05.mma (kind::f16, CTA pairs, fp32 accumulation in tensor
+ * memory) against segments of up to 160 routes of one expert. Same shape rules and status word
+ * as decode; ftb_moe_prefill_workspace_bytes() bytes of workspace.
  */
 FTB_API size_t ftb_moe_prefill_workspace_bytes(int64_t T, int H, int I, int E, int top_k,
                                                int has_shared);

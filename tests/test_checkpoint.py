@@ -68,3 +68,19 @@ def test_layer_discovery_and_errors():
     bad[f"{PREFIX}.experts.0.down_proj.weight"] = bad[f"{PREFIX}.experts.0.down_proj.weight"].float()
     with pytest.raises(ValueError):
         checkpoint.bank_from_modelopt(bad.__getitem__, PREFIX, 4)
+
+
+def test_split_phase_masks():
+    # the split decode's mask forms (ftb.fused_nvfp4._phase_masks, host logic only)
+    from ftb.fused_nvfp4 import _phase_masks
+    miss = torch.tensor([[True, False], [False, False], [True, True]])
+    a, b = _phase_masks(miss, 6, torch.device("cpu"))
+    assert a.dtype == torch.int8 and a.tolist() == [0, 1, 1, 1, 0, 0]
+    assert b.tolist() == [1, 0, 0, 0, 1, 1]
+    hit8, miss8 = a.clone(), b.clone()
+    a2, b2 = _phase_masks((hit8, miss8), 6, torch.device("cpu"))
+    assert torch.equal(a2, a) and torch.equal(b2, b)
+    with pytest.raises(ValueError, match="T\\*top_k"):
+        _phase_masks(miss, 8, torch.device("cpu"))
+    with pytest.raises(ValueError):
+        _phase_masks((hit8,), 6, torch.device("cpu"))

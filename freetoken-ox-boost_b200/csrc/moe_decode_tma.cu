@@ -708,8 +708,15 @@ int launch_decode_gemvs_tma(const DecodeParams& P, cudaStream_t stream) {
   const int64_t many = 4 * (int64_t)sm_count();
   int st;
   prof_mark(FTB_KERNEL_GATE_UP, true, stream);
+  // makespan estimate in weight rows per SM: ceil(tiles / SMs) x tile rows
+  auto span = [&](int64_t rows_e, int64_t rt) {
+    return ceil_div(est_seg * (rows_e / rt), (int64_t)sm_count()) * rt;
+  };
   if (est_seg * (2 * P.I / 256) >= many) {
     st = launch_one<kGateUp, 1, 16>(P, max_seg * (2 * P.I / 256), stream);
+  } else if ((2 * P.I) % 96 == 0 && span(2 * P.I, 96) < span(2 * P.I, 128)) {
+    // few tiles (T of a few tokens): 96-row tiles even out the last wave
+    st = launch_one<kGateUp, 1, 6>(P, max_seg * (2 * P.I / 96), stream);
   } else {
     st = launch_one<kGateUp, 1, 8>(P, max_seg * (2 * P.I / 128), stream);
   }

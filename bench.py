@@ -815,7 +815,7 @@ def main():
             return 0  # the reference arm runs on rank 0 only
         print(json.dumps(run_reference(args, torch)), flush=True)
         return 0
-    if world > 1 and args.stack > 0:
+    if args.stack > 0:
         out = run_ep_stack(args, torch, rank, world, local)
         if rank == 0:
             print(json.dumps(out), flush=True)

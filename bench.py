@@ -598,11 +598,14 @@ def run_ep(args, torch, rank: int, world: int, local: int):
     timed = graph_steps(torch, step, len(layers)) if use_graphs else step
     for i in range(max(3, args.warmup)):
         timed(i)
-    torch.cuda.synchronize()
-    dist.barrier()
+    # the sampler starts (NVML set-up, first sample) before the barrier: started after it,
+    # rank 0 would enter the timed loop tens of ms after the others, whose first step then
+    # waits for it and whose timed region absorbs the skew
     clocks = ClockSampler(torch, local) if rank == 0 else None
     if clocks:
         clocks.start()
+    torch.cuda.synchronize()
+    dist.barrier()
     ms = time_steps(torch, timed, args.steps)
     host_ms = time_steps.host_ms
     dist.barrier()
@@ -751,11 +754,11 @@ def run_ep_stack(args, torch, rank: int, world: int, local: int):
     timed = graph_steps(torch, stack_step, 1) if args.graphs else stack_step
     for i in range(2):
         timed(i)
-    torch.cuda.synchronize()
-    dist.barrier()
-    clocks = ClockSampler(torch, local) if rank == 0 else None
+    clocks = ClockSampler(torch, local) if rank == 0 else None  # before the barrier, as above
     if clocks:
         clocks.start()
+    torch.cuda.synchronize()
+    dist.barrier()
     steps = max(3, min(args.steps, 20))
     ms = time_steps(torch, timed, steps)
     dist.barrier()

@@ -165,6 +165,48 @@ def gate_up_bytes_per_expert(h=H, i=I):
     return 2 * i * (h // 2 + h // 16 + 2)
 
 
+def workload_config(args, world: int) -> dict:
+    """The workload this run measures, printed identically by both arms (ftb and reference)."""
+    if world > 1:
+        work = (f"config 3 expert-parallel decode: T={args.tokens} tokens per GPU x {world} GPUs, "
+                f"H{H} I{I} E{E} top{TOPK} +1 shared expert, softmax-renorm router, "
+                f"{E // world} experts per GPU")
+    else:
+        work = (f"config 1 decode T={args.tokens}: H{H} I{I} E{E} top{TOPK} +1 shared expert, "
+                f"softmax-renorm router")
+    return {"workload": work, "tokens_per_step": args.tokens * world, "hidden": H,
+            "inter": I, "experts": E, "top_k": TOPK, "shared_experts": 1,
+            "l2": "inputs larger than L2: distinct 2.7 GB layer banks rotated across steps "
+                  "(GPU arm); the CPU arm streams its banks from DRAM"}
+
+
+def host_cpu() -> dict:
+    """CPU model, logical CPUs usable by this process and physical cores (from /proc/cpuinfo)."""
+    model, cores = None, set()
+    phys = core = None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                k, _, v = line.partition(":")
+                k, v = k.strip(), v.strip()
+                if k == "model name" and model is None:
+                    model = v
+                elif k == "physical id":
+                    phys = v
+                elif k == "core id":
+                    core = v
+                elif not k and phys is not None:
+                    cores.add((phys, core))
+                    phys = core = None
+        if phys is not None:
+            cores.add((phys, core))
+    except OSError:
+        pass
+    logical = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    return {"cpu_model": model, "logical_cpus": logical,
+            "physical_cores": len(cores) or None}
+
+
 class Layers:
     """L distinct synthetic layers on the GPU plus per-layer step inputs."""
 
@@ -302,7 +344,7 @@ def cpu_baseline(torch, layers: "Layers", budget_s: float):
         times.append(time.perf_counter() - t0)
     t = statistics.median(times)
     return {"value": layers.T / t, "unit": "tokens/s", "cores": threads,
-            "kind": "port",
+            "kind": "port", **host_cpu(),
             "sample": f"{len(times)} full T={layers.T} layer steps (config 1 shape, layer 0, "
                       f"{layers.uniq[0]} routed experts + shared), median {t * 1e3:.0f} ms; "
                       f"avx512={cpu_moe.has_avx512()}"}
@@ -364,15 +406,12 @@ def run_ftb_single(args, torch):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "nvfp4 (e2m1+e4m3) x bf16 -> fp32 accumulate, bf16 out",
         "data": "synthetic: seeded NVFP4 banks and N(0,1) logits/activations per BASELINE config 1",
-        "config": {"workload": f"config 1 decode T={args.tokens}: H{H} I{I} E{E} top{TOPK} "
-                               f"+1 shared expert, softmax-renorm router",
-                   "tokens_per_step": args.tokens, "layers_rotated": args.layers,
-                   "l2": f"inputs larger than L2: {args.layers} distinct 2.7 GB layer banks "
-                         "rotated across steps",
-                   "routed_experts_per_step": round(statistics.mean(layers.uniq), 1),
-                   "launch": "CUDA graph per layer (route + layer), replayed" if args.graphs
-                             else "eager launches",
-                   "host_issue_ms_per_step": round(host_ms, 4)},
+        "config": workload_config(args, 1),
+        "run": {"layers_rotated": args.layers,
+                "routed_experts_per_step": round(statistics.mean(layers.uniq), 1),
+                "launch": "CUDA graph per layer (route + layer), replayed" if args.graphs
+                          else "eager launches",
+                "host_issue_ms_per_step": round(host_ms, 4)},
         "layer_hbm_gbs": round(layer_bytes / (ms * 1e-3) / 1e9, 1),
         "roofline": roofline_entry(kt, layers, args.steps),
         "kernels_ms": {k: round(statistics.mean(v), 4) for k, v in kt.items()},
@@ -507,43 +546,50 @@ def bench_prefill(torch, ftb, layers: "Layers", args):
     }
 
 
-def run_reference(args, torch):
+def run_reference(args, torch, world: int = 1):
     """The reference arm: the reference's CPU MoE executor semantics (C++ restatement in
-    oracle/cpu_moe.cpp; the reference's cpu_moe_ext.cpp is absent and unbuildable) on all
-    host threads, same metric/config; each step = one T-token layer sample on layer 0."""
-    import ftb
-    from ftb import synth
-    from oracle import cpu_moe
+    oracle/cpu_moe.cpp; the reference's cpu_moe_ext.cpp is absent and unbuildable) on all host
+    threads, same metric and config; each step = one layer over the whole job's tokens
+    (T per GPU x GPUs). Everything is built on the host: seeded inputs, the oracle's softmax
+    top-k, and NVFP4 banks for the routed experts only (the executor reads nothing else); no
+    GPU and no product code is involved."""
+    import numpy as np
 
-    dev = "cuda" if torch.cuda.is_available() else "cpu"
-    layers = Layers(torch, ftb, synth, 1, args.tokens, None, dev) if dev == "cuda" else None
-    if layers is None:
-        raise RuntimeError("the reference arm generates its banks on the GPU")
-    bank, shared = layers.banks[0].numpy(), layers.shared[0].numpy()
-    x_bits = layers.inputs[0].x.cpu().contiguous().view(torch.int16).numpy().view("uint16")
-    w, ids = layers.routes[0]
-    w, ids = w.cpu().numpy(), ids.cpu().numpy()
+    from ftb import synth  # seeded generator only (pure torch on the CPU)
+    from oracle import cpu_moe
+    from oracle import moe_oracle as m
+
+    T = args.tokens * world
+    inp = synth.make_inputs(T, H, E, seed=1000, device="cpu")
+    w, ids = m.topk_softmax(inp.logits.numpy(), TOPK, True)
+    used = np.unique(ids)
+    remap = np.full(E, -1, np.int32)
+    remap[used] = np.arange(used.size, dtype=np.int32)
+    bank = synth.make_bank(int(used.size), H, I, seed=0, device="cpu").numpy()
+    shared = synth.make_shared(H, I, seed=0, device="cpu").numpy()
+    x_bits = inp.x.contiguous().view(torch.int16).numpy().view("uint16")
+    cids = remap[ids]
     threads = cpu_moe.max_threads()
-    for _ in range(args.warmup):
-        cpu_moe.moe_layer(x_bits, bank, w, ids, shared, nthreads=threads)
+    for _ in range(max(1, args.warmup)):
+        cpu_moe.moe_layer(x_bits, bank, w, cids, shared, nthreads=threads)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        cpu_moe.moe_layer(x_bits, bank, w, ids, shared, nthreads=threads)
+        cpu_moe.moe_layer(x_bits, bank, w, cids, shared, nthreads=threads)
     dt = (time.perf_counter() - t0) / args.steps
-    value = args.tokens / dt
+    value = T / dt
     return {
         "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": "tokens/s",
-        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(dt * 1e3, 2), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "nvfp4 x bf16 -> fp32 (CPU)",
-        "data": "synthetic: seeded NVFP4 banks and N(0,1) logits/activations per BASELINE config 1",
-        "config": {"workload": f"config 1 decode T={args.tokens}: H{H} I{I} E{E} top{TOPK} "
-                               "+1 shared expert, softmax-renorm router",
-                   "tokens_per_step": args.tokens},
+        "data": "synthetic: seeded NVFP4 banks and N(0,1) logits/activations per BASELINE config "
+                f"{3 if world > 1 else 1} (generated on the host)",
+        "config": workload_config(args, world),
         "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": threads,
-                         "kind": "port",
-                         "sample": f"{args.steps} full T={args.tokens} layer steps on layer 0 "
-                                   "(C++ restatement of the reference CPU executor semantics)"},
+                         "kind": "port", **host_cpu(),
+                         "sample": f"{args.steps} full T={T} layer steps ({used.size} routed "
+                                   "experts + shared; C++ restatement of the reference CPU "
+                                   "executor semantics, all host threads)"},
         "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -674,17 +720,13 @@ def run_ep(args, torch, rank: int, world: int, local: int):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "nvfp4 (e2m1+e4m3) x bf16 -> fp32 accumulate, bf16 out",
         "data": "synthetic: seeded NVFP4 banks and N(0,1) logits/activations per BASELINE config 3",
-        "config": {"workload": f"config 3 expert-parallel decode: T={args.tokens} tokens per GPU, "
-                               f"H{H} I{I} E{E} top{TOPK} +1 replicated shared expert, "
-                               f"{E // world} experts per GPU, transport {transport}",
-                   "transport": transport,
-                   "tokens_per_step_per_gpu": args.tokens, "layers_rotated": args.layers,
-                   "owned_experts_hit_per_layer_rank0": hits,
-                   "launch": "CUDA graph per layer (route + layer), replayed" if use_graphs
-                             else "eager launches",
-                   "host_issue_ms_per_step_rank0": round(host_ms, 4),
-                   "l2": f"{args.layers} distinct layer shards rotated across steps",
-                   "timing": "per-rank CUDA events, max over ranks"},
+        "config": workload_config(args, world),
+        "run": {"transport": transport, "layers_rotated": args.layers,
+                "owned_experts_hit_per_layer_rank0": hits,
+                "launch": "CUDA graph per layer (route + layer), replayed" if use_graphs
+                          else "eager launches",
+                "host_issue_ms_per_step_rank0": round(host_ms, 4),
+                "timing": "per-rank CUDA events, max over ranks"},
         "e2e": {"value": round(world * args.tokens / e2e_s, 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": args.tokens * (H * 2 + E * 4),
                 "d2h_bytes_per_step": args.tokens * H * 2,
@@ -816,7 +858,7 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return 0  # the reference arm runs on rank 0 only
-        print(json.dumps(run_reference(args, torch)), flush=True)
+        print(json.dumps(run_reference(args, torch, world)), flush=True)
         return 0
     if args.stack > 0:
         out = run_ep_stack(args, torch, rank, world, local)

@@ -154,11 +154,10 @@ static int layer_impl(bool prefill, const uint16_t* x, const ftb_nvfp4_bank* ban
                       uint16_t* dbg_ic3, uint16_t* dbg_sic1, uint16_t* dbg_sh,
                       uint16_t* dbg_sout, cudaStream_t stream, const int8_t* route_mask = nullptr,
                       int phase = FTB_PHASE_SHARED | FTB_PHASE_COMBINE) {
-  if (T < 0 || H <= 0 || I <= 0 || top_k < 1 || top_k > 32) return FTB_ERR_SHAPE;
-  if (H % 256 || I % 256) return FTB_ERR_SHAPE;
   if (!bank_ok(bank) || (shared && !bank_ok(shared))) return FTB_ERR_ARG;
   const int64_t E = bank->num_experts;
-  if (E < 1 || E > 1024 || (shared && shared->num_experts < 1)) return FTB_ERR_SHAPE;
+  if (layer_shape_status(T, H, I, E, top_k) != FTB_OK || (shared && shared->num_experts < 1))
+    return FTB_ERR_SHAPE;
   if (phase & ~(FTB_PHASE_SHARED | FTB_PHASE_COMBINE)) return FTB_ERR_ARG;
   const bool combine = (phase & FTB_PHASE_COMBINE) != 0;
   if (T == 0) return FTB_OK;
@@ -392,6 +391,17 @@ int ftb_moe_combine(const uint16_t* ic3, const int32_t* topk_ids, const uint16_t
 
 size_t ftb_moe_decode_workspace_bytes(int64_t T, int H, int I, int E, int top_k, int has_shared) {
   return carve_decode(nullptr, T, H, I, E, top_k, has_shared).bytes;
+}
+
+int ftb_moe_decode_plan(int64_t T, int H, int I, int E, int top_k, int has_shared,
+                        int32_t* plan) {
+  if (!plan) return FTB_ERR_ARG;
+  const int st = layer_shape_status(T, H, I, E, top_k);
+  if (st != FTB_OK) return st;
+  const DecodePlan p = decode_tile_plan(T * top_k, E, T, has_shared ? 1 : 0, H, I, sm_count());
+  plan[0] = p.gate_up_rows;
+  plan[1] = p.down_rows;
+  return FTB_OK;
 }
 
 size_t ftb_moe_prefill_workspace_bytes(int64_t T, int H, int I, int E, int top_k,

@@ -80,10 +80,4 @@ int launch_combine(const DecodeParams& P, cudaStream_t stream) {
   return cuda_status(err);
 }
 
-int launch_decode_gemvs(const DecodeParams& P, cudaStream_t stream) {
-  const int st = launch_decode_gemvs_tma(P, stream);
-  if (st) return st;
-  return launch_combine(P, stream);
-}
-
 }  // namespace ftb

@@ -695,39 +695,50 @@ int launch_one(const DecodeParams& P, int64_t est_tiles, cudaStream_t stream) {
 
 }  // namespace
 
-int launch_decode_gemvs_tma(const DecodeParams& P, cudaStream_t stream) {
-  if (P.H % 256 || P.I % 256) return FTB_ERR_SHAPE;
-  const int64_t max_seg = max_segments(P.R, P.E, P.Ts, P.has_shared);
+DecodePlan decode_tile_plan(int64_t R, int64_t E, int64_t Ts, int has_shared, int H, int I,
+                            int sms) {
   // Expected segments: at least one per distinct expert (<= min(R, E)), at least
   // R / kSegRoutes when experts hold more routes than a segment (expert-parallel ranks), plus
   // the shared expert's. 256-row tiles (16 consumer warps) when that still gives every SM
   // several tiles, else 128-row tiles (8 warps) for balance.
-  const int64_t routed_seg = (P.R < P.E ? P.R : P.E) > P.R / kSegRoutes ? (P.R < P.E ? P.R : P.E)
-                                                                          : P.R / kSegRoutes;
-  const int64_t est_seg = routed_seg + (P.has_shared ? (P.Ts + kSegRoutes - 1) / kSegRoutes : 0);
-  const int64_t many = 4 * (int64_t)sm_count();
-  int st;
-  prof_mark(FTB_KERNEL_GATE_UP, true, stream);
+  const int64_t distinct = R < E ? R : E;
+  const int64_t routed_seg = distinct > R / kSegRoutes ? distinct : R / kSegRoutes;
+  const int64_t est_seg = routed_seg + (has_shared ? (Ts + kSegRoutes - 1) / kSegRoutes : 0);
+  const int64_t many = 4 * (int64_t)sms;
   // makespan estimate in weight rows per SM: ceil(tiles / SMs) x tile rows
   auto span = [&](int64_t rows_e, int64_t rt) {
-    return ceil_div(est_seg * (rows_e / rt), (int64_t)sm_count()) * rt;
+    return ceil_div(est_seg * (rows_e / rt), (int64_t)sms) * rt;
   };
-  if (est_seg * (2 * P.I / 256) >= many) {
+  DecodePlan p;
+  if (est_seg * (2 * (int64_t)I / 256) >= many)
+    p.gate_up_rows = 256;
+  else if ((2 * I) % 96 == 0 && span(2 * I, 96) < span(2 * I, 128))
+    p.gate_up_rows = 96;  // few tiles (T of a few tokens): 96-row tiles even out the last wave
+  else
+    p.gate_up_rows = 128;
+  p.down_rows = est_seg * (H / 256) >= many ? 256 : 128;
+  return p;
+}
+
+int launch_decode_gemvs_tma(const DecodeParams& P, cudaStream_t stream) {
+  if (P.H % 256 || P.I % 256) return FTB_ERR_SHAPE;
+  const int64_t max_seg = max_segments(P.R, P.E, P.Ts, P.has_shared);
+  const DecodePlan plan = decode_tile_plan(P.R, P.E, P.Ts, P.has_shared, P.H, P.I, sm_count());
+  int st;
+  prof_mark(FTB_KERNEL_GATE_UP, true, stream);
+  if (plan.gate_up_rows == 256)
     st = launch_one<kGateUp, 1, 16>(P, max_seg * (2 * P.I / 256), stream);
-  } else if ((2 * P.I) % 96 == 0 && span(2 * P.I, 96) < span(2 * P.I, 128)) {
-    // few tiles (T of a few tokens): 96-row tiles even out the last wave
+  else if (plan.gate_up_rows == 96)
     st = launch_one<kGateUp, 1, 6>(P, max_seg * (2 * P.I / 96), stream);
-  } else {
+  else
     st = launch_one<kGateUp, 1, 8>(P, max_seg * (2 * P.I / 128), stream);
-  }
   prof_mark(FTB_KERNEL_GATE_UP, false, stream);
   if (st) return st;
   prof_mark(FTB_KERNEL_DOWN, true, stream);
-  if (est_seg * (P.H / 256) >= many) {
+  if (plan.down_rows == 256)
     st = launch_one<kDown, 1, 16>(P, max_seg * (P.H / 256), stream);
-  } else {
+  else
     st = launch_one<kDown, 1, 8>(P, max_seg * (P.H / 128), stream);
-  }
   prof_mark(FTB_KERNEL_DOWN, false, stream);
   return st;
 }

@@ -174,8 +174,24 @@ inline BankView view_dn(const ftb_nvfp4_bank* b, const ftb_nvfp4_bank* s) {
 }
 
 
-// gate_up+SwiGLU and down GEMVs, then the combine.
-int launch_decode_gemvs(const DecodeParams& P, cudaStream_t stream);
+// Work-tile rows of the decode GEMV launches (gate_up: 96, 128 or 256; down: 128 or 256), a
+// pure function of the call's shape and the device's SM count.
+struct DecodePlan {
+  int gate_up_rows;
+  int down_rows;
+};
+DecodePlan decode_tile_plan(int64_t R, int64_t E, int64_t Ts, int has_shared, int H, int I,
+                            int sms);
+
+// Shape rules shared by the decode and prefill layer entry points (FTB_OK or FTB_ERR_SHAPE).
+inline int layer_shape_status(int64_t T, int H, int I, int64_t E, int top_k) {
+  if (T < 0 || T > (int64_t(1) << 24) || H <= 0 || I <= 0 || top_k < 1 || top_k > 32)
+    return FTB_ERR_SHAPE;
+  if (H % 256 || I % 256 || H > 65536 || I > 65536) return FTB_ERR_SHAPE;
+  if (E < 1 || E > 1024) return FTB_ERR_SHAPE;
+  return FTB_OK;
+}
+
 // TMA-fed pipelined GEMVs (moe_decode_tma.cu).
 int launch_decode_gemvs_tma(const DecodeParams& P, cudaStream_t stream);
 // Tensor-core grouped GEMMs for prefill (moe_prefill.cu): segments of <= kPrefillSegRoutes.

@@ -11,7 +11,7 @@
 //   * the scratch is kNoAllocScratchBytes (16 MiB) per GPU that loads the library, held until
 //     the process exits, whether or not this entry point is used;
 //   * a call whose workspace would exceed it is rejected with FTB_ERR_WORKSPACE (config-1
-//     shape, H=4096 I=1536 E=256 top-8 + shared expert: up to T = 150 tokens);
+//     shape, H=4096 I=1536 E=256 top-8 + shared expert: up to T = 153 tokens);
 //   * the first call on a device looks up the scratch's device address (cudaGetSymbolAddress,
 //     with that device current) and caches it; make that first call before any CUDA-graph
 //     stream capture;
@@ -63,7 +63,10 @@ extern "C" int ftb_moe_decode_noalloc(const uint16_t* x, const ftb_nvfp4_bank* b
                                       int top_k, float act_limit, uint16_t* out,
                                       ftb_stream_t stream) {
   if (!bank) return FTB_ERR_ARG;
-  if (T < 0 || H <= 0 || I <= 0 || top_k < 1) return FTB_ERR_SHAPE;
+  // the layer's own shape rules (top_k <= 32, 1 <= E <= 1024, T <= 2^24, ...) first, so the
+  // workspace size below cannot overflow
+  const int shape = ftb::layer_shape_status(T, H, I, bank->num_experts, top_k);
+  if (shape != FTB_OK) return shape;
   const size_t need = ftb_moe_decode_workspace_bytes(T, H, I, (int)bank->num_experts, top_k,
                                                      shared ? 1 : 0);
   if (need > ftb::kNoAllocScratchBytes) return FTB_ERR_WORKSPACE;

@@ -63,6 +63,7 @@ SIGNATURES = {
     "ftb_moe_decode_workspace_bytes": (_sz, [_i64, _i32, _i32, _i32, _i32, _i32]),
     "ftb_moe_decode": (_i32, [_vp, _BP, _BP, _vp, _vp, _i64, _i32, _i32, _i32, _f32, _vp, _vp,
                               _sz, _vp]),
+    "ftb_moe_decode_plan": (_i32, [_i64, _i32, _i32, _i32, _i32, _i32, _vp]),
     "ftb_moe_decode_debug": (_i32, [_vp, _BP, _BP, _vp, _vp, _i64, _i32, _i32, _i32, _f32, _vp,
                                     _vp, _sz, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "ftb_moe_combine": (_i32, [_vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp]),

@@ -65,6 +65,17 @@ def decode_workspace_bytes(T: int, bank: Nvfp4Bank, top_k: int, has_shared: bool
         T, bank.hidden, bank.inter, bank.num_experts, top_k, 1 if has_shared else 0))
 
 
+def decode_plan(T: int, hidden: int, inter: int, num_experts: int, top_k: int,
+                has_shared: bool) -> tuple[int, int]:
+    """Work-tile rows (gate_up, down) the decode GEMVs use for a call of this shape on the
+    current device (a host-side query; no kernel runs)."""
+    plan = (ctypes.c_int32 * 2)()
+    st = _lib.load().ftb_moe_decode_plan(T, hidden, inter, num_experts, top_k,
+                                         1 if has_shared else 0, plan)
+    _lib.check("ftb_moe_decode_plan", st)
+    return int(plan[0]), int(plan[1])
+
+
 def prefill_workspace_bytes(T: int, bank: Nvfp4Bank, top_k: int, has_shared: bool) -> int:
     return int(_lib.load().ftb_moe_prefill_workspace_bytes(
         T, bank.hidden, bank.inter, bank.num_experts, top_k, 1 if has_shared else 0))

@@ -124,6 +124,16 @@ FTB_API int ftb_moe_decode(const uint16_t* x, const ftb_nvfp4_bank* bank, const 
                    uint16_t* out, void* workspace, size_t workspace_bytes, ftb_stream_t stream);
 
 /*
+ * Host-only query (launches nothing): the work-tile rows the decode GEMVs of a call with this
+ * shape use on the current device, plan[0] = gate_up (96, 128 or 256), plan[1] = down (128 or
+ * 256). Returns FTB_ERR_SHAPE for a shape ftb_moe_decode() rejects. No counterpart in the
+ * reference (its Triton launch configuration is fixed per kernel,
+ * patches/moe_fused_nvfp4.patch:66-82); it lets tests and callers see which tile variant runs.
+ */
+FTB_API int ftb_moe_decode_plan(int64_t T, int H, int I, int E, int top_k, int has_shared,
+                                int32_t* plan);
+
+/*
  * Same layer with its intermediates exposed (parity tests): ic1 bf16 [T, top_k, 2I] (gate_up
  * outputs x global, before the activation), h bf16 [T, top_k, I] (activation), ic3 bf16
  * [T, top_k, H] (down outputs x global x routed weight), and for the shared expert
@@ -199,7 +209,7 @@ FTB_API int ftb_moe_combine(const uint16_t* ic3, const int32_t* topk_ids, const 
  * reference): same arguments and result as ftb_moe_decode() without the workspace, which is
  * taken from a 16 MiB scratch array the library holds in device memory on every GPU that
  * loads it, until the process exits. Larger needs return FTB_ERR_WORKSPACE (config-1 shape
- * with a shared expert: T <= 150). The first call on a device looks the scratch up; make it
+ * with a shared expert: T <= 153). The first call on a device looks the scratch up; make it
  * before any CUDA-graph capture. All calls share the scratch: calls that may overlap on the
  * GPU race and must be serialised by the caller. Allocates nothing.
  */

@@ -5,11 +5,11 @@ arm may import, call or link anything in this package, and only as the checker o
 timed CPU baseline. The product path (``ftb``) never routes through it: the product fails
 loudly when its CUDA library is missing.
 
-Modules:
+Modules (the seeded synthetic generator the tests feed them lives in the product package,
+``ftb.synth``, because bench.py and the tests generate device-side inputs with it):
   moe_oracle   numpy restatement of the reference's op order (per-route NVFP4 GEMV with
                per-word partials, bf16 stage roundings, SwiGLU, routed-weight down GEMV,
                fixed-order combine, shared-expert add), the router, and the permutation.
-  synth        seeded synthetic generator for BASELINE configs 0-4 (host or device).
   cpu_moe      ctypes binding of cpu_moe.cpp, the OpenMP/AVX-512 C++ restatement that is
                both a second oracle and the timed CPU baseline.
 

@@ -2,7 +2,7 @@
 kernels on the CPU (Triton's interpreter, TRITON_INTERPRET=1).
 
 Run here, in the container that has the reference checkout (never on the GPU box):
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py /path/to/reference
 
 Kernels executed (unmodified, imported from the reference tree):
   * ``_fused_route_kernel`` via ``fused_route`` - overlay/freetoken/kernel/triton/fused_route.py
@@ -30,7 +30,9 @@ import triton  # noqa: E402
 import triton.language as tl  # noqa: E402
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("FTB_REFERENCE", "/root/reference")
+if len(sys.argv) < 2:
+    sys.exit("usage: python tests/golden/make_golden.py /path/to/reference-checkout")
+REF = sys.argv[1]
 
 SHIM = '''
 import triton

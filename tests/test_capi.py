@@ -84,3 +84,76 @@ def test_ep_host_checks():
     assert not h.value
     assert lib.ftb_ep_destroy(None) == _lib.FTB_OK
     assert lib.ftb_ep_forward(None, None, None, None, None, None, 0.0, None, None) == _lib.FTB_ERR_ARG
+
+
+def _plan(T, H, I, E, K, shared):
+    import ctypes
+
+    plan = (ctypes.c_int32 * 2)()
+    st = _lib.load().ftb_moe_decode_plan(T, H, I, E, K, 1 if shared else 0, plan)
+    return st, (plan[0], plan[1])
+
+
+def test_smoke_shape_is_accepted_by_the_library():
+    """__graft_entry__.smoke() calls the decode layer at SMOKE_SHAPE: the library's host-side
+    shape rules (the same check ftb_moe_decode applies) must accept it."""
+    import __graft_entry__ as g
+
+    S = g.SMOKE_SHAPE
+    st, plan = _plan(S["T"], S["H"], S["I"], S["E"], S["K"], S["shared"])
+    assert st == _lib.FTB_OK, _lib.status_string(st)
+    assert plan[0] in (96, 128, 256) and plan[1] in (128, 256)
+
+
+@pytest.mark.parametrize("T,want", [(1, (96, 128)), (4, (128, 128)), (16, (256, 256)),
+                                    (64, (256, 256))])
+def test_decode_plan_config1(T, want):
+    """Tile rows of the config-1 decode (H4096 I1536 E256 top-8 + shared) on 148 SMs: the
+    GPU parity tests at these T assert the same plan, so each launched variant is tested."""
+    st, plan = _plan(T, 4096, 1536, 256, 8, True)
+    assert st == _lib.FTB_OK and plan == want
+
+
+def test_decode_plan_config0_t1_uses_96_row_tiles():
+    st, plan = _plan(1, 2048, 768, 64, 8, False)
+    assert st == _lib.FTB_OK and plan == (96, 128)
+
+
+def test_decode_plan_rejects_what_decode_rejects():
+    assert _plan(4, 256, 128, 8, 2, True)[0] == _lib.FTB_ERR_SHAPE
+    assert _plan(4, 256, 256, 8, 33, True)[0] == _lib.FTB_ERR_SHAPE
+    assert _plan(4, 256, 256, 2048, 8, True)[0] == _lib.FTB_ERR_SHAPE
+
+
+# Largest config-1 token count (with a shared expert) whose decode workspace fits the
+# allocation-free entry point's 16 MiB scratch.
+NOALLOC_MAX_T_CONFIG1 = 153
+
+
+def test_noalloc_scratch_limit_host_only():
+    """The allocation-free decode uses a 16 MiB static scratch: at the config-1 shape with a
+    shared expert it fits up to NOALLOC_MAX_T_CONFIG1 tokens (the figure include/ftb.h states)
+    and not one more; bigger calls, and shapes the layer rejects, are refused on the host
+    before any device call."""
+    import ctypes
+
+    lib = _lib.load()
+    limit = 16 << 20
+    fits = [T for T in range(1, 400)
+            if lib.ftb_moe_decode_workspace_bytes(T, 4096, 1536, 256, 8, 1) <= limit]
+    assert max(fits) == NOALLOC_MAX_T_CONFIG1
+    header = open(os.path.join(ROOT, "include", "ftb.h")).read()
+    assert f"T <= {NOALLOC_MAX_T_CONFIG1})" in header
+    b = _lib.Nvfp4BankStruct(16, 16, 16, 16, 16, 16, 256)
+    inf = float("inf")
+    sh = _lib.Nvfp4BankStruct(16, 16, 16, 16, 16, 16, 1)
+    assert lib.ftb_moe_decode_noalloc(None, ctypes.byref(b), ctypes.byref(sh), None, None,
+                                      NOALLOC_MAX_T_CONFIG1 + 1, 4096, 1536, 8, inf, None,
+                                      None) == _lib.FTB_ERR_WORKSPACE
+    assert lib.ftb_moe_decode_noalloc(None, ctypes.byref(b), None, None, None, 4, 4096, 1536,
+                                      33, inf, None, None) == _lib.FTB_ERR_SHAPE
+    assert lib.ftb_moe_decode_noalloc(None, ctypes.byref(b), None, None, None, 1 << 40, 4096,
+                                      1536, 8, inf, None, None) == _lib.FTB_ERR_SHAPE
+    big = _lib.Nvfp4BankStruct(16, 16, 16, 16, 16, 16, 4096)
+    assert lib.ftb_moe_decode_noalloc(None, ctypes.byref(big), None, None, None, 4, 4096, 1536,
+                                      8, inf, None, None) == _lib.FTB_ERR_SHAPE

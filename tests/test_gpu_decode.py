@@ -65,6 +65,24 @@ def test_decode_cfg0_full_router_gemv():
     assert m.max_abs_rel(to_f32(out), f64) <= TOL
 
 
+def test_decode_cfg0_t1_96_row_tiles():
+    """Config 0 at T=1 (8 routes of 64 experts, 2I = 1536): the gate_up GEMV runs its 96-row
+    work tiles (k_gemv_tma<0,1,6>); every intermediate against the oracle."""
+    from ftb.fused_nvfp4 import decode_plan
+
+    assert decode_plan(1, 2048, 768, 64, 8, False) == (96, 128)
+    case = build_case(64, 2048, 768, 1, 8, seed=5, shared=False)
+    ref = oracle_layer(case)
+    out, it = run_gpu(case)
+    torch.cuda.synchronize()
+    assert it["status"] == 0
+    for key in ("ic1", "h", "ic3"):
+        rel, _ = compare(to_f32(it[key]), ref[key])
+        assert rel <= TOL, (key, rel)
+    rel, frac = compare(to_f32(out), ref["out"])
+    assert rel <= TOL and frac < 0.05, (rel, frac)
+
+
 def test_decode_swiglu_clamp():
     case = build_case(8, 256, 256, 5, 2, seed=7)
     ref = oracle_layer(case, limit=0.75)

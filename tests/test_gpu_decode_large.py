@@ -1,7 +1,8 @@
 """GPU parity at the BASELINE config-1 shape (H=4096, I=1536, 256 experts, top-8, shared
-expert) and T in {16, 64}: the sizes at which the decode GEMVs use their 256-row work tiles
-and segments with both one and two n-tiles of routes (the small-shape tests run the
-128-row tiles).
+expert) at every config-1 token count, T in {1, 4, 16, 64}. Each T asserts the decode GEMVs'
+work-tile plan, so every tile variant the library can launch at this shape is checked here:
+96-row gate_up tiles at T=1, 128-row tiles at T=4, 256-row tiles at T=16 and 64, with segments
+of one and of two n-tiles of routes at T=64.
 
 The reference here is a torch fp32 restatement, on the GPU, of the CPU oracle's arithmetic
 (oracle/moe_oracle.py expert_forward / moe_layer: exact NVFP4 dequantisation, fp32 dot
@@ -82,8 +83,15 @@ def layer():
     return bank, shared
 
 
-@pytest.mark.parametrize("T", [16, 64])
+PLANS = {1: (96, 128), 4: (128, 128), 16: (256, 256), 64: (256, 256)}
+
+
+@pytest.mark.parametrize("T", [1, 4, 16, 64])
 def test_config1_decode_matches_fp32_restatement(layer, T):
+    from ftb.fused_nvfp4 import decode_plan
+
+    if torch.cuda.get_device_properties(0).multi_processor_count == 148:
+        assert decode_plan(T, H, I, E, K, True) == PLANS[T]
     bank, shared = layer
     inp = synth.make_inputs(T, H, E, seed=300 + T, device=DEV)
     logits = inp.logits.clone()

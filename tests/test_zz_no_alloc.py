@@ -1,11 +1,16 @@
-"""ftb_moe_decode_noalloc: the decode layer for callers that cannot allocate device memory
-(a runtime that owns every allocation, an FFI host without a device allocator, a process that
-must not allocate after start-up). It takes its workspace from the library's own fixed
-device scratch array instead of a caller buffer. This file is collected last on purpose.
+"""ftb_moe_decode_noalloc: the decode layer for callers that cannot allocate device memory.
 
-The entry point is called through the C ABI on two calls in a row (different batch sizes,
-so the second call runs on the first call's leftover scratch) and must match the existing
-workspace entry point, ftb_moe_decode, within the parity tolerance used by the other tests.
+Who needs it: code that runs inside a runtime owning every device allocation (a serving
+engine's caching allocator that this call site cannot reach), a foreign-language host (Go,
+Java, Rust over FFI) with no device-allocator binding, or a process that must not allocate
+after start-up (allocation can fail, fragment memory or synchronise the device). Such callers
+cannot pass the workspace ftb_moe_decode() asks for, so this entry point takes it from the
+library's own fixed device scratch array.
+
+The test calls it through the C ABI on two calls in a row (different shapes, so the second
+call runs on the first call's leftover scratch) and requires outputs bit-identical to the
+workspace entry point, ftb_moe_decode, which runs the same kernels on the same inputs. This
+file is collected last on purpose; it passes alone in a fresh process and after the others.
 """
 import ctypes
 
@@ -14,10 +19,9 @@ import torch
 
 import ftb
 from ftb import _lib
-from tests.moe_cases import build_case, compare, to_f32
+from tests.moe_cases import build_case
 
 pytestmark = pytest.mark.gpu
-TOL = 1e-2
 DEV = "cuda:0"
 
 
@@ -44,12 +48,11 @@ def _noalloc(case, limit=float("inf")):
 
 
 def test_noalloc_matches_workspace_entry_point_twice():
-    first = build_case(8, 256, 256, 17, 2, seed=41)
-    second = build_case(8, 256, 256, 3, 2, seed=42)
-    for case in (first, second):
+    cases = [build_case(8, 256, 256, 17, 2, seed=41),         # shared expert, 128-row tiles
+             build_case(64, 2048, 768, 1, 8, seed=42, shared=False)]  # config 0, 96-row tiles
+    for case in cases:
         out, ref = _noalloc(case)
-        rel, _ = compare(to_f32(out), to_f32(ref))
-        assert rel <= TOL, rel
+        assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
 
 
 def test_noalloc_rejects_sizes_beyond_its_scratch():

@@ -10,7 +10,7 @@ namespace ftb {
 
 int launch_route_topk(const float* logits, int64_t T, int E, int top_k, int mode,
                       const float* bias, float scaling, int renorm, float* w, int32_t* ids,
-                      cudaStream_t stream);
+                      int n_rank, int32_t* rank_ids, float* rank_sc, cudaStream_t stream);
 int launch_router_gemv(const uint16_t* x, const float* G, int64_t T, int H, int E, float* logits,
                        cudaStream_t stream);
 
@@ -18,7 +18,10 @@ namespace {
 thread_local char g_last_error[256] = "";
 
 struct DecodeWs {
-  int32_t* status;
+  int32_t* status;  // kCtlWords control words, then hshift [Rs] (one block, cleared per call)
+  int32_t* hshift;
+  int32_t* hlist;
+  uint16_t* hb;
   __half* x16;
   float* xscale;
   int32_t* offsets;
@@ -41,7 +44,10 @@ DecodeWs carve_decode(void* ws, int64_t T, int H, int I, int64_t E, int top_k, i
   const int64_t Rs = R + (has_shared ? T : 0);
   Carver c(ws);
   DecodeWs w;
-  w.status = c.take<int32_t>(4);  // [0] status, [1..2] GEMV work counters
+  w.status = c.take<int32_t>(kCtlWords + Rs);  // control words (kCtl*), then hshift
+  w.hshift = w.status ? w.status + kCtlWords : nullptr;
+  w.hlist = c.take<int32_t>(Rs);
+  w.hb = c.take<uint16_t>(Rs * I);
   w.x16 = c.take<__half>(T * H);
   w.xscale = c.take<float>(T);
   w.offsets = c.take<int32_t>(E + 1);
@@ -144,40 +150,46 @@ int sm_count() {
   return cache[dev];
 }
 
-// The layer, decode GEMVs (prefill == false) or tensor-core grouped GEMMs (prefill == true).
+// The layer, decode GEMVs (FTB_PATH_DECODE) or tensor-core grouped GEMMs (FTB_PATH_PREFILL).
 // route_mask / phase: one phase of the split decode (routes with mask 0 are not computed; the
 // shared expert only with FTB_PHASE_SHARED; the combine only with FTB_PHASE_COMBINE).
-static int layer_impl(bool prefill, const uint16_t* x, const ftb_nvfp4_bank* bank,
-                      const ftb_nvfp4_bank* shared, const float* topk_w, const int32_t* topk_ids,
-                      int64_t T, int H, int I, int top_k, float act_limit, uint16_t* out,
-                      void* workspace, size_t workspace_bytes, uint16_t* dbg_ic1, uint16_t* dbg_h,
-                      uint16_t* dbg_ic3, uint16_t* dbg_sic1, uint16_t* dbg_sh,
-                      uint16_t* dbg_sout, cudaStream_t stream, const int8_t* route_mask = nullptr,
-                      int phase = FTB_PHASE_SHARED | FTB_PHASE_COMBINE) {
+static int layer_impl(const ftb_moe_args& a, cudaStream_t stream) {
+  const bool prefill = a.path == FTB_PATH_PREFILL;
+  if (a.path != FTB_PATH_DECODE && a.path != FTB_PATH_PREFILL) return FTB_ERR_ARG;
+  if (a.activation != FTB_ACT_SILU && a.activation != FTB_ACT_SWIGLU_CLAMP &&
+      a.activation != FTB_ACT_SWIGLUOAI)
+    return FTB_ERR_ARG;
+  if (prefill && a.route_mask) return FTB_ERR_ARG;  // the split decode runs the GEMVs only
+  const ftb_nvfp4_bank* bank = a.bank;
+  const ftb_nvfp4_bank* shared = a.shared;
   if (!bank_ok(bank) || (shared && !bank_ok(shared))) return FTB_ERR_ARG;
+  const int64_t T = a.T;
+  const int H = a.H, I = a.I, top_k = a.top_k;
   const int64_t E = bank->num_experts;
   if (layer_shape_status(T, H, I, E, top_k) != FTB_OK || (shared && shared->num_experts < 1))
     return FTB_ERR_SHAPE;
+  const int phase = a.route_mask ? a.phase : (FTB_PHASE_SHARED | FTB_PHASE_COMBINE);
   if (phase & ~(FTB_PHASE_SHARED | FTB_PHASE_COMBINE)) return FTB_ERR_ARG;
   const bool combine = (phase & FTB_PHASE_COMBINE) != 0;
   if (T == 0) return FTB_OK;
-  if (!x || !topk_w || !topk_ids || (combine && !out)) return FTB_ERR_ARG;
-  if (!aligned16(x) || (out && !aligned16(out))) return FTB_ERR_ALIGN;
+  if (!a.x || !a.topk_w || !a.topk_ids || (combine && !a.out)) return FTB_ERR_ARG;
+  if (!aligned16(a.x) || (a.out && !aligned16(a.out))) return FTB_ERR_ALIGN;
   const int has_shared = shared ? 1 : 0;
   // this call computes the shared expert's rows (the combine adds them whenever shared != 0)
   const int run_shared = has_shared && (phase & FTB_PHASE_SHARED) ? 1 : 0;
   const int cap = prefill ? kPrefillSegRoutes : kSegRoutes;
   const DecodeWs need = carve_decode(nullptr, T, H, I, E, top_k, has_shared, cap);
-  if (!workspace || workspace_bytes < need.bytes) return FTB_ERR_WORKSPACE;
-  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return FTB_ERR_ALIGN;
-  const DecodeWs w = carve_decode(workspace, T, H, I, E, top_k, has_shared, cap);
+  if (!a.workspace || a.workspace_bytes < need.bytes) return FTB_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(a.workspace) & 255u) != 0) return FTB_ERR_ALIGN;
+  const DecodeWs w = carve_decode(a.workspace, T, H, I, E, top_k, has_shared, cap);
   const int64_t R = T * top_k;
+  const int64_t Rs = R + (has_shared ? T : 0);
 
   SortParams sp{};
-  sp.zero_words = w.status;  // status word and the two GEMV work counters
-  sp.n_zero = 4;
-  sp.ids = topk_ids;
-  sp.route_mask = route_mask;
+  sp.zero_words = w.status;  // control words and the per-row h shifts
+  sp.n_zero = kCtlWords + Rs;
+  sp.ids = a.topk_ids;
+  sp.route_mask = a.route_mask;
   sp.R = R;
   sp.T = T;
   sp.Ts = run_shared ? T : 0;
@@ -194,7 +206,7 @@ static int layer_impl(bool prefill, const uint16_t* x, const ftb_nvfp4_bank* ban
   sp.seg_cnt = w.seg_cnt;
   sp.n_seg = w.n_seg;
   sp.status = w.status;
-  sp.x = x;
+  sp.x = a.x;
   sp.x16 = w.x16;
   sp.xscale = w.xscale;
   sp.H = H;
@@ -211,9 +223,10 @@ static int layer_impl(bool prefill, const uint16_t* x, const ftb_nvfp4_bank* ban
   dp.T = T;
   dp.R = R;
   dp.Ts = T;
-  dp.limit = act_limit;
-  dp.topk_w = topk_w;
-  dp.topk_ids = topk_ids;
+  dp.act = ActSpec{a.activation, a.act_alpha, a.act_limit};
+  dp.w_on_input = a.weight_on_input ? 1 : 0;
+  dp.topk_w = a.topk_w;
+  dp.topk_ids = a.topk_ids;
   dp.sorted = w.sorted;
   dp.seg_expert = w.seg_expert;
   dp.seg_off = w.seg_off;
@@ -225,13 +238,18 @@ static int layer_impl(bool prefill, const uint16_t* x, const ftb_nvfp4_bank* ban
   dp.h16 = w.h16;
   dp.ic3 = w.ic3;
   dp.ic3s = w.ic3s;
-  dp.out = out;
+  dp.out = a.out;
   dp.status = w.status;
-  dp.work_counter = w.status + 1;
-  dp.dbg_ic1 = dbg_ic1;
-  dp.dbg_h = dbg_h;
-  dp.dbg_sic1 = dbg_sic1;
-  dp.dbg_sh = dbg_sh;
+  dp.work_counter = w.status + kCtlWorkGu;
+  dp.hshift = w.hshift;
+  dp.hlist = w.hlist;
+  dp.hcount = w.status + kCtlHCount;
+  dp.gu_done = w.status + kCtlGuDone;
+  dp.hb = w.hb;
+  dp.dbg_ic1 = a.ic1;
+  dp.dbg_h = a.h;
+  dp.dbg_sic1 = a.shared_ic1;
+  dp.dbg_sh = a.shared_h;
   dp.has_shared = has_shared;
   if (prefill)
     st = launch_prefill_gemms(dp, stream);
@@ -239,17 +257,45 @@ static int layer_impl(bool prefill, const uint16_t* x, const ftb_nvfp4_bank* ban
     st = launch_decode_gemvs_tma(dp, stream);
   if (!st && combine) st = launch_combine(dp, stream);
   if (st) return st;
-  if (dbg_ic3) {
-    st = cuda_status(cudaMemcpyAsync(dbg_ic3, w.ic3, (size_t)R * H * 2, cudaMemcpyDeviceToDevice,
+  if (a.ic3) {
+    st = cuda_status(cudaMemcpyAsync(a.ic3, w.ic3, (size_t)R * H * 2, cudaMemcpyDeviceToDevice,
                                      stream));
     if (st) return st;
   }
-  if (dbg_sout && has_shared) {
-    st = cuda_status(cudaMemcpyAsync(dbg_sout, w.ic3s, (size_t)T * H * 2,
+  if (a.shared_out && has_shared) {
+    st = cuda_status(cudaMemcpyAsync(a.shared_out, w.ic3s, (size_t)T * H * 2,
                                      cudaMemcpyDeviceToDevice, stream));
     if (st) return st;
   }
+  (void)Rs;
   return FTB_OK;
+}
+
+// The older entry points' argument lists as an ftb_moe_args.
+static ftb_moe_args legacy_args(int path, const uint16_t* x, const ftb_nvfp4_bank* bank,
+                                const ftb_nvfp4_bank* shared, const float* topk_w,
+                                const int32_t* topk_ids, int64_t T, int H, int I, int top_k,
+                                float act_limit, uint16_t* out, void* workspace,
+                                size_t workspace_bytes) {
+  ftb_moe_args a{};
+  const ActSpec act = act_from_limit(act_limit);
+  a.x = x;
+  a.bank = bank;
+  a.shared = shared;
+  a.topk_w = topk_w;
+  a.topk_ids = topk_ids;
+  a.T = T;
+  a.H = H;
+  a.I = I;
+  a.top_k = top_k;
+  a.activation = act.kind;
+  a.act_alpha = act.alpha;
+  a.act_limit = act.limit;
+  a.path = path;
+  a.out = out;
+  a.workspace = workspace;
+  a.workspace_bytes = workspace_bytes;
+  return a;
 }
 
 }  // namespace ftb
@@ -311,11 +357,24 @@ int ftb_route_topk(const float* logits, int64_t T, int E, int top_k, int mode, c
                    float scaling, int renorm, float* topk_w, int32_t* topk_ids,
                    ftb_stream_t stream) {
   if (T < 0 || E < 1 || E > 1024 || top_k < 1 || top_k > 32 || top_k > E) return FTB_ERR_SHAPE;
-  if (mode != FTB_ROUTE_SOFTMAX && mode != FTB_ROUTE_SIGMOID) return FTB_ERR_ARG;
+  if (mode != FTB_ROUTE_SOFTMAX && mode != FTB_ROUTE_SIGMOID && mode != FTB_ROUTE_SQRTSOFTPLUS)
+    return FTB_ERR_ARG;
   if (T == 0) return FTB_OK;
   if (!logits || !topk_w || !topk_ids) return FTB_ERR_ARG;
   return launch_route_topk(logits, T, E, top_k, mode, bias, scaling, renorm, topk_w, topk_ids,
-                           (cudaStream_t)stream);
+                           0, nullptr, nullptr, (cudaStream_t)stream);
+}
+
+int ftb_route_ranked(const float* logits, int64_t T, int E, int top_k, int n_rank,
+                     const float* bias, float scaling, int renorm, float* topk_w,
+                     int32_t* topk_ids, int32_t* rank_ids, float* rank_scores,
+                     ftb_stream_t stream) {
+  if (T < 0 || E < 1 || E > 1024 || top_k < 1 || top_k > 32 || top_k > E) return FTB_ERR_SHAPE;
+  if (n_rank < top_k || n_rank > E) return FTB_ERR_SHAPE;
+  if (T == 0) return FTB_OK;
+  if (!logits || !topk_w || !topk_ids || !rank_ids || !rank_scores) return FTB_ERR_ARG;
+  return launch_route_topk(logits, T, E, top_k, FTB_ROUTE_SIGMOID, bias, scaling, renorm, topk_w,
+                           topk_ids, n_rank, rank_ids, rank_scores, (cudaStream_t)stream);
 }
 
 int ftb_router_gemv(const uint16_t* x, const float* gate_w, int64_t T, int H, int E,
@@ -409,13 +468,18 @@ size_t ftb_moe_prefill_workspace_bytes(int64_t T, int H, int I, int E, int top_k
   return carve_decode(nullptr, T, H, I, E, top_k, has_shared, kPrefillSegRoutes).bytes;
 }
 
+int ftb_moe_layer(const ftb_moe_args* args, ftb_stream_t stream) {
+  if (!args) return FTB_ERR_ARG;
+  return layer_impl(*args, (cudaStream_t)stream);
+}
+
 int ftb_moe_prefill(const uint16_t* x, const ftb_nvfp4_bank* bank, const ftb_nvfp4_bank* shared,
                     const float* topk_w, const int32_t* topk_ids, int64_t T, int H, int I,
                     int top_k, float act_limit, uint16_t* out, void* workspace,
                     size_t workspace_bytes, ftb_stream_t stream) {
-  return layer_impl(true, x, bank, shared, topk_w, topk_ids, T, H, I, top_k, act_limit, out,
-                    workspace, workspace_bytes, nullptr, nullptr, nullptr, nullptr, nullptr,
-                    nullptr, (cudaStream_t)stream);
+  const ftb_moe_args a = legacy_args(FTB_PATH_PREFILL, x, bank, shared, topk_w, topk_ids, T, H,
+                                     I, top_k, act_limit, out, workspace, workspace_bytes);
+  return layer_impl(a, (cudaStream_t)stream);
 }
 
 int ftb_moe_prefill_debug(const uint16_t* x, const ftb_nvfp4_bank* bank,
@@ -425,18 +489,24 @@ int ftb_moe_prefill_debug(const uint16_t* x, const ftb_nvfp4_bank* bank,
                           size_t workspace_bytes, uint16_t* ic1, uint16_t* h, uint16_t* ic3,
                           uint16_t* shared_ic1, uint16_t* shared_h, uint16_t* shared_out,
                           ftb_stream_t stream) {
-  return layer_impl(true, x, bank, shared, topk_w, topk_ids, T, H, I, top_k, act_limit, out,
-                    workspace, workspace_bytes, ic1, h, ic3, shared_ic1, shared_h, shared_out,
-                    (cudaStream_t)stream);
+  ftb_moe_args a = legacy_args(FTB_PATH_PREFILL, x, bank, shared, topk_w, topk_ids, T, H, I,
+                               top_k, act_limit, out, workspace, workspace_bytes);
+  a.ic1 = ic1;
+  a.h = h;
+  a.ic3 = ic3;
+  a.shared_ic1 = shared_ic1;
+  a.shared_h = shared_h;
+  a.shared_out = shared_out;
+  return layer_impl(a, (cudaStream_t)stream);
 }
 
 int ftb_moe_decode(const uint16_t* x, const ftb_nvfp4_bank* bank, const ftb_nvfp4_bank* shared,
                    const float* topk_w, const int32_t* topk_ids, int64_t T, int H, int I,
                    int top_k, float act_limit, uint16_t* out, void* workspace,
                    size_t workspace_bytes, ftb_stream_t stream) {
-  return layer_impl(false, x, bank, shared, topk_w, topk_ids, T, H, I, top_k, act_limit, out, workspace,
-                     workspace_bytes, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
-                     (cudaStream_t)stream);
+  const ftb_moe_args a = legacy_args(FTB_PATH_DECODE, x, bank, shared, topk_w, topk_ids, T, H,
+                                     I, top_k, act_limit, out, workspace, workspace_bytes);
+  return layer_impl(a, (cudaStream_t)stream);
 }
 
 int ftb_moe_decode_debug(const uint16_t* x, const ftb_nvfp4_bank* bank,
@@ -445,9 +515,15 @@ int ftb_moe_decode_debug(const uint16_t* x, const ftb_nvfp4_bank* bank,
                          float act_limit, uint16_t* out, void* workspace, size_t workspace_bytes,
                          uint16_t* ic1, uint16_t* h, uint16_t* ic3, uint16_t* shared_ic1,
                          uint16_t* shared_h, uint16_t* shared_out, ftb_stream_t stream) {
-  return layer_impl(false, x, bank, shared, topk_w, topk_ids, T, H, I, top_k, act_limit, out, workspace,
-                     workspace_bytes, ic1, h, ic3, shared_ic1, shared_h, shared_out,
-                     (cudaStream_t)stream);
+  ftb_moe_args a = legacy_args(FTB_PATH_DECODE, x, bank, shared, topk_w, topk_ids, T, H, I,
+                               top_k, act_limit, out, workspace, workspace_bytes);
+  a.ic1 = ic1;
+  a.h = h;
+  a.ic3 = ic3;
+  a.shared_ic1 = shared_ic1;
+  a.shared_h = shared_h;
+  a.shared_out = shared_out;
+  return layer_impl(a, (cudaStream_t)stream);
 }
 
 int ftb_moe_decode_phase(const uint16_t* x, const ftb_nvfp4_bank* bank,
@@ -456,9 +532,11 @@ int ftb_moe_decode_phase(const uint16_t* x, const ftb_nvfp4_bank* bank,
                          int64_t T, int H, int I, int top_k, float act_limit, uint16_t* out,
                          void* workspace, size_t workspace_bytes, ftb_stream_t stream) {
   if (!route_mask) return FTB_ERR_ARG;
-  return layer_impl(false, x, bank, shared, topk_w, topk_ids, T, H, I, top_k, act_limit, out,
-                    workspace, workspace_bytes, nullptr, nullptr, nullptr, nullptr, nullptr,
-                    nullptr, (cudaStream_t)stream, route_mask, phase);
+  ftb_moe_args a = legacy_args(FTB_PATH_DECODE, x, bank, shared, topk_w, topk_ids, T, H, I,
+                               top_k, act_limit, out, workspace, workspace_bytes);
+  a.route_mask = route_mask;
+  a.phase = phase;
+  return layer_impl(a, (cudaStream_t)stream);
 }
 
 }  // extern "C"

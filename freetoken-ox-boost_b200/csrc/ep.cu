@@ -77,7 +77,10 @@ EpRegion carve_region(void* base, int W, int64_t T, int H, int K) {
 }
 
 struct EpWs {
-  int32_t* status;  // [0] status word (sticky), [1] [2] GEMV work counters, [3] combine blocks
+  int32_t* status;  // kCtlWords control words ([0] status word, sticky), then hshift [Ra + T]
+  int32_t* hshift;
+  int32_t* hlist;
+  uint16_t* hb;
   uint32_t* epoch;
   int32_t* ids_all;
   float* w_all;
@@ -98,7 +101,10 @@ EpWs carve_ws(void* base, const ftb_ep& g) {
   const int64_t Ta = (int64_t)g.world * g.T, Ra = Ta * g.K;
   Carver c(base);
   EpWs w;
-  w.status = c.take<int32_t>(4);
+  w.status = c.take<int32_t>(kCtlWords + Ra + g.T);
+  w.hshift = w.status ? w.status + kCtlWords : nullptr;
+  w.hlist = c.take<int32_t>(Ra + g.T);
+  w.hb = c.take<uint16_t>((Ra + g.T) * g.I);
   w.epoch = c.take<uint32_t>(1);
   w.ids_all = c.take<int32_t>(Ra);
   w.w_all = c.take<float>(Ra);
@@ -126,7 +132,8 @@ struct PublishParams {
   int32_t* rids;
   int64_t nx;  // 16-byte vectors of x
   int64_t nr;  // routes
-  int32_t* counters;  // [3] zeroed
+  int32_t* ctl;       // control words: all but the sticky status word are zeroed, and the
+  int64_t n_hshift;   // n_hshift per-row h shifts that follow them
 };
 
 __global__ void __launch_bounds__(256) k_ep_publish(const PublishParams P) {
@@ -139,7 +146,7 @@ __global__ void __launch_bounds__(256) k_ep_publish(const PublishParams P) {
     P.rw[i] = P.w[i];
     P.rids[i] = P.ids[i];
   }
-  if (i0 < 3) P.counters[i0] = 0;
+  for (int64_t i = i0 + 1; i < kCtlWords + P.n_hshift; i += stride) P.ctl[i] = 0;
 }
 
 struct CombineParams {
@@ -246,7 +253,7 @@ EpLinks make_links(const ftb_ep& g, const EpWs& w) {
   L.in_flag = own.in_flag;
   L.done_flag = own.done_flag;
   L.epoch = w.epoch;
-  L.done_blocks = w.status + 3;
+  L.done_blocks = w.status + kCtlEpBlocks;
   L.ids_all = w.ids_all;
   L.w_all = w.w_all;
   L.wait_ns = g.wait_ns;
@@ -355,10 +362,13 @@ int ftb_ep_set_wait_ns(ftb_ep* g, int64_t ns) {
   return FTB_OK;
 }
 
-int ftb_ep_forward(ftb_ep* g, const uint16_t* x, const float* topk_w, const int32_t* topk_ids,
-                   const ftb_nvfp4_bank* local_bank, const ftb_nvfp4_bank* shared,
-                   float act_limit, uint16_t* out, ftb_stream_t stream) {
+static int ep_forward_impl(ftb_ep* g, const uint16_t* x, const float* topk_w,
+                           const int32_t* topk_ids, const ftb_nvfp4_bank* local_bank,
+                           const ftb_nvfp4_bank* shared, ActSpec act, int w_on_input,
+                           uint16_t* out, ftb_stream_t stream) {
   if (!g || !g->opened) return FTB_ERR_ARG;
+  if (act.kind != kActSilu && act.kind != kActSwigluClamp && act.kind != kActSwigluOai)
+    return FTB_ERR_ARG;
   if (!x || !topk_w || !topk_ids || !out) return FTB_ERR_ARG;
   if (!bank_ok(local_bank) || local_bank->num_experts != g->per) return FTB_ERR_ARG;
   if ((shared != nullptr) != (g->has_shared != 0) || (shared && !bank_ok(shared)))
@@ -374,7 +384,7 @@ int ftb_ep_forward(ftb_ep* g, const uint16_t* x, const float* topk_w, const int3
 
   PublishParams pp{reinterpret_cast<const uint4*>(x), topk_w, topk_ids,
                    reinterpret_cast<uint4*>(own.x), own.w, own.ids, g->T * g->H / 8,
-                   g->T * g->K, w.status + 1};
+                   g->T * g->K, w.status, Ra + g->T};
   int64_t gp = ceil_div(pp.nx, 256);
   if (gp > sm_count()) gp = sm_count();
   prof_mark(FTB_KERNEL_EP_PUBLISH, true, s);
@@ -418,7 +428,8 @@ int ftb_ep_forward(ftb_ep* g, const uint16_t* x, const float* topk_w, const int3
   dp.T = Ta;
   dp.R = Ra;
   dp.Ts = g->T;
-  dp.limit = act_limit;
+  dp.act = act;
+  dp.w_on_input = w_on_input ? 1 : 0;
   dp.topk_w = w.w_all;
   dp.topk_ids = w.ids_all;
   dp.sorted = w.sorted;
@@ -433,7 +444,12 @@ int ftb_ep_forward(ftb_ep* g, const uint16_t* x, const float* topk_w, const int3
   dp.ic3s = w.ic3s;
   dp.out = nullptr;
   dp.status = w.status;
-  dp.work_counter = w.status + 1;
+  dp.work_counter = w.status + kCtlWorkGu;
+  dp.hshift = w.hshift;
+  dp.hlist = w.hlist;
+  dp.hcount = w.status + kCtlHCount;
+  dp.gu_done = w.status + kCtlGuDone;
+  dp.hb = w.hb;
   dp.has_shared = g->has_shared;
   st = launch_decode_gemvs_tma(dp, s);
   if (st) return st;
@@ -450,6 +466,22 @@ int ftb_ep_forward(ftb_ep* g, const uint16_t* x, const float* topk_w, const int3
   st = cuda_status(launch_pdl(k_ep_combine, dim3((unsigned)gc), dim3(256), 0, s, cp));
   prof_mark(FTB_KERNEL_EP_COMBINE, false, s);
   return st;
+}
+
+int ftb_ep_forward(ftb_ep* g, const uint16_t* x, const float* topk_w, const int32_t* topk_ids,
+                   const ftb_nvfp4_bank* local_bank, const ftb_nvfp4_bank* shared,
+                   float act_limit, uint16_t* out, ftb_stream_t stream) {
+  return ep_forward_impl(g, x, topk_w, topk_ids, local_bank, shared, act_from_limit(act_limit),
+                         0, out, stream);
+}
+
+int ftb_ep_forward_act(ftb_ep* g, const uint16_t* x, const float* topk_w,
+                       const int32_t* topk_ids, const ftb_nvfp4_bank* local_bank,
+                       const ftb_nvfp4_bank* shared, int activation, float act_alpha,
+                       float act_limit, int weight_on_input, uint16_t* out,
+                       ftb_stream_t stream) {
+  return ep_forward_impl(g, x, topk_w, topk_ids, local_bank, shared,
+                         ActSpec{activation, act_alpha, act_limit}, weight_on_input, out, stream);
 }
 
 int ftb_ep_status(ftb_ep* g, int clear, ftb_stream_t stream) {

@@ -178,14 +178,34 @@ __device__ __forceinline__ void named_bar(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
-// SwiGLU of the reference: bf16((g * sigmoid(g)) * u), clamps when limit > 0.
-__device__ __forceinline__ float swiglu_f32(float g, float u, float limit) {
-  if (limit > 0.f) {
-    g = fminf(g, limit);
-    u = fminf(fmaxf(u, -limit), limit);
+// Activations between the two GEMVs (the reference's _run_act, patches/moe_fused_nvfp4.patch:
+// 12-22), before the one bf16 rounding:
+//   kActSilu         (g * sigmoid(g)) * u
+//   kActSwigluClamp  g = min(g, L), u = clamp(u, -L, L), then as silu
+//                    (kernel_triton_dsv4_fused_moe.patch:22-36)
+//   kActSwigluOai    g = min(g, L), u = clamp(u, -L, L), (g * sigmoid(alpha * g)) * (u + 1)
+//                    (swigluoai_and_mul(gate_up, out, alpha, limit), the GPT-OSS gated unit)
+enum { kActSilu = 0, kActSwigluClamp = 1, kActSwigluOai = 2 };
+struct ActSpec {
+  int kind;
+  float alpha;
+  float limit;
+};
+
+template <bool FAST>
+__device__ __forceinline__ float sigmoid_f32(float v) {
+  if (FAST) return __frcp_rn(1.0f + __expf(-v));
+  return 1.0f / (1.0f + expf(-v));
+}
+
+template <bool FAST = false>
+__device__ __forceinline__ float act_f32(float g, float u, const ActSpec& a) {
+  if (a.kind != kActSilu) {
+    g = fminf(g, a.limit);
+    u = fminf(fmaxf(u, -a.limit), a.limit);
   }
-  const float sg = 1.0f / (1.0f + expf(-g));
-  return (g * sg) * u;
+  if (a.kind == kActSwigluOai) return (g * sigmoid_f32<FAST>(a.alpha * g)) * (u + 1.0f);
+  return (g * sigmoid_f32<FAST>(g)) * u;
 }
 
 }  // namespace ftb

@@ -316,6 +316,7 @@ template <int MT, int NT>
 struct EpiPre {
   int r[NT][2];
   float f[NT][2];
+  float w[NT][2];  // gate_up with the routed weight on the input: the weight, else 1
   float g0[MT], g1[MT];
 };
 
@@ -336,14 +337,20 @@ __device__ __forceinline__ void epi_prefetch(const DecodeParams& P, EpiPre<MT, N
 #pragma unroll
     for (int jj = 0; jj < 2; ++jj) {
       const int r = q.r[nt][jj];
-      float f = 1.f;
+      float f = 1.f, wr = 1.f;
       if (r >= 0) {
-        if (MODE == kGateUp)
+        if (MODE == kGateUp) {
           f = P.xscale[sh ? (int64_t)r - P.R : (int64_t)r / P.top_k];
-        else if (!sh)
-          f = P.topk_w[r];
+          if (P.w_on_input && !sh) wr = P.topk_w[r];
+        } else {
+          // routed weight (unless it went on the input) times the row's h shift 2^c: scaling
+          // by a power of two commutes with the rounding, so (acc g) (w 2^c) == ((acc 2^c) g) w
+          if (!sh && !P.w_on_input) f = P.topk_w[r];
+          f *= pow2i(P.hshift[off + nt * 8 + 2 * tig + jj]);
+        }
       }
       q.f[nt][jj] = f;
+      q.w[nt][jj] = wr;
     }
 #pragma unroll
   for (int m = 0; m < MT; ++m) {
@@ -382,11 +389,16 @@ __device__ void epi_gate_up(const DecodeParams& P, const float (&acc)[MT][NT][4]
         if (r < 0) continue;
         const int j = nt * 8 + 2 * tig + jj;
         const float xs = q.f[nt][jj];
-        const float gv = bf16_round((acc[m][nt][jj] * xs) * q.g0[m]);
-        const float uv = bf16_round((acc[m][nt][2 + jj] * xs) * q.g1[m]);
-        const float hv = bf16_round(swiglu_f32(gv, uv, P.limit));
-        if (fabsf(hv) > 65504.f) atomicOr(P.status, kStatusF16Overflow);
-        P.h16[(int64_t)(off + j) * I + hp] = __float2half_rn(hv);
+        float gv = (acc[m][nt][jj] * xs) * q.g0[m];
+        float uv = (acc[m][nt][2 + jj] * xs) * q.g1[m];
+        if (P.w_on_input) {
+          gv *= q.w[nt][jj];
+          uv *= q.w[nt][jj];
+        }
+        gv = bf16_round(gv);
+        uv = bf16_round(uv);
+        const float hv = bf16_round(act_f32(gv, uv, P.act));
+        store_h(P, off + j, hp, hv);
         if (sh) {
           const int64_t t = (int64_t)r - P.R;
           if (P.dbg_sic1) {
@@ -422,15 +434,11 @@ __device__ void epi_down(const DecodeParams& P, const float (&acc)[MT][NT][4],
       for (int jj = 0; jj < 2; ++jj) {
         const int r = q.r[nt][jj];
         if (r < 0) continue;
-        if (sh) {
-          const int64_t t = (int64_t)r - P.R;
-          P.ic3s[t * H + na] = f32_to_bf16_bits(acc[m][nt][jj] * q.g0[m]);
-          P.ic3s[t * H + nb] = f32_to_bf16_bits(acc[m][nt][2 + jj] * q.g1[m]);
-        } else {
-          const float wr = q.f[nt][jj];
-          P.ic3[(int64_t)r * H + na] = f32_to_bf16_bits((acc[m][nt][jj] * q.g0[m]) * wr);
-          P.ic3[(int64_t)r * H + nb] = f32_to_bf16_bits((acc[m][nt][2 + jj] * q.g1[m]) * wr);
-        }
+        // f = routed weight x 2^hshift (shared expert: 2^hshift); x 1.0 is exact
+        const float f = q.f[nt][jj];
+        uint16_t* dst = sh ? P.ic3s + ((int64_t)r - P.R) * H : P.ic3 + (int64_t)r * H;
+        dst[na] = f32_to_bf16_bits((acc[m][nt][jj] * q.g0[m]) * f);
+        dst[nb] = f32_to_bf16_bits((acc[m][nt][2 + jj] * q.g1[m]) * f);
       }
     }
   }
@@ -478,6 +486,7 @@ __global__ void __launch_bounds__((NW + 1) * kWarp, 1)
   uint64_t* empty = full + kMaxStages;
   int64_t* tile_of = reinterpret_cast<int64_t*>(empty + kMaxStages);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tile_of + kMaxStages);
+  volatile int* last_flag = abort_flag + 1;
   uint8_t* stages = smem + kHeader;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   pdl_launch_dependents();
@@ -518,6 +527,8 @@ __global__ void __launch_bounds__((NW + 1) * kWarp, 1)
       i = warp_tile<MODE, MT, NW, 1>(P, L, stages, sy, i, nk, K, warp, lane, p, e, off, cnt);
     if (i < 0) break;
   }
+  // every consumer warp gets here (aborts break out of the loop too)
+  if (MODE == kGateUp) finish_gate_up(P, 1, NW * kWarp, threadIdx.x, last_flag);
 }
 
 // ---------------------------------------------------------------------------------------

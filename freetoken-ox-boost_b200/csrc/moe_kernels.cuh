@@ -7,8 +7,19 @@ namespace ftb {
 
 // Bits of the device status word (workspace), OR-ed by kernels.
 constexpr int kStatusBadId = 1;         // a top-k id outside [0, E): route skipped
-constexpr int kStatusF16Overflow = 2;   // |activation| >= 65504 met on the f16 MMA operand
+constexpr int kStatusF16Overflow = 2;   // reserved: no longer raised (rows of h beyond the f16
+                                        // range are rescaled, see store_h)
 constexpr int kStatusTimeout = 4;       // a bounded device-side wait gave up
+
+// Control words at the start of a layer workspace (int32), cleared per call together with the
+// per-row h shifts that follow them.
+constexpr int kCtlStatus = 0;      // device status word
+constexpr int kCtlWorkGu = 1;      // gate_up GEMV tile counter
+constexpr int kCtlWorkDn = 2;      // down GEMV tile counter
+constexpr int kCtlEpBlocks = 3;    // expert-parallel combine: finished blocks
+constexpr int kCtlGuDone = 4;      // gate_up CTAs finished (last-CTA detection)
+constexpr int kCtlHCount = 5;      // rows of h rescaled by this call
+constexpr int kCtlWords = 8;
 
 // Work segments hold at most this many routes of one expert (one pass of two mma n-tiles);
 // an expert with more routes is split into several segments.
@@ -85,8 +96,8 @@ struct SortParams {
   int32_t* padded_off;  // [E] scratch
   int32_t* padded_cnt;  // [E] scratch
   int32_t* status;
-  int32_t* zero_words;  // [n_zero] cleared by block 0 before any other use (status, counters)
-  int n_zero;
+  int32_t* zero_words;  // [n_zero] cleared by block 0 before any other use (control words,
+  int64_t n_zero;       // counters and the per-row h shifts)
   // activation staging (x16 == null: no staging blocks)
   const uint16_t* x;    // [T, H] bf16
   __half* x16;          // [T, H]
@@ -112,7 +123,8 @@ struct DecodeParams {
   int H, I, E, top_k;
   int64_t T, R;
   int64_t Ts;              // shared-expert tokens (rows 0..Ts-1 of x16)
-  float limit;
+  ActSpec act;             // activation between the GEMVs
+  int w_on_input;          // apply_router_weight_on_input: the routed weight scales ic1, not ic3
   const float* topk_w;     // [R]
   const int32_t* topk_ids; // [R]
   // sort results
@@ -132,6 +144,12 @@ struct DecodeParams {
   uint16_t* out;           // [T, H]
   int32_t* status;
   int* work_counter;       // [2] tile-chunk counters of the gate_up / down launches, zeroed
+  // h beyond the f16 range: row sp of h16 holds h * 2^-hshift[sp] (hshift 0 = unscaled)
+  int32_t* hshift;         // [R + Ts] per sorted row, zeroed per call
+  int32_t* hlist;          // [R + Ts] sorted rows whose hshift is set
+  int32_t* hcount;         // entries of hlist (zeroed per call)
+  int32_t* gu_done;        // gate_up CTAs finished (zeroed per call)
+  uint16_t* hb;            // [R + Ts, I] bf16 h of the elements beyond the f16 range
   // optional debug copies (route order)
   uint16_t* dbg_ic1;       // [R, 2I]
   uint16_t* dbg_h;         // [R, I]
@@ -140,7 +158,71 @@ struct DecodeParams {
   int has_shared;
 };
 
+// ---------------------------------------------------------------------------------------
+// h beyond the f16 range. The down GEMV's activation operand is f16 (the tensor cores take one
+// type for both operands, and the dequantised weights are f16), while the reference keeps h
+// in bf16. An element whose bf16 value is beyond the f16 range (|h| >= 65520) is kept exactly
+// in hb and its row is marked with the shift c that brings the whole row below 2^15; the last
+// gate_up CTA to finish rewrites the marked rows as f16(h * 2^-c), and the down GEMV multiplies
+// those rows' accumulators by 2^c (exact: powers of two). Rows within range are untouched.
+// ---------------------------------------------------------------------------------------
+
+// Stores h (a bf16 value held in fp32) at element pos of sorted row sp.
+__device__ __forceinline__ void store_h(const DecodeParams& P, int64_t sp, int64_t pos, float hv) {
+  const __half h = __float2half_rn(hv);
+  const int64_t idx = sp * P.I + pos;
+  if ((__half_as_ushort(h) & 0x7FFFu) == 0x7C00u) {  // f16 infinity: beyond range, or +-inf
+    P.hb[idx] = f32_to_bf16_bits(hv);
+    if (isfinite(hv)) {
+      const int ex = (int)((__float_as_uint(hv) >> 23) & 0xFFu) - 126;  // |hv| < 2^ex
+      if (atomicMax(P.hshift + sp, ex - 15) == 0) P.hlist[atomicAdd(P.hcount, 1)] = (int)sp;
+    }
+  }
+  P.h16[idx] = h;
+}
+
+// 2^c for an integer c in [-126, 127].
+__device__ __forceinline__ float pow2i(int c) { return __uint_as_float((uint32_t)(127 + c) << 23); }
+
+// Run by the nthr threads (whole warps, tid = 0..nthr-1, named barrier bar_id) of a gate_up CTA
+// that wrote h, after their last tile: the last CTA of the launch to get here rewrites the
+// marked rows. Every CTA of the launch must call it once.
+__device__ __forceinline__ void finish_gate_up(const DecodeParams& P, int bar_id, int nthr,
+                                               int tid, volatile int* sm_last) {
+  named_bar(bar_id, nthr);
+  if (tid == 0) {
+    __threadfence();  // this CTA's h, hb, hshift and hlist writes before its arrival
+    const int done = atomicAdd(P.gu_done, 1);
+    const int last = done == (int)(gridDim.x * gridDim.y * gridDim.z) - 1;
+    if (last) __threadfence();
+    *sm_last = last;
+  }
+  named_bar(bar_id, nthr);
+  if (!*sm_last) return;
+  const int n = *reinterpret_cast<volatile int*>(P.hcount);
+  const int lane = tid & 31;
+  for (int i = tid >> 5; i < n; i += nthr >> 5) {
+    const int64_t sp = __ldcg(P.hlist + i);
+    const float f = pow2i(-__ldcg(P.hshift + sp));
+    __half* row = P.h16 + sp * P.I;
+    const uint16_t* brow = P.hb + sp * P.I;
+    for (int k = lane; k < P.I; k += 32) {
+      const unsigned short u = __ldcg(reinterpret_cast<const unsigned short*>(row + k));
+      const float v = (u & 0x7FFFu) == 0x7C00u ? bf16_bits_to_f32(__ldcg(brow + k))
+                                               : __half2float(__ushort_as_half(u));
+      row[k] = __float2half_rn(v * f);
+    }
+  }
+}
+
 // ---- host helpers shared by the entry points ----
+
+// Activation of the entry points that take only act_limit: +inf (or <= 0) = silu, finite
+// L > 0 = swiglu_clamp with limit L.
+inline ActSpec act_from_limit(float act_limit) {
+  const bool clamp = act_limit > 0.f && act_limit < INFINITY;
+  return ActSpec{clamp ? kActSwigluClamp : kActSilu, 1.f, act_limit};
+}
 
 // Carves 256-byte aligned sub-buffers out of a workspace.
 struct Carver {

@@ -128,6 +128,7 @@ struct PfShared {
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
+  int last;  // gate_up: this CTA is the launch's last to finish its epilogue
   // epilogue warp w (0..3): route id and factor of each column of its current item
   int col_r[kEpiWarps][kPrefillSegRoutes];
   float col_f[kEpiWarps][kPrefillSegRoutes];
@@ -293,14 +294,6 @@ __device__ __forceinline__ void tc_fence_after() {
 // SwiGLU for the prefill epilogue, which evaluates it for every (row, route): the hardware
 // exp2-based exponential and a correctly rounded reciprocal instead of expf and a division.
 // The result is rounded to bf16 right after, like the decode path's.
-__device__ __forceinline__ float swiglu_fast(float g, float u, float limit) {
-  if (limit > 0.f) {
-    g = fminf(g, limit);
-    u = fminf(fmaxf(u, -limit), limit);
-  }
-  const float sg = __frcp_rn(1.0f + __expf(-g));
-  return (g * sg) * u;
-}
 
 struct Item {
   int e, off, cnt, mt, n;  // expert (E = shared), segment start/size, weight tile, MMA N
@@ -586,16 +579,21 @@ __device__ __forceinline__ void meta_routes(const DecodeParams& P, const Item& i
 }
 
 template <int MODE>
-__device__ __forceinline__ void meta_factors(const DecodeParams& P, const Item& im, Meta& m) {
+__device__ __forceinline__ void meta_factors(const DecodeParams& P, const Item& im, int lane,
+                                             Meta& m) {
 #pragma unroll
   for (int k = 0; k < kMetaK; ++k) {
     const int r = m.r[k];
     float f = 1.f;
     if (r >= 0) {
-      if (MODE == kGateUp)
+      if (MODE == kGateUp) {
         f = P.xscale[im.sh ? (int64_t)r - P.R : (int64_t)r / P.top_k];
-      else if (!im.sh)
-        f = P.topk_w[r];
+      } else {
+        // routed weight (unless it went on the input) times the row's h shift 2^c (a power of
+        // two commutes with the rounding: (acc g) (w 2^c) == ((acc 2^c) g) w)
+        if (!im.sh && !P.w_on_input) f = P.topk_w[r];
+        f *= pow2i(P.hshift[im.off + lane + kWarp * k]);
+      }
     }
     m.f[k] = f;
   }
@@ -638,7 +636,7 @@ __device__ void pf_epilogue(const DecodeParams& P, const PfSync& sy, int64_t n_i
   if (it < n_items) {
     im = item_of<MODE>(P, it, mpairs, sy.rank);
     meta_routes(P, im, lane, nx);
-    meta_factors<MODE>(P, im, nx);
+    meta_factors<MODE>(P, im, lane, nx);
   }
   for (; it < n_items; it += gridDim.x / kPair) {
 #pragma unroll
@@ -657,7 +655,7 @@ __device__ void pf_epilogue(const DecodeParams& P, const PfSync& sy, int64_t n_i
     const int buf = (int)(di & 1);
     if (!sy.wait(&sh->full_d[buf], (uint32_t)(di / 2) & 1u)) return;
     tc_fence_after();
-    if (has_next) meta_factors<MODE>(P, im2, nx);
+    if (has_next) meta_factors<MODE>(P, im2, lane, nx);
     const uint32_t taddr = tbase + (uint32_t)(buf * kPrefillSegRoutes);
     if (MODE == kGateUp) {
       const int I = P.I;
@@ -684,11 +682,17 @@ __device__ void pf_epilogue(const DecodeParams& P, const PfSync& sy, int64_t n_i
           const int r = col_r[n];
           if (r < 0) continue;
           const float xs = col_f[n];
-          const float gv = bf16_round((g * xs) * glg);
-          const float uv = bf16_round((u * xs) * glu);
-          const float hv = bf16_round(swiglu_fast(gv, uv, P.limit));
-          if (fabsf(hv) > 65504.f) atomicOr(P.status, kStatusF16Overflow);
-          P.h16[(int64_t)(im.off + n) * I + j] = __float2half_rn(hv);
+          float gv = (g * xs) * glg;
+          float uv = (u * xs) * glu;
+          if (P.w_on_input && !im.sh) {  // the routed weight goes on ic1 (rare mode)
+            const float wr = P.topk_w[r];
+            gv *= wr;
+            uv *= wr;
+          }
+          gv = bf16_round(gv);
+          uv = bf16_round(uv);
+          const float hv = bf16_round(act_f32<true>(gv, uv, P.act));
+          store_h(P, im.off + n, j, hv);
           if (dbg) {
             if (im.sh) {
               const int64_t tok = (int64_t)r - P.R;
@@ -722,8 +726,8 @@ __device__ void pf_epilogue(const DecodeParams& P, const PfSync& sy, int64_t n_i
           const int n = c0 + i;
           const int r = col_r[n];
           if (r < 0) continue;
-          out[((int64_t)r - r0) * H] =
-              f32_to_bf16_bits(im.sh ? v[i] * gl : (v[i] * gl) * col_f[n]);
+          // col_f = routed weight x 2^hshift (shared expert: 2^hshift); x 1.0 is exact
+          out[((int64_t)r - r0) * H] = f32_to_bf16_bits((v[i] * gl) * col_f[n]);
         }
       }
     }
@@ -799,6 +803,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     pf_dequant<MODE>(smem, sy, n_items, nk);
   } else {
     pf_epilogue<MODE>(P, sy, n_items, mpairs);
+    // every epilogue warp gets here (a timeout returns from the epilogue loop)
+    if (MODE == kGateUp)
+      finish_gate_up(P, 1, kEpiWarps * kWarp, threadIdx.x - kWarpEpi * kWarp, &sh->last);
   }
   // neither CTA leaves (or frees tensor memory) while the leader's MMAs may read the peer's
   // shared and tensor memory or either CTA may still arrive on the other's barriers

@@ -84,7 +84,8 @@ __device__ void sort_block_t(const SortParams& P, int* hist /* [32][E] */) {
   __shared__ int sm_scan[33];
   __shared__ int sm_total;
 
-  if (P.zero_words && tid < P.n_zero) P.zero_words[tid] = 0;
+  if (P.zero_words)
+    for (int i = tid; i < P.n_zero; i += kSortThreads) P.zero_words[i] = 0;
   for (int i = tid; i < kSortWarps * E; i += kSortThreads) hist[i] = 0;
   __syncthreads();
 

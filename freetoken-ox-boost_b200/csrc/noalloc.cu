@@ -11,7 +11,7 @@
 //   * the scratch is kNoAllocScratchBytes (16 MiB) per GPU that loads the library, held until
 //     the process exits, whether or not this entry point is used;
 //   * a call whose workspace would exceed it is rejected with FTB_ERR_WORKSPACE (config-1
-//     shape, H=4096 I=1536 E=256 top-8 + shared expert: up to T = 153 tokens);
+//     shape, H=4096 I=1536 E=256 top-8 + shared expert: up to T = 122 tokens);
 //   * the first call on a device looks up the scratch's device address (cudaGetSymbolAddress,
 //     with that device current) and caches it; make that first call before any CUDA-graph
 //     stream capture;

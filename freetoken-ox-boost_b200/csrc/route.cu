@@ -1,4 +1,5 @@
-// route.cu - router GEMV and top-k (softmax-renormalise and sigmoid-bias modes).
+// route.cu - router GEMV and top-k (softmax-renormalise, sigmoid-bias and sqrt-softplus-bias
+// modes, optionally with the ranked top-NRANK list of the score-aware expert cache).
 //
 // One warp per token; lane l holds experts l, l+32, ... in registers (E <= 1024), sorted per
 // lane. Top-k is k rounds of a warp argmax over the lanes' heads on (score, index), the
@@ -56,12 +57,16 @@ __device__ __forceinline__ void sort_lane(Cand (&c)[PER]) {
 // One warp per token; lane l holds experts l, l+32, ..., sorted in selection order. Each of
 // the top_k rounds takes the warp-wide best of the lanes' heads (shuffle argmax with the
 // same order) and the winning lane pops its head.
+// n_rank > 0 (sigmoid-family modes): the selection continues to n_rank rounds and writes the
+// ranked list (rank_ids, rank_sc: the raw score, 0 for NaN) beside the top_k routing result.
 template <int PER>
 __global__ void __launch_bounds__(128) k_route_topk(const float* __restrict__ logits, int64_t T,
                                                     int E, int top_k, int mode,
                                                     const float* __restrict__ bias, float scaling,
                                                     int renorm, float* __restrict__ w_out,
-                                                    int32_t* __restrict__ id_out) {
+                                                    int32_t* __restrict__ id_out, int n_rank,
+                                                    int32_t* __restrict__ rank_ids,
+                                                    float* __restrict__ rank_sc) {
   pdl_launch_dependents();
   pdl_wait();
   const int lane = threadIdx.x & 31;
@@ -76,8 +81,12 @@ __global__ void __launch_bounds__(128) k_route_topk(const float* __restrict__ lo
     c[i] = Cand{-INFINITY, -1, 0.f};
     if (e < E) {
       const float l = row[e];
-      if (mode == FTB_ROUTE_SIGMOID) {
-        const float s = 1.0f / (1.0f + expf(-l));
+      if (mode != FTB_ROUTE_SOFTMAX) {
+        // sigmoid, or sqrt(softplus) in its overflow-stable form max(l,0) + log(1 + exp(-|l|))
+        // (fused_route.py:39-45)
+        const float s = mode == FTB_ROUTE_SQRTSOFTPLUS
+                            ? sqrtf(fmaxf(l, 0.f) + logf(1.0f + expf(-fabsf(l))))
+                            : 1.0f / (1.0f + expf(-l));
         float k = s + (bias ? bias[e] : 0.f);
         if (k != k) k = -3.4028234663852886e38f;  // NaN -> -FLT_MAX
         c[i] = Cand{k, e, s};
@@ -106,7 +115,8 @@ __global__ void __launch_bounds__(128) k_route_topk(const float* __restrict__ lo
   sort_lane<PER>(c);
   float wsum = 0.f;
   float wk = 0.f;  // this lane keeps the weight of selection k == lane
-  for (int k = 0; k < top_k; ++k) {
+  const int rounds = n_rank > top_k ? n_rank : top_k;
+  for (int k = 0; k < rounds; ++k) {
     Cand b = c[0];
     int src = lane;
 #pragma unroll
@@ -131,6 +141,11 @@ __global__ void __launch_bounds__(128) k_route_topk(const float* __restrict__ lo
     const int idx = b.idx < 0 ? 0 : (b.idx > E - 1 ? E - 1 : b.idx);
     float v = b.val;
     if (mode == FTB_ROUTE_SOFTMAX) v = v / denom;
+    if (k < n_rank && lane == 0) {
+      rank_ids[t * n_rank + k] = idx;
+      rank_sc[t * n_rank + k] = v == v ? v : 0.f;  // NaN scores rank with weight 0
+    }
+    if (k >= top_k) continue;
     wsum += v;
     if (lane == k) wk = v;
     if (lane == 0) id_out[t * top_k + k] = idx;
@@ -177,7 +192,7 @@ __global__ void __launch_bounds__(256) k_router_gemv(const uint16_t* __restrict_
 
 int launch_route_topk(const float* logits, int64_t T, int E, int top_k, int mode,
                       const float* bias, float scaling, int renorm, float* w, int32_t* ids,
-                      cudaStream_t stream) {
+                      int n_rank, int32_t* rank_ids, float* rank_sc, cudaStream_t stream) {
   if (T == 0) return FTB_OK;
   const int wpb = 4;
   const int64_t blocks = ceil_div(T, wpb);
@@ -186,7 +201,7 @@ int launch_route_topk(const float* logits, int64_t T, int E, int top_k, int mode
   cudaError_t err = cudaSuccess;
 #define FTB_ROUTE_LAUNCH(PER)                                                                \
   err = launch_pdl(k_route_topk<PER>, dim3((unsigned)blocks), dim3(32 * wpb), 0, stream, logits, \
-                   T, E, top_k, mode, bias, scaling, renorm, w, ids)
+                   T, E, top_k, mode, bias, scaling, renorm, w, ids, n_rank, rank_ids, rank_sc)
   if (per <= 1)
     FTB_ROUTE_LAUNCH(1);
   else if (per <= 2)

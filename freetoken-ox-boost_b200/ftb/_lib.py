@@ -24,9 +24,10 @@ FTB_ERR_NOT_BUILT = 7
 
 FTB_ROUTE_SOFTMAX = 0
 FTB_ROUTE_SIGMOID = 1
+FTB_ROUTE_SQRTSOFTPLUS = 2
 
 STATUS_BAD_ID = 1
-STATUS_F16_OVERFLOW = 2
+STATUS_F16_OVERFLOW = 2  # reserved: no longer raised (out-of-range rows of h are rescaled)
 STATUS_TIMEOUT = 4
 
 EP_HANDLE_BYTES = 64
@@ -52,17 +53,39 @@ class Nvfp4BankStruct(ctypes.Structure):
 
 _BP = ctypes.POINTER(Nvfp4BankStruct)
 
+FTB_ACT_SILU = 0
+FTB_ACT_SWIGLU_CLAMP = 1
+FTB_ACT_SWIGLUOAI = 2
+FTB_PATH_DECODE = 0
+FTB_PATH_PREFILL = 1
+
+
+class MoeArgsStruct(ctypes.Structure):
+    """``ftb_moe_args``: one layer call (every option of the reference's drivers)."""
+    _fields_ = [
+        ("x", _vp), ("bank", _BP), ("shared", _BP), ("topk_w", _vp), ("topk_ids", _vp),
+        ("T", _i64), ("H", _i32), ("I", _i32), ("top_k", _i32),
+        ("activation", _i32), ("act_alpha", _f32), ("act_limit", _f32),
+        ("weight_on_input", _i32), ("path", _i32), ("route_mask", _vp), ("phase", _i32),
+        ("out", _vp), ("workspace", _vp), ("workspace_bytes", _sz),
+        ("ic1", _vp), ("h", _vp), ("ic3", _vp), ("shared_ic1", _vp), ("shared_h", _vp),
+        ("shared_out", _vp),
+    ]
+
 SIGNATURES = {
     "ftb_status_string": (ctypes.c_char_p, [_i32]),
     "ftb_version": (_i32, []),
     "ftb_last_cuda_error": (ctypes.c_char_p, []),
     "ftb_route_topk": (_i32, [_vp, _i64, _i32, _i32, _i32, _vp, _f32, _i32, _vp, _vp, _vp]),
+    "ftb_route_ranked": (_i32, [_vp, _i64, _i32, _i32, _i32, _vp, _f32, _i32, _vp, _vp, _vp, _vp,
+                                _vp]),
     "ftb_router_gemv": (_i32, [_vp, _vp, _i64, _i32, _i32, _vp, _vp]),
     "ftb_moe_align_workspace_bytes": (_sz, [_i64, _i32, _i32]),
     "ftb_moe_align": (_i32, [_vp, _i64, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "ftb_moe_decode_workspace_bytes": (_sz, [_i64, _i32, _i32, _i32, _i32, _i32]),
     "ftb_moe_decode": (_i32, [_vp, _BP, _BP, _vp, _vp, _i64, _i32, _i32, _i32, _f32, _vp, _vp,
                               _sz, _vp]),
+    "ftb_moe_layer": (_i32, [ctypes.POINTER(MoeArgsStruct), _vp]),
     "ftb_moe_decode_plan": (_i32, [_i64, _i32, _i32, _i32, _i32, _i32, _vp]),
     "ftb_moe_decode_debug": (_i32, [_vp, _BP, _BP, _vp, _vp, _i64, _i32, _i32, _i32, _f32, _vp,
                                     _vp, _sz, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
@@ -83,6 +106,8 @@ SIGNATURES = {
     "ftb_ep_open": (_i32, [_vp, _vp]),
     "ftb_ep_set_wait_ns": (_i32, [_vp, _i64]),
     "ftb_ep_forward": (_i32, [_vp, _vp, _vp, _vp, _BP, _BP, _f32, _vp, _vp]),
+    "ftb_ep_forward_act": (_i32, [_vp, _vp, _vp, _vp, _BP, _BP, _i32, _f32, _f32, _i32, _vp,
+                                  _vp]),
     "ftb_ep_status": (_i32, [_vp, _i32, _vp]),
     "ftb_ep_destroy": (_i32, [_vp]),
     "ftb_profile_begin": (_i32, []),

@@ -81,7 +81,12 @@ class EpGroup:
 
     def forward(self, x: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor,
                 bank: Nvfp4Bank, shared: Nvfp4Bank | None, act_limit: float = float("inf"),
-                out: torch.Tensor | None = None) -> torch.Tensor:
+                out: torch.Tensor | None = None, *, activation: str | None = None,
+                act_alpha: float = 1.702, apply_router_weight_on_input: bool = False
+                ) -> torch.Tensor:
+        """One layer step. ``activation=None`` picks silu for an infinite ``act_limit`` and
+        swiglu_clamp otherwise (the reference's two GLM activations); "swigluoai" takes
+        ``act_alpha``."""
         if self._h is None:
             raise RuntimeError("EpGroup is closed")
         dev = require_cuda(x, topk_weights, topk_ids, bank.gate_up_packed)
@@ -95,12 +100,19 @@ class EpGroup:
             raise ValueError("shared expert presence differs from the group's")
         if out is None:
             out = torch.empty(self.T, self.H, dtype=torch.bfloat16, device=dev)
+        from .fused_nvfp4 import _act_spec
+
+        if activation is None:
+            activation = "silu" if act_limit == float("inf") else "swiglu_clamp"
+        kind, alpha, limit = _act_spec(activation, act_alpha, act_limit)
         b = bank.struct()
         s = shared.struct() if shared is not None else None
-        st = _lib.load().ftb_ep_forward(self._h, ptr(x), ptr(topk_weights), ptr(topk_ids),
-                                        ctypes.byref(b), ctypes.byref(s) if s is not None else None,
-                                        float(act_limit), ptr(out), stream_handle(dev))
-        _lib.check("ftb_ep_forward", st)
+        st = _lib.load().ftb_ep_forward_act(self._h, ptr(x), ptr(topk_weights), ptr(topk_ids),
+                                            ctypes.byref(b),
+                                            ctypes.byref(s) if s is not None else None, kind,
+                                            alpha, limit, 1 if apply_router_weight_on_input else 0,
+                                            ptr(out), stream_handle(dev))
+        _lib.check("ftb_ep_forward_act", st)
         return out
 
     def status(self, clear: bool = True) -> int:
@@ -125,7 +137,8 @@ class ExpertParallelMoE:
 
     def __init__(self, local_bank: Nvfp4Bank | None, shared: Nvfp4Bank | None, num_experts: int,
                  top_k: int, rank: int, world: int, group=None, activation: str = "silu",
-                 act_limit: float = 7.0, expert_fn: Callable | None = None,
+                 act_limit: float = 7.0, act_alpha: float = 1.702,
+                 apply_router_weight_on_input: bool = False, expert_fn: Callable | None = None,
                  shared_fn: Callable | None = None, combine_fn: Callable | None = None,
                  transport: str | None = None, ep_group: EpGroup | None = None):
         if transport is None:  # peer memory for libftb compute on CUDA banks, else NCCL
@@ -142,7 +155,8 @@ class ExpertParallelMoE:
         self.e0, self.e1 = shard_range(num_experts, rank, world)
         self.per = self.e1 - self.e0
         self.bank, self.shared = local_bank, shared
-        self.activation, self.act_limit = activation, act_limit
+        self.activation, self.act_limit, self.act_alpha = activation, act_limit, act_alpha
+        self.w_on_input = apply_router_weight_on_input
         self.expert_fn = expert_fn or self._gpu_experts
         self.shared_fn = shared_fn or self._gpu_shared
         self.combine_fn = combine_fn or self._gpu_combine
@@ -153,7 +167,9 @@ class ExpertParallelMoE:
         from .fused_nvfp4 import moe_decode
 
         return moe_decode(rows, self.bank, w.view(-1, 1), eids.view(-1, 1),
-                          activation=self.activation, act_limit=self.act_limit)
+                          activation=self.activation, act_limit=self.act_limit,
+                          act_alpha=self.act_alpha,
+                          apply_router_weight_on_input=self.w_on_input)
 
     def _gpu_shared(self, x):
         if self.shared is None:
@@ -164,7 +180,7 @@ class ExpertParallelMoE:
         ones = torch.ones(T, 1, dtype=torch.float32, device=x.device)
         zeros = torch.zeros(T, 1, dtype=torch.int32, device=x.device)
         return moe_decode(x, self.shared, ones, zeros, activation=self.activation,
-                          act_limit=self.act_limit)
+                          act_limit=self.act_limit, act_alpha=self.act_alpha)
 
     def _gpu_combine(self, ic3, ids, shared_out):
         from .fused_nvfp4 import moe_sum_reduce
@@ -185,13 +201,13 @@ class ExpertParallelMoE:
         return self._nccl_forward(x, topk_weights, topk_ids)
 
     def _p2p_forward(self, x, topk_weights, topk_ids):
-        from .fused_nvfp4 import _act_limit
-
         if self.ep_group is None:
             self.ep_group = EpGroup(x.shape[0], x.shape[1], self.bank.inter, self.E, self.K,
                                     self.shared is not None, self.rank, self.world, self.group)
-        limit = _act_limit(self.activation, self.act_limit)
-        return self.ep_group.forward(x, topk_weights, topk_ids, self.bank, self.shared, limit)
+        return self.ep_group.forward(x, topk_weights, topk_ids, self.bank, self.shared,
+                                     self.act_limit, activation=self.activation,
+                                     act_alpha=self.act_alpha,
+                                     apply_router_weight_on_input=self.w_on_input)
 
     def _nccl_forward(self, x: torch.Tensor, topk_weights: torch.Tensor,
                       topk_ids: torch.Tensor) -> torch.Tensor:

@@ -27,7 +27,7 @@ def select_nvfp4_backend(device, moe_intermediate_size=None, nvfp4_backend: str 
     if nvfp4_backend not in ("auto", "b200"):
         raise ValueError(f"nvfp4 backend {nvfp4_backend!r} is not available in this build")
     if activation not in _ACTS:
-        raise NotImplementedError(f"activation {activation!r} is not built (have {_ACTS})")
+        raise NotImplementedError(f"activation {activation!r} is not built (have {sorted(_ACTS)})")
     dev = torch.device(device)
     if dev.type != "cuda":
         raise ValueError("the b200 NVFP4 backend needs a CUDA device")
@@ -41,16 +41,19 @@ class B200Nvfp4Experts:
     """GPU-resident NVFP4 routed experts (+ optional shared expert) of one MoE layer."""
 
     def __init__(self, bank: Nvfp4Bank, activation: str = "silu", swiglu_limit=None,
-                 shared: Nvfp4Bank | None = None, layer_id: int = -1):
+                 shared: Nvfp4Bank | None = None, layer_id: int = -1,
+                 hidden_act_alpha: float = 1.702, apply_router_weight_on_input: bool = False):
         if activation not in _ACTS:
-            raise NotImplementedError(f"activation {activation!r} is not built (have {_ACTS})")
+            raise NotImplementedError(f"activation {activation!r} is not built (have {sorted(_ACTS)})")
         bank.validate()
         self.bank = bank
         self.shared = shared
         self.layer_id = layer_id
         self.num_experts = bank.num_experts
         self.activation = activation
-        self.apply_router_weight_on_input = False
+        # the resident layer's attributes (experts_resident.py:32-33)
+        self.apply_router_weight_on_input = apply_router_weight_on_input
+        self.hidden_act_alpha = hidden_act_alpha
         self.swiglu_limit = swiglu_limit
 
     @classmethod
@@ -89,7 +92,10 @@ class B200Nvfp4Experts:
             is_prefill = hidden_states.shape[0] >= PREFILL_MIN_TOKENS
         layer = moe_prefill if is_prefill else moe_decode
         return layer(hidden_states, self.bank, topk_weights, topk_ids,
-                     activation=self.activation, act_limit=self._limit(), shared=shared)
+                     activation=self.activation, act_limit=self._limit(),
+                     act_alpha=self.hidden_act_alpha,
+                     apply_router_weight_on_input=self.apply_router_weight_on_input,
+                     shared=shared)
 
 
 class Nvfp4MoELayer:
@@ -98,7 +104,7 @@ class Nvfp4MoELayer:
     def __init__(self, experts: B200Nvfp4Experts, top_k: int, renormalize: bool = True,
                  router: str = "softmax", gate_weight: torch.Tensor | None = None,
                  score_bias: torch.Tensor | None = None, routed_scaling: float = 1.0):
-        if router not in ("softmax", "sigmoid"):
+        if router not in ("softmax", "sigmoid", "sqrtsoftplus"):
             raise ValueError(f"router {router!r}")
         self.experts = experts
         self.top_k = top_k
@@ -117,7 +123,8 @@ class Nvfp4MoELayer:
             return fused_topk(hidden_states, logits, self.top_k, self.renormalize)
         bias = self.score_bias if self.score_bias is not None else torch.zeros(
             logits.shape[1], device=logits.device)
-        return fused_route(logits, bias, self.top_k, self.renormalize, self.routed_scaling)
+        return fused_route(logits, bias, self.top_k, self.renormalize, self.routed_scaling,
+                           act=self.router)
 
     def forward(self, hidden_states: torch.Tensor, logits: torch.Tensor | None = None):
         w, ids = self.route(hidden_states, logits)

@@ -11,10 +11,13 @@ Extension: keyword ``shared=`` adds one always-on NVFP4 shared expert exactly as
 block does after ``routed_forward`` (``out + shared_experts(x)``, routed first, bf16;
 patches/models_glm_moe_dsa_moe.patch:203-206).
 
-Activations: ``"silu"`` (plain, act_limit ignored like the reference's silu path) and
-``"swiglu_clamp"`` (silu(min(g, L)) * clamp(u, +-L) with L = act_limit). Errors mirror the
-reference's setup checks: ``ValueError`` for bad shapes/dtypes, ``NotImplementedError`` for
-activations/modes this build does not implement.
+Activations (``_run_act``, patches/moe_fused_nvfp4.patch:12-22): ``"silu"`` (plain, act_limit
+ignored like the reference's silu path), ``"swiglu_clamp"`` (silu(min(g, L)) * clamp(u, +-L)
+with L = act_limit) and ``"swigluoai"`` (g' = min(g, L), u' = clamp(u, +-L),
+g' * sigmoid(act_alpha * g') * (u' + 1); gate rows 0..I-1, up rows I..2I-1 of the bank).
+``apply_router_weight_on_input=True`` puts the routed weight on the gate_up output instead of
+the down output, as the reference's two MUL_ROUTED_WEIGHT flags do (:138, :145). Errors mirror
+the reference's setup checks: ``ValueError`` for bad shapes/dtypes and unknown activations.
 """
 from __future__ import annotations
 
@@ -26,16 +29,18 @@ from . import _lib
 from ._runtime import ptr, read_status, require, require_cuda, stream_handle, workspace
 from .banks import Nvfp4Bank
 
-_ACTS = ("silu", "swiglu_clamp")
+_ACTS = {"silu": _lib.FTB_ACT_SILU, "swiglu_clamp": _lib.FTB_ACT_SWIGLU_CLAMP,
+         "swigluoai": _lib.FTB_ACT_SWIGLUOAI}
 
 
-def _act_limit(activation: str, act_limit: float) -> float:
+def _act_spec(activation: str, act_alpha: float, act_limit: float):
+    """(FTB_ACT_*, alpha, limit) for the library."""
     if activation not in _ACTS:
-        raise NotImplementedError(f"activation {activation!r} is not built (have {_ACTS})")
-    if activation == "silu":
-        return float("inf")
+        raise ValueError(f"activation {activation!r} is not one of {sorted(_ACTS)}")
     L = float("inf") if act_limit is None else float(act_limit)
-    return L
+    if activation == "silu":
+        L = float("inf")
+    return _ACTS[activation], float(act_alpha), L
 
 
 def _check_inputs(x, bank: Nvfp4Bank, topk_weights, topk_ids, shared):
@@ -83,51 +88,56 @@ def prefill_workspace_bytes(T: int, bank: Nvfp4Bank, top_k: int, has_shared: boo
 
 def moe_decode(x: torch.Tensor, bank: Nvfp4Bank, topk_weights: torch.Tensor,
                topk_ids: torch.Tensor, *, activation: str = "silu", act_limit: float = 7.0,
+               act_alpha: float = 1.702, apply_router_weight_on_input: bool = False,
                shared: Nvfp4Bank | None = None, out: torch.Tensor | None = None,
                debug: bool = False, check_status: bool = False):
     """Decode layer on a bank object. ``debug=True`` returns (out, intermediates dict)."""
-    return _layer(False, x, bank, topk_weights, topk_ids, activation, act_limit, shared, out,
-                  debug, check_status)
+    return _layer(_lib.FTB_PATH_DECODE, x, bank, topk_weights, topk_ids, activation, act_alpha,
+                  act_limit, apply_router_weight_on_input, shared, out, debug, check_status)
 
 
 def moe_prefill(x: torch.Tensor, bank: Nvfp4Bank, topk_weights: torch.Tensor,
                 topk_ids: torch.Tensor, *, activation: str = "silu", act_limit: float = 7.0,
+                act_alpha: float = 1.702, apply_router_weight_on_input: bool = False,
                 shared: Nvfp4Bank | None = None, out: torch.Tensor | None = None,
                 debug: bool = False, check_status: bool = False):
     """The same layer on the tensor-core grouped GEMMs (large T). Same contract and result
     as ``moe_decode``; ``debug=True`` returns (out, intermediates dict)."""
-    return _layer(True, x, bank, topk_weights, topk_ids, activation, act_limit, shared, out,
-                  debug, check_status)
+    return _layer(_lib.FTB_PATH_PREFILL, x, bank, topk_weights, topk_ids, activation, act_alpha,
+                  act_limit, apply_router_weight_on_input, shared, out, debug, check_status)
 
 
-def _layer(prefill: bool, x, bank, topk_weights, topk_ids, activation, act_limit, shared, out,
-           debug, check_status):
+def _layer(path: int, x, bank, topk_weights, topk_ids, activation, act_alpha, act_limit,
+           weight_on_input, shared, out, debug, check_status, route_mask=None, phase=0,
+           ws=None):
     dev = _check_inputs(x, bank, topk_weights, topk_ids, shared)
-    limit = _act_limit(activation, act_limit)
+    kind, alpha, limit = _act_spec(activation, act_alpha, act_limit)
     T, H = x.shape
     K = topk_ids.shape[1]
     I = bank.inter
-    if out is None:
+    if out is None and (route_mask is None or phase & _lib.PHASE_COMBINE):
         out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
     lib = _lib.load()
-    if prefill:
-        nbytes = prefill_workspace_bytes(T, bank, K, shared is not None)
-        run, run_dbg = lib.ftb_moe_prefill, lib.ftb_moe_prefill_debug
-        name = "ftb_moe_prefill"
-    else:
-        nbytes = decode_workspace_bytes(T, bank, K, shared is not None)
-        run, run_dbg = lib.ftb_moe_decode, lib.ftb_moe_decode_debug
-        name = "ftb_moe_decode"
-    ws = workspace(nbytes, dev)
+    if ws is None:
+        wsb = (prefill_workspace_bytes if path == _lib.FTB_PATH_PREFILL else
+               decode_workspace_bytes)(T, bank, K, shared is not None)
+        ws = workspace(wsb, dev)
     b = bank.struct()
     s = shared.struct() if shared is not None else None
-    sp = ctypes.byref(s) if s is not None else None
-    if not debug:
-        st = run(ptr(x), ctypes.byref(b), sp, ptr(topk_weights), ptr(topk_ids), T, H, I, K,
-                 limit, ptr(out), ptr(ws), ws.numel(), stream_handle(dev))
-        _lib.check(name, st)
-        inter = None
-    else:
+    a = _lib.MoeArgsStruct()
+    a.x, a.topk_w, a.topk_ids = x.data_ptr(), topk_weights.data_ptr(), topk_ids.data_ptr()
+    a.bank = ctypes.pointer(b)
+    a.shared = ctypes.pointer(s) if s is not None else None
+    a.T, a.H, a.I, a.top_k = T, H, I, K
+    a.activation, a.act_alpha, a.act_limit = kind, alpha, limit
+    a.weight_on_input = 1 if weight_on_input else 0
+    a.path = path
+    a.route_mask = route_mask.data_ptr() if route_mask is not None else None
+    a.phase = phase
+    a.out = out.data_ptr() if out is not None else None
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    inter = None
+    if debug:
         bf = torch.bfloat16
         inter = dict(ic1=torch.zeros(T, K, 2 * I, dtype=bf, device=dev),
                      h=torch.zeros(T, K, I, dtype=bf, device=dev),
@@ -136,20 +146,18 @@ def _layer(prefill: bool, x, bank, topk_weights, topk_ids, activation, act_limit
             inter.update(shared_ic1=torch.zeros(T, 2 * I, dtype=bf, device=dev),
                          shared_h=torch.zeros(T, I, dtype=bf, device=dev),
                          shared_out=torch.zeros(T, H, dtype=bf, device=dev))
-        g = inter.get
-        st = run_dbg(ptr(x), ctypes.byref(b), sp, ptr(topk_weights), ptr(topk_ids), T, H, I, K,
-                     limit, ptr(out), ptr(ws), ws.numel(), ptr(g("ic1")), ptr(g("h")),
-                     ptr(g("ic3")), ptr(g("shared_ic1")), ptr(g("shared_h")),
-                     ptr(g("shared_out")), stream_handle(dev))
-        _lib.check(name + "_debug", st)
+        for name, t in inter.items():
+            setattr(a, name, t.data_ptr())
+    st = lib.ftb_moe_layer(ctypes.byref(a), stream_handle(dev))
+    _lib.check("ftb_moe_layer", st)
     if check_status or debug:
         status = read_status(ws)
         if inter is not None:
             inter["status"] = status
         if check_status and status & _lib.STATUS_BAD_ID:
             raise ValueError("topk_ids holds ids outside [0, num_experts)")
-        if check_status and status & _lib.STATUS_F16_OVERFLOW:
-            raise OverflowError("an expert activation exceeded the f16 operand range")
+        if check_status and status & _lib.STATUS_TIMEOUT:
+            raise RuntimeError("a bounded device-side wait of the layer timed out")
     return (out, inter) if debug else out
 
 
@@ -171,13 +179,11 @@ def fused_experts_decode_nvfp4_marlin(
     shared: Nvfp4Bank | None = None,
 ) -> torch.Tensor:
     """Drop-in for the reference decode driver (CUDA-graph safe after one eager call)."""
-    del act_alpha  # only the swigluoai activation uses it; not built
-    if apply_router_weight_on_input:
-        raise NotImplementedError("apply_router_weight_on_input=True is not built")
     bank = Nvfp4Bank(gate_up_packed, gate_up_scale, gate_up_global, down_packed, down_scale,
                      down_global)
     return moe_decode(hidden_states, bank, topk_weights, topk_ids, activation=activation,
-                      act_limit=act_limit, shared=shared)
+                      act_limit=act_limit, act_alpha=act_alpha,
+                      apply_router_weight_on_input=apply_router_weight_on_input, shared=shared)
 
 
 def _phase_masks(miss_mask, R: int, dev):
@@ -226,32 +232,23 @@ def fused_experts_decode_nvfp4_split(
     phases write disjoint route rows of the same workspace, so the result is bit-identical
     to ``fused_experts_decode_nvfp4_marlin``. ``topk_ids`` may be cache-slot ids of a bank of
     slots (position == slot). The shared expert (keyword, resident) runs in phase A."""
-    del act_alpha
-    if apply_router_weight_on_input:
-        raise NotImplementedError("apply_router_weight_on_input=True is not built")
     bank = Nvfp4Bank(gate_up_packed, gate_up_scale, gate_up_global, down_packed, down_scale,
                      down_global)
     x = hidden_states
     dev = _check_inputs(x, bank, topk_weights, topk_ids, shared)
-    limit = _act_limit(activation, act_limit)
+    _act_spec(activation, act_alpha, act_limit)
     T, H = x.shape
     K = topk_ids.shape[1]
     mask_a, mask_b = _phase_masks(miss_mask, T * K, dev)
     out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
-    lib = _lib.load()
     ws = workspace(decode_workspace_bytes(T, bank, K, shared is not None), dev)
-    b = bank.struct()
-    s = shared.struct() if shared is not None else None
-    sp = ctypes.byref(s) if s is not None else None
     for phase, mask in ((0, mask_a), (1, mask_b)):
         if phase == 1 and copy_event is not None:
             torch.cuda.current_stream(dev).wait_event(copy_event)
         flags = _lib.PHASE_SHARED if phase == 0 else _lib.PHASE_COMBINE
-        st = lib.ftb_moe_decode_phase(ptr(x), ctypes.byref(b), sp, ptr(topk_weights),
-                                      ptr(topk_ids), ptr(mask), flags, T, H, bank.inter, K,
-                                      limit, ptr(out) if phase == 1 else None, ptr(ws),
-                                      ws.numel(), stream_handle(dev))
-        _lib.check("ftb_moe_decode_phase", st)
+        _layer(_lib.FTB_PATH_DECODE, x, bank, topk_weights, topk_ids, activation, act_alpha,
+               act_limit, apply_router_weight_on_input, shared, out if phase == 1 else None,
+               False, False, route_mask=mask, phase=flags, ws=ws)
     return out
 
 
@@ -280,12 +277,10 @@ def fused_experts_nvfp4(
                      down_global)
     if num_experts != bank.num_experts:
         raise ValueError(f"num_experts {num_experts} != bank experts {bank.num_experts}")
-    if apply_router_weight_on_input:
-        raise NotImplementedError("apply_router_weight_on_input=True is not built")
-    del act_alpha
     layer = moe_prefill if hidden_states.shape[0] >= PREFILL_MIN_TOKENS else moe_decode
     return layer(hidden_states, bank, topk_weights, topk_ids, activation=activation,
-                 act_limit=act_limit, shared=shared)
+                 act_limit=act_limit, act_alpha=act_alpha,
+                 apply_router_weight_on_input=apply_router_weight_on_input, shared=shared)
 
 
 def moe_sum_reduce(ic3: torch.Tensor, topk_ids: torch.Tensor, num_experts: int,

@@ -45,8 +45,10 @@ enum {
 
 /* Router modes of ftb_route_topk. */
 enum {
-  FTB_ROUTE_SOFTMAX = 0, /* fused_topk(..., renormalize): softmax, top-k, renormalise */
-  FTB_ROUTE_SIGMOID = 1  /* fused_route(): sigmoid + bias, top-k, renorm /(sum+1e-20), scale */
+  FTB_ROUTE_SOFTMAX = 0,     /* fused_topk(..., renormalize): softmax, top-k, renormalise */
+  FTB_ROUTE_SIGMOID = 1,     /* fused_route(): sigmoid + bias, top-k, renorm /(sum+1e-20), scale */
+  FTB_ROUTE_SQRTSOFTPLUS = 2 /* fused_route(act="sqrtsoftplus"): score sqrt(softplus(l)),
+                                otherwise as FTB_ROUTE_SIGMOID (fused_route.py:39-45) */
 };
 
 typedef struct ftb_nvfp4_bank {
@@ -77,6 +79,20 @@ FTB_API const char* ftb_last_cuda_error(void);
 FTB_API int ftb_route_topk(const float* logits, int64_t T, int E, int top_k, int mode,
                    const float* bias, float scaling, int renorm,
                    float* topk_w, int32_t* topk_ids, ftb_stream_t stream);
+
+/*
+ * The sigmoid + bias router with the ranked list the score-aware expert cache feeds on,
+ * replacing fused_route_ranked(logits, bias, top_k, renorm, scaling, n_rank)
+ * (overlay/freetoken/kernel/triton/fused_route.py:85-137): topk_w / topk_ids exactly as
+ * ftb_route_topk(FTB_ROUTE_SIGMOID), plus rank_ids int32 [T, n_rank] = the top n_rank experts
+ * by selection score (the first top_k are the selected ids, same order and tie-break) and
+ * rank_scores fp32 [T, n_rank] = their raw sigmoid scores (0 where the score is NaN).
+ * Requires top_k <= n_rank <= E.
+ */
+FTB_API int ftb_route_ranked(const float* logits, int64_t T, int E, int top_k, int n_rank,
+                             const float* bias, float scaling, int renorm, float* topk_w,
+                             int32_t* topk_ids, int32_t* rank_ids, float* rank_scores,
+                             ftb_stream_t stream);
 
 /*
  * fp32 router GEMV logits[T, E] = float(x[T, H]) . gate_w[E, H]^T, replacing
@@ -115,13 +131,67 @@ FTB_API int ftb_moe_align(const int32_t* topk_ids, int64_t T, int top_k, int E, 
  * Workspace: ftb_moe_decode_workspace_bytes() bytes of device memory, 256-byte aligned.
  * Bytes [0, 4) of every workspace hold the device status word, cleared at each call:
  * bit 0 = a top-k id outside [0, E) was skipped (its route contributes 0);
- * bit 1 = an activation reached |v| >= 65504 on the f16 tensor-core operand.
+ * bit 1 = reserved (no longer raised: a route whose activation h exceeds the f16 range of the
+ * tensor-core operand is rescaled by a power of two inside the call and stays exact).
  */
 FTB_API size_t ftb_moe_decode_workspace_bytes(int64_t T, int H, int I, int E, int top_k, int has_shared);
 FTB_API int ftb_moe_decode(const uint16_t* x, const ftb_nvfp4_bank* bank, const ftb_nvfp4_bank* shared,
                    const float* topk_w, const int32_t* topk_ids,
                    int64_t T, int H, int I, int top_k, float act_limit,
                    uint16_t* out, void* workspace, size_t workspace_bytes, ftb_stream_t stream);
+
+/*
+ * The layer with every option of the reference's drivers, in one argument block: the decode
+ * driver fused_experts_decode_nvfp4_marlin(x, gu_p, gu_s, gu_g, dn_p, dn_s, dn_g, w, ids,
+ * activation, apply_router_weight_on_input, act_alpha, act_limit)
+ * (patches/moe_fused_nvfp4.patch:136-152; caller
+ * overlay/freetoken/models/glm5_next/experts_resident.py:79-83), the prefill driver
+ * fused_experts_nvfp4(...) (experts_resident.py:69-75) and one phase of the split decode
+ * (patches/moe_fused_nvfp4.patch:189-272). ftb_moe_decode / _prefill / _debug / _phase are this
+ * call with activation = act_limit finite and > 0 ? FTB_ACT_SWIGLU_CLAMP : FTB_ACT_SILU.
+ *   activation  FTB_ACT_SILU: h = silu(g) * u;
+ *               FTB_ACT_SWIGLU_CLAMP: silu(min(g, L)) * clamp(u, -L, L), L = act_limit;
+ *               FTB_ACT_SWIGLUOAI: g' = min(g, L), u' = clamp(u, -L, L),
+ *               h = g' * sigmoid(act_alpha * g') * (u' + 1) (the reference's
+ *               swigluoai_and_mul(gate_up, out, alpha, limit), patches/moe_fused_nvfp4.patch:
+ *               12-14); rows 0..I-1 of gate_up are g, rows I..2I-1 are u in every mode.
+ *   weight_on_input  apply_router_weight_on_input: the routed weight multiplies the gate_up
+ *               output (ic1 = bf16(acc * global * w)) and not the down output, as the
+ *               reference's MUL_ROUTED_WEIGHT flags do (patches/moe_fused_nvfp4.patch:138,145).
+ *   path        FTB_PATH_DECODE (HBM-streaming GEMVs, ftb_moe_decode_workspace_bytes()) or
+ *               FTB_PATH_PREFILL (tensor-core GEMMs, ftb_moe_prefill_workspace_bytes()).
+ *   route_mask, phase  NULL, or one phase of the split decode as ftb_moe_decode_phase()
+ *               (decode path only).
+ *   ic1 .. shared_out  debug copies of the intermediates as ftb_moe_decode_debug(), or NULL.
+ */
+enum { FTB_ACT_SILU = 0, FTB_ACT_SWIGLU_CLAMP = 1, FTB_ACT_SWIGLUOAI = 2 };
+enum { FTB_PATH_DECODE = 0, FTB_PATH_PREFILL = 1 };
+typedef struct ftb_moe_args {
+  const uint16_t* x;             /* [T, H] bf16 */
+  const ftb_nvfp4_bank* bank;    /* routed experts */
+  const ftb_nvfp4_bank* shared;  /* one always-on expert (weight 1.0), or NULL */
+  const float* topk_w;           /* [T, top_k] */
+  const int32_t* topk_ids;       /* [T, top_k] */
+  int64_t T;
+  int H, I, top_k;
+  int activation;                /* FTB_ACT_* */
+  float act_alpha;
+  float act_limit;
+  int weight_on_input;
+  int path;                      /* FTB_PATH_* */
+  const int8_t* route_mask;      /* [T * top_k] or NULL */
+  int phase;                     /* FTB_PHASE_* flags when route_mask != NULL */
+  uint16_t* out;                 /* [T, H] bf16 */
+  void* workspace;
+  size_t workspace_bytes;
+  uint16_t* ic1;                 /* debug copies, each may be NULL */
+  uint16_t* h;
+  uint16_t* ic3;
+  uint16_t* shared_ic1;
+  uint16_t* shared_h;
+  uint16_t* shared_out;
+} ftb_moe_args;
+FTB_API int ftb_moe_layer(const ftb_moe_args* args, ftb_stream_t stream);
 
 /*
  * Host-only query (launches nothing): the work-tile rows the decode GEMVs of a call with this
@@ -209,7 +279,7 @@ FTB_API int ftb_moe_combine(const uint16_t* ic3, const int32_t* topk_ids, const 
  * reference): same arguments and result as ftb_moe_decode() without the workspace, which is
  * taken from a 16 MiB scratch array the library holds in device memory on every GPU that
  * loads it, until the process exits. Larger needs return FTB_ERR_WORKSPACE (config-1 shape
- * with a shared expert: T <= 153). The first call on a device looks the scratch up; make it
+ * with a shared expert: T <= 122). The first call on a device looks the scratch up; make it
  * before any CUDA-graph capture. All calls share the scratch: calls that may overlap on the
  * GPU race and must be serialised by the caller. Allocates nothing.
  */
@@ -251,6 +321,13 @@ FTB_API int ftb_ep_forward(ftb_ep* ep, const uint16_t* x, const float* topk_w,
                            const int32_t* topk_ids, const ftb_nvfp4_bank* local_bank,
                            const ftb_nvfp4_bank* shared, float act_limit, uint16_t* out,
                            ftb_stream_t stream);
+/* ftb_ep_forward() with the activation options of ftb_moe_args (FTB_ACT_*, act_alpha,
+ * act_limit, weight_on_input = apply_router_weight_on_input). */
+FTB_API int ftb_ep_forward_act(ftb_ep* ep, const uint16_t* x, const float* topk_w,
+                               const int32_t* topk_ids, const ftb_nvfp4_bank* local_bank,
+                               const ftb_nvfp4_bank* shared, int activation, float act_alpha,
+                               float act_limit, int weight_on_input, uint16_t* out,
+                               ftb_stream_t stream);
 FTB_API int ftb_ep_status(ftb_ep* ep, int clear, ftb_stream_t stream);
 FTB_API int ftb_ep_destroy(ftb_ep* ep);
 

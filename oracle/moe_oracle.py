@@ -147,17 +147,27 @@ def f32_sigmoid(x: np.ndarray) -> np.ndarray:
         return (F32(1.0) / (F32(1.0) + np.exp(-x))).astype(F32)
 
 
-def swiglu(gate: np.ndarray, up: np.ndarray, limit: float = float("inf"), rnd=None) -> np.ndarray:
-    """``bf16((min(g,L) * sigmoid(min(g,L))) * clamp(u,-L,L))`` in fp32 with one rounding
-    (``kernel_triton_dsv4_fused_moe.patch:22-36`` ``_swiglu_kernel``;
-    ``nvfp4_marlin_swiglu.py:109-116``; C++ twin ``kernel_csrc_cpu_moe_cpu_moe_ext.patch:7-13``).
-    ``limit > 0`` enables the clamps exactly as ``HAS_LIMIT=limit > 0``; +inf is plain silu."""
+def swiglu(gate: np.ndarray, up: np.ndarray, limit: float = float("inf"), rnd=None,
+           act: str | None = None, alpha: float = 1.702) -> np.ndarray:
+    """The activation between the GEMVs, in fp32 with one bf16 rounding (``_run_act``,
+    ``patches/moe_fused_nvfp4.patch:12-22``):
+
+    * silu / swiglu_clamp (``act`` None): ``bf16((min(g,L) * sigmoid(min(g,L))) *
+      clamp(u,-L,L))`` (``kernel_triton_dsv4_fused_moe.patch:22-36`` ``_swiglu_kernel``;
+      ``nvfp4_marlin_swiglu.py:109-116``; C++ twin ``kernel_csrc_cpu_moe_cpu_moe_ext.patch:7-13``).
+      ``limit > 0`` enables the clamps exactly as ``HAS_LIMIT=limit > 0``; +inf is plain silu.
+    * ``act="swigluoai"``: ``swigluoai_and_mul(gate_up, out, alpha, limit)`` (called at
+      ``patches/moe_fused_nvfp4.patch:12-14``; its body is upstream and absent, so this
+      restates the published GPT-OSS gated unit): g' = min(g, L), u' = clamp(u, -L, L),
+      ``bf16((g' * sigmoid(alpha * g')) * (u' + 1))``."""
     g = np.asarray(gate, dtype=F32)
     u = np.asarray(up, dtype=F32)
     if limit > 0:
         L = F32(limit)
         g = np.minimum(g, L)
         u = np.minimum(np.maximum(u, -L), L)
+    if act == "swigluoai":
+        return (rnd or bf16_round)((g * f32_sigmoid(F32(alpha) * g)) * (u + F32(1)))
     return (rnd or bf16_round)((g * f32_sigmoid(g)) * u)
 
 
@@ -202,34 +212,58 @@ def topk_softmax(logits: np.ndarray, top_k: int, renormalize: bool = True):
     return w.astype(F32), ids
 
 
+def f32_sqrtsoftplus(x: np.ndarray) -> np.ndarray:
+    """sqrt(softplus(x)) in its overflow-stable fp32 form max(x, 0) + log(1 + exp(-|x|))
+    (``overlay/freetoken/kernel/triton/fused_route.py:39-43``)."""
+    x = np.asarray(x, dtype=F32)
+    with np.errstate(over="ignore", invalid="ignore"):
+        sp = (np.maximum(x, F32(0)) + np.log(F32(1) + np.exp(-np.abs(x)))).astype(F32)
+        return np.sqrt(sp).astype(F32)
+
+
 def fused_route_sigmoid(logits: np.ndarray, bias: np.ndarray, top_k: int, renorm: bool,
-                        scaling: float):
+                        scaling: float, act: str = "sigmoid", n_rank: int = 0):
     """GLM router epilogue ``_fused_route_kernel`` (``overlay/freetoken/kernel/triton/fused_route.py:28-62``):
-    sc = sigmoid(l); s4c = sc + bias (NaN -> -FLT_MAX); ids by iterative first-index argmax;
-    w = sc[ids]; wsum accumulated in selection order; w = w / (wsum + 1e-20) if renorm;
-    w *= scaling. Ids are clamped to [0, E-1]."""
+    sc = sigmoid(l) (``act="sigmoid"``) or sqrt(softplus(l)) (``act="sqrtsoftplus"``, :39-45);
+    s4c = sc + bias (NaN -> -FLT_MAX); ids by iterative first-index argmax; w = sc[ids]; wsum
+    accumulated in selection order; w = w / (wsum + 1e-20) if renorm; w *= scaling. Ids are
+    clamped to [0, E-1].
+
+    ``n_rank > 0`` restates ``_fused_route_ext_kernel`` (:85-121): the selection runs n_rank
+    rounds, the first top_k of which are the routing result, and also returns the ranked list
+    (rank_ids [T, n_rank], rank_scores [T, n_rank] = sc of each, 0 where it is NaN)."""
     lg = np.asarray(logits, dtype=F32)
     T, E = lg.shape
-    sc = f32_sigmoid(lg)
+    sc = f32_sqrtsoftplus(lg) if act == "sqrtsoftplus" else f32_sigmoid(lg)
     s4c = (sc + np.asarray(bias, dtype=F32)[None, :]).astype(F32)
     s4c = np.where(np.isnan(s4c), F32(-3.4028234663852886e38), s4c)
+    rounds = max(top_k, n_rank)
     ids = np.zeros((T, top_k), np.int32)
     w = np.zeros((T, top_k), F32)
+    rid = np.zeros((T, n_rank), np.int32)
+    rsc = np.zeros((T, n_rank), F32)
     for t in range(T):
         row = s4c[t].copy()
         wsum = F32(0.0)
-        for k in range(top_k):
+        for k in range(rounds):
             idx = int(np.argmax(row))  # first index of the max
             idx = min(max(idx, 0), E - 1)
-            ids[t, k] = idx
-            w[t, k] = sc[t, idx]
-            wsum = F32(wsum + sc[t, idx])
+            val = sc[t, idx]
+            if k < n_rank:
+                rid[t, k] = idx
+                rsc[t, k] = val if val == val else F32(0)
+            if k < top_k:
+                ids[t, k] = idx
+                w[t, k] = val
+                wsum = F32(wsum + val)
             row[idx] = -np.inf
         for k in range(top_k):
             v = w[t, k]
             if renorm:
                 v = F32(v / F32(wsum + F32(1e-20)))
             w[t, k] = F32(v * F32(scaling))
+    if n_rank:
+        return w, ids, rid, rsc
     return w, ids
 
 
@@ -276,7 +310,8 @@ def _f16_to_f32(g) -> np.ndarray:
     return g.astype(F32)
 
 
-def expert_forward(a: np.ndarray, bank: dict, e: int, limit: float, route_w=None, rnd=None):
+def expert_forward(a: np.ndarray, bank: dict, e: int, limit: float, route_w=None, rnd=None,
+                   act: str | None = None, alpha: float = 1.702, w_on_input: bool = False):
     """One expert for the rows ``a`` [R, H]: gate_up GEMV -> ic1 (bf16, x global) ->
     SwiGLU -> h (bf16) -> down GEMV -> ic3 = bf16(acc * global * w) (``route_w`` None = no
     routed weight, the shared-expert case).
@@ -284,22 +319,29 @@ def expert_forward(a: np.ndarray, bank: dict, e: int, limit: float, route_w=None
     Follows ``fused_experts_decode_nvfp4_marlin`` (``patches/moe_fused_nvfp4.patch:136-152``):
     ``_decode_gemm_marlin`` with ``mul_routed_weight=False`` for gate_up, activation, then
     the down GEMV with the routed weight applied in fp32 before the bf16 store
-    (``nvfp4_marlin_swiglu.py:120-129``). Rows 0..I-1 of gate_up are gate, I..2I-1 up."""
+    (``nvfp4_marlin_swiglu.py:120-129``). Rows 0..I-1 of gate_up are gate, I..2I-1 up.
+    ``w_on_input`` (``apply_router_weight_on_input=True``) moves the routed weight to the
+    gate_up GEMV's epilogue, as the driver's ``mul_routed_weight`` arguments do
+    (``patches/moe_fused_nvfp4.patch:138,145``)."""
     gu_p, gu_s, gu_g = bank["gate_up_packed"][e], bank["gate_up_scale"][e], bank["gate_up_global"][e]
     dn_p, dn_s, dn_g = bank["down_packed"][e], bank["down_scale"][e], bank["down_global"][e]
     rnd = rnd or bf16_round
     I = gu_p.shape[0] // 2
-    acc1 = nvfp4_gemv(a, gu_p, gu_s)
-    ic1 = rnd(acc1 * _f16_to_f32(gu_g)[None, :])
-    h = swiglu(ic1[:, :I], ic1[:, I:], limit, rnd)
+    rw = None if route_w is None else np.asarray(route_w, F32)[:, None]
+    acc1 = nvfp4_gemv(a, gu_p, gu_s) * _f16_to_f32(gu_g)[None, :]
+    if w_on_input and rw is not None:
+        acc1 = acc1 * rw
+    ic1 = rnd(acc1)
+    h = swiglu(ic1[:, :I], ic1[:, I:], limit, rnd, act, alpha)
     acc3 = nvfp4_gemv(h, dn_p, dn_s) * _f16_to_f32(dn_g)[None, :]
-    if route_w is not None:
-        acc3 = acc3 * np.asarray(route_w, F32)[:, None]
+    if rw is not None and not w_on_input:
+        acc3 = acc3 * rw
     return ic1, h, rnd(acc3)
 
 
 def moe_layer(x: np.ndarray, bank: dict, topk_w: np.ndarray, topk_ids: np.ndarray,
-              shared: dict | None = None, limit: float = float("inf")) -> dict:
+              shared: dict | None = None, limit: float = float("inf"), act: str | None = None,
+              alpha: float = 1.702, w_on_input: bool = False) -> dict:
     """Full decode/prefill layer on bf16-valued fp32 inputs.
 
     routed = ``moe_sum_reduce_triton(ic3)`` = bf16(sum over k of fp32(ic3[t,k]), k in order)
@@ -316,7 +358,8 @@ def moe_layer(x: np.ndarray, bank: dict, topk_w: np.ndarray, topk_ids: np.ndarra
     ids = np.asarray(topk_ids, np.int64)
     for e in np.unique(ids):
         tt, kk = np.nonzero(ids == e)
-        a, b, c = expert_forward(x[tt], bank, int(e), limit, np.asarray(topk_w, F32)[tt, kk])
+        a, b, c = expert_forward(x[tt], bank, int(e), limit, np.asarray(topk_w, F32)[tt, kk],
+                                 act=act, alpha=alpha, w_on_input=w_on_input)
         ic1[tt, kk], h[tt, kk], ic3[tt, kk] = a, b, c
     s = ic3[:, 0, :].copy()
     for k in range(1, K):
@@ -324,7 +367,7 @@ def moe_layer(x: np.ndarray, bank: dict, topk_w: np.ndarray, topk_ids: np.ndarra
     routed = bf16_round(s)
     out = {"ic1": ic1, "h": h, "ic3": ic3, "routed": routed, "out": routed}
     if shared is not None:
-        s1, sh, s3 = expert_forward(x, shared, 0, limit, None)
+        s1, sh, s3 = expert_forward(x, shared, 0, limit, None, act=act, alpha=alpha)
         out.update(shared_ic1=s1, shared_h=sh, shared_out=s3, out=bf16_round(routed + s3))
     return out
 

@@ -5,7 +5,8 @@ Run here, in the container that has the reference checkout (never on the GPU box
     python tests/golden/make_golden.py /path/to/reference
 
 Kernels executed (unmodified, imported from the reference tree):
-  * ``_fused_route_kernel`` via ``fused_route`` - overlay/freetoken/kernel/triton/fused_route.py
+  * ``_fused_route_kernel`` via ``fused_route`` (sigmoid and sqrtsoftplus scores) and
+    ``_fused_route_ext_kernel`` via ``fused_route_ranked`` - overlay/freetoken/kernel/triton/fused_route.py
   * ``_decode_nvfp4_marlin_swiglu_kernel`` - overlay/freetoken/kernel/triton/nvfp4_marlin_swiglu.py
     (the down GEMV with the activation folded in; same GEMV body as the gate_up kernel)
   * ``_e2m1_to_f32`` / ``_e2m1_to_bf16`` - the added lines of
@@ -158,6 +159,40 @@ def route_cases(fr) -> dict:
     return out
 
 
+def route_variant_cases(fr) -> dict:
+    """sqrt(softplus) scores through ``fused_route(..., act="sqrtsoftplus")`` and the ranked list
+    of ``fused_route_ranked`` (both from fused_route.py)."""
+    out = {}
+    g = torch.Generator().manual_seed(33)
+    for name, T, E, K, renorm, scaling, kind in [
+        ("sqrtsoftplus_e256_k8", 6, 256, 8, True, 2.5, None),
+        ("sqrtsoftplus_e64_k4_nan", 3, 64, 4, False, 1.0, "nan"),
+    ]:
+        lg = torch.randn(T, E, generator=g) * 3.0
+        bias = torch.randn(E, generator=g) * 0.1
+        if kind == "nan":
+            lg[0, 7] = float("nan")
+            lg[2, :] = float("nan")
+        w, ids = fr.fused_route(lg, bias, K, renorm, scaling, act="sqrtsoftplus")
+        out[name] = dict(logits=lg.numpy(), bias=bias.numpy(), top_k=K, renorm=int(renorm),
+                         scaling=np.float32(scaling), act="sqrtsoftplus", w=w.numpy(),
+                         ids=ids.numpy())
+    for name, T, E, K, NR, renorm, scaling, kind in [
+        ("ranked_e256_k8_r16", 5, 256, 8, 16, True, 2.5, None),
+        ("ranked_e64_k4_r12_nan", 3, 64, 4, 12, True, 1.0, "nan"),
+    ]:
+        lg = torch.randn(T, E, generator=g)
+        bias = torch.randn(E, generator=g) * 0.1
+        if kind == "nan":
+            lg[1, 3] = float("nan")
+            lg[2, :] = float("nan")
+        w, ids, rid, rsc = fr.fused_route_ranked(lg, bias, K, renorm, scaling, n_rank=NR)
+        out[name] = dict(logits=lg.numpy(), bias=bias.numpy(), top_k=K, n_rank=NR,
+                         renorm=int(renorm), scaling=np.float32(scaling), w=w.numpy(),
+                         ids=ids.numpy(), rank_ids=rid.numpy(), rank_scores=rsc.numpy())
+    return out
+
+
 def down_swiglu_cases(ms) -> dict:
     out = {}
     g = torch.Generator().manual_seed(22)
@@ -202,6 +237,8 @@ def main() -> None:
     np.savez_compressed(os.path.join(HERE, "e2m1_table.npz"), **e2m1_table())
     for name, d in route_cases(fr).items():
         np.savez_compressed(os.path.join(HERE, f"route_sigmoid_{name}.npz"), **d)
+    for name, d in route_variant_cases(fr).items():
+        np.savez_compressed(os.path.join(HERE, f"route_{name}.npz"), **d)
     for name, d in down_swiglu_cases(ms).items():
         np.savez_compressed(os.path.join(HERE, f"down_swiglu_{name}.npz"), **d)
     print("golden vectors written to", HERE)

@@ -19,10 +19,11 @@ def build_case(E, H, I, T, K, *, seed=0, shared=True, router_gemv=False, ids=Non
     return dict(bank=bank, shared=sh, inp=inp, w=w.astype(np.float32), ids=oid, K=K)
 
 
-def oracle_layer(case, limit=float("inf")):
+def oracle_layer(case, limit=float("inf"), **kw):
+    """The oracle's layer on a case; ``kw``: act, alpha, w_on_input (moe_oracle.moe_layer)."""
     x = case["inp"].x.float().numpy()
     sh = case["shared"].numpy() if case["shared"] is not None else None
-    return m.moe_layer(x, case["bank"].numpy(), case["w"], case["ids"], sh, limit)
+    return m.moe_layer(x, case["bank"].numpy(), case["w"], case["ids"], sh, limit, **kw)
 
 
 def to_f32(t: torch.Tensor) -> np.ndarray:

@@ -127,7 +127,7 @@ def test_decode_plan_rejects_what_decode_rejects():
 
 # Largest config-1 token count (with a shared expert) whose decode workspace fits the
 # allocation-free entry point's 16 MiB scratch.
-NOALLOC_MAX_T_CONFIG1 = 153
+NOALLOC_MAX_T_CONFIG1 = 122
 
 
 def test_noalloc_scratch_limit_host_only():

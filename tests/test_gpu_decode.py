@@ -167,6 +167,41 @@ def test_sigmoid_router_golden_on_gpu():
         assert np.abs(got[fin] - ref[fin]).max() <= 2e-6 * max(1.0, np.abs(ref[fin]).max())
 
 
+def _golden(pattern):
+    import glob
+    import os
+
+    return sorted(glob.glob(os.path.join(os.path.dirname(__file__), "golden", pattern)))
+
+
+@pytest.mark.parametrize("path", _golden("route_sqrtsoftplus_*.npz"))
+def test_sqrtsoftplus_router_golden_on_gpu(path):
+    d = np.load(path)
+    w, ids = ftb.fused_route(torch.from_numpy(d["logits"]).to(DEV),
+                             torch.from_numpy(d["bias"]).to(DEV), int(d["top_k"]),
+                             bool(d["renorm"]), float(d["scaling"]), act="sqrtsoftplus")
+    assert np.array_equal(ids.cpu().numpy(), d["ids"])
+    got, ref = w.cpu().numpy(), d["w"]
+    fin = np.isfinite(ref)
+    assert np.array_equal(np.isfinite(got), fin)
+    assert np.abs(got[fin] - ref[fin]).max(initial=0) <= 2e-6 * max(1.0, np.abs(ref[fin]).max())
+
+
+@pytest.mark.parametrize("path", _golden("route_ranked_*.npz"))
+def test_ranked_router_golden_on_gpu(path):
+    d = np.load(path)
+    w, ids, rid, rsc = ftb.fused_route_ranked(torch.from_numpy(d["logits"]).to(DEV),
+                                              torch.from_numpy(d["bias"]).to(DEV),
+                                              int(d["top_k"]), bool(d["renorm"]),
+                                              float(d["scaling"]), n_rank=int(d["n_rank"]))
+    assert np.array_equal(ids.cpu().numpy(), d["ids"])
+    assert np.array_equal(rid.cpu().numpy(), d["rank_ids"])
+    for got, ref in ((w.cpu().numpy(), d["w"]), (rsc.cpu().numpy(), d["rank_scores"])):
+        fin = np.isfinite(ref)
+        assert np.array_equal(np.isfinite(got), fin)
+        assert np.abs(got[fin] - ref[fin]).max(initial=0) <= 2e-6 * max(1.0, np.abs(ref[fin]).max())
+
+
 def test_softmax_router_ties_on_gpu():
     lg = torch.zeros(2, 256)
     lg[0, ::3] = 1.0

@@ -46,6 +46,31 @@ def test_sigmoid_router_bit_exact(path):
     assert np.array_equal(w.view(np.uint32), d["w"].view(np.uint32))
 
 
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLDEN, "route_sqrtsoftplus_*.npz"))))
+def test_sqrtsoftplus_router_matches_reference(path):
+    """The sqrt(softplus) score mode: ids bit-exact; weights within 2 ulp-scale (the
+    interpreter's exp/log are numpy's, the oracle's too, but the fused form rounds twice)."""
+    d = np.load(path)
+    w, ids = m.fused_route_sigmoid(d["logits"], d["bias"], int(d["top_k"]), bool(d["renorm"]),
+                                   float(d["scaling"]), act="sqrtsoftplus")
+    assert np.array_equal(ids, d["ids"])
+    fin = np.isfinite(d["w"])
+    assert np.array_equal(np.isfinite(w), fin)
+    assert np.abs(w[fin] - d["w"][fin]).max(initial=0) <= 2e-6 * max(1.0, np.abs(d["w"][fin]).max())
+
+
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLDEN, "route_ranked_*.npz"))))
+def test_ranked_router_bit_exact(path):
+    d = np.load(path)
+    w, ids, rid, rsc = m.fused_route_sigmoid(d["logits"], d["bias"], int(d["top_k"]),
+                                             bool(d["renorm"]), float(d["scaling"]),
+                                             n_rank=int(d["n_rank"]))
+    assert np.array_equal(ids, d["ids"]) and np.array_equal(rid, d["rank_ids"])
+    assert np.array_equal(rsc.view(np.uint32), d["rank_scores"].view(np.uint32))
+    assert np.array_equal(w.view(np.uint32), d["w"].view(np.uint32))
+    assert np.array_equal(rid[:, :int(d["top_k"])], ids)
+
+
 @pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLDEN, "down_swiglu_*.npz"))))
 def test_down_gemv_swiglu_bit_exact(path):
     """SwiGLU + down GEMV + global + routed weight, in the reference kernel's op order.

@@ -199,6 +199,7 @@ static int layer_impl(const ftb_moe_args& a, cudaStream_t stream) {
   sp.seg_cap = cap;
   sp.x_plain = prefill ? 1 : 0;
   sp.block_m = 0;
+  sp.route_major = !prefill && R <= kRouteMajorMaxRoutes && R <= E;
   sp.offsets = w.offsets;
   sp.sorted = w.sorted;
   sp.seg_expert = w.seg_expert;

@@ -5,13 +5,15 @@
 // call however many routes hit it (the reference's route-major grid re-reads them per route;
 // patches/moe_fused_nvfp4.patch:66, kernel_triton_nvfp4_fused_moe.patch:3-47).
 //
-// Work tile = RT weight rows (RT = 128 * G) of one segment (<= 16 routes of one expert),
-// full K. K is streamed in stages of 256 k; a stage holds, in shared memory:
+// Work tile = RT weight rows (96, 128 or 256) of one segment (<= 16 routes of one expert),
+// full K; 256-row tiles run one CTA per SM, 96- and 128-row tiles (small T) two. K is
+// streamed in stages of 256 k; a stage holds, in shared memory:
 //   packed rows  RT x 128 B   one or two 2D TMA boxes (cp.async.bulk.tensor, no multicast),
 //                             128-byte swizzled, so the A-fragment reads are conflict-free;
 //   scales       RT x 16 B    2D TMA boxes (E4M3, one per 16 k);
-//   activations  16 x 512 B   the segment's f16 rows for these 256 k (per-row bulk copies,
-//                             pitch 576 B), in the round-interleaved layout below.
+//   activations  XR x 512 B   the segment's f16 rows for these 256 k (per-row bulk copies,
+//                             pitch 576 B; XR = 8 when T <= 8, else 16), in the
+//                             round-interleaved layout below.
 // One producer warp claims tiles from a launch-wide counter and fills an S-stage ring
 // (mbarrier full/empty, bounded waits). Eight consumer warps all read every stage: warp w
 // owns G m16 tiles (16G rows) of the tile for the whole K and keeps their fp32 accumulators
@@ -37,7 +39,8 @@
 // gate_up: an m16 tile is 8 gate rows (m 0-7) + the same 8 up rows (m 8-15): after the last
 //   stage a lane holds gate and up of one (row, route) pair; epilogue ic1 = bf16(acc * 2^s *
 //   global), h = bf16(SwiGLU), written as f16 in the round-interleaved layout for down.
-// down: m16 tiles of 16 consecutive rows; epilogue ic3 = bf16(acc * global * w).
+// down: m16 tiles of 16 consecutive rows; epilogue ic3 = bf16(acc * global * w), where rows
+//   of h that were rescaled by 2^-c (h beyond the f16 range, see store_h) take w * 2^c.
 //
 // Waits are bounded (kSpinLimit polls). A timeout raises the CTA abort flag and
 // kStatusTimeout; consumers stop, and the producer drains its copies in flight before the
@@ -58,7 +61,6 @@ constexpr int kMaxStages = 8;
 constexpr int kSmemLimit = 227 * 1024;
 constexpr int kStageK = 256;               // k per stage (two 128-k rounds)
 constexpr int kXPitch = 576;               // bytes per activation row in a stage
-constexpr int kXRows = kSegRoutes;         // activation rows per stage (<= 2 n-tiles)
 constexpr int kHeader = 1024;              // barriers, tile ids, abort flag
 
 enum { kGateUp = 0, kDown = 1 };
@@ -78,16 +80,19 @@ struct Layout {
   int total;
 };
 
-// NW consumer warps x MT m16 tiles each: RT = 16 * NW * MT rows per tile.
-__host__ __device__ inline Layout make_layout(int MT, int NW) {
-  Layout L;
+// NW consumer warps x MT m16 tiles each: RT = 16 * NW * MT rows per tile. XR activation rows
+// per stage (8 when no segment can hold more than 8 routes, i.e. T <= 8; else kSegRoutes = 16)
+// and CPS CTAs per SM, which split the SM's shared memory.
+__host__ __device__ constexpr Layout make_layout(int MT, int NW, int XR, int CPS) {
+  Layout L{};
   L.RT = 16 * NW * MT;
   L.wbytes = L.RT * 128;
   L.sbytes = L.RT * 16;
   L.s_off = L.wbytes;
   L.x_off = L.s_off + L.sbytes;
-  L.stage_bytes = (L.x_off + kXRows * kXPitch + 1023) / 1024 * 1024;
-  int s = (kSmemLimit - kHeader) / L.stage_bytes;
+  L.stage_bytes = (L.x_off + XR * kXPitch + 1023) / 1024 * 1024;
+  const int limit = CPS == 1 ? kSmemLimit : 113 * 1024;
+  const int s = (limit - kHeader) / L.stage_bytes;
   L.stages = s > kMaxStages ? kMaxStages : s;
   L.total = kHeader + L.stages * L.stage_bytes;
   return L;
@@ -162,6 +167,7 @@ __device__ void producer(const DecodeParams& P, const GemvMaps& M, const Layout&
       e = P.seg_expert[a];
       off = P.seg_off[a];
       cnt = P.seg_cnt[a];
+      if (cnt == 0) continue;  // an empty segment (a skipped route of the route-major front)
       sh = (e == P.E);
       if (lane < cnt) {
         if (MODE == kGateUp) {
@@ -477,11 +483,11 @@ __device__ int64_t warp_tile(const DecodeParams& P, const Layout& L, uint8_t* st
   return i;
 }
 
-template <int MODE, int MT, int NW>
-__global__ void __launch_bounds__((NW + 1) * kWarp, 1)
+template <int MODE, int MT, int NW, int XR, int CPS>
+__global__ void __launch_bounds__((NW + 1) * kWarp, CPS)
     k_gemv_tma(const __grid_constant__ DecodeParams P, const __grid_constant__ GemvMaps M) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  const Layout L = make_layout(MT, NW);
+  constexpr Layout L = make_layout(MT, NW, XR, CPS);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + kMaxStages;
   int64_t* tile_of = reinterpret_cast<int64_t*>(empty + kMaxStages);
@@ -687,21 +693,43 @@ int make_maps(const DecodeParams& P, int RT, GemvMaps* M) {
   return st;
 }
 
-template <int MODE, int MT, int NW>
+template <int MODE, int MT, int NW, int XR, int CPS>
 int launch_one(const DecodeParams& P, int64_t est_tiles, cudaStream_t stream) {
-  const Layout L = make_layout(MT, NW);
-  if (L.stages < 2) return FTB_ERR_SHAPE;
+  constexpr Layout L = make_layout(MT, NW, XR, CPS);
+  static_assert(L.stages >= 2, "at least two stages per CTA");
   GemvMaps M;
   int st = make_maps<MODE>(P, L.RT, &M);
   if (st) return st;
-  cudaError_t err = cudaFuncSetAttribute(k_gemv_tma<MODE, MT, NW>,
+  cudaError_t err = cudaFuncSetAttribute(k_gemv_tma<MODE, MT, NW, XR, CPS>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, L.total);
   if (err != cudaSuccess) return cuda_status(err);
-  int64_t grid = sm_count();
+  int64_t grid = (int64_t)CPS * sm_count();
   if (est_tiles < grid) grid = est_tiles;
   if (grid < 1) grid = 1;
-  return cuda_status(launch_pdl(k_gemv_tma<MODE, MT, NW>, dim3((unsigned)grid),
+  return cuda_status(launch_pdl(k_gemv_tma<MODE, MT, NW, XR, CPS>, dim3((unsigned)grid),
                                 dim3((NW + 1) * kWarp), (size_t)L.total, stream, P, M));
+}
+
+// One launch of the chosen tile rows: 256-row tiles (16 consumer warps) one CTA per SM;
+// 96- and 128-row tiles two CTAs per SM (one wave more often at small T, twice the copies in
+// flight per SM); 8 activation rows per stage when T <= 8 (no segment holds more routes).
+template <int MODE>
+int launch_rows(const DecodeParams& P, int rows, int64_t max_seg, cudaStream_t stream) {
+  const int64_t per_e = MODE == kGateUp ? 2 * (int64_t)P.I : P.H;
+  const int64_t tiles = max_seg * (per_e / rows);
+  const bool x8 = P.T <= 8;
+  switch (rows) {
+    case 256: return launch_one<MODE, 1, 16, kSegRoutes, 1>(P, tiles, stream);
+    case 128:
+      return x8 ? launch_one<MODE, 1, 8, 8, 2>(P, tiles, stream)
+                : launch_one<MODE, 1, 8, kSegRoutes, 2>(P, tiles, stream);
+    case 96:
+      if constexpr (MODE == kGateUp)
+        return x8 ? launch_one<MODE, 1, 6, 8, 2>(P, tiles, stream)
+                  : launch_one<MODE, 1, 6, kSegRoutes, 2>(P, tiles, stream);
+      return FTB_ERR_SHAPE;
+    default: return FTB_ERR_SHAPE;
+  }
 }
 
 }  // namespace
@@ -735,21 +763,12 @@ int launch_decode_gemvs_tma(const DecodeParams& P, cudaStream_t stream) {
   if (P.H % 256 || P.I % 256) return FTB_ERR_SHAPE;
   const int64_t max_seg = max_segments(P.R, P.E, P.Ts, P.has_shared);
   const DecodePlan plan = decode_tile_plan(P.R, P.E, P.Ts, P.has_shared, P.H, P.I, sm_count());
-  int st;
   prof_mark(FTB_KERNEL_GATE_UP, true, stream);
-  if (plan.gate_up_rows == 256)
-    st = launch_one<kGateUp, 1, 16>(P, max_seg * (2 * P.I / 256), stream);
-  else if (plan.gate_up_rows == 96)
-    st = launch_one<kGateUp, 1, 6>(P, max_seg * (2 * P.I / 96), stream);
-  else
-    st = launch_one<kGateUp, 1, 8>(P, max_seg * (2 * P.I / 128), stream);
+  int st = launch_rows<kGateUp>(P, plan.gate_up_rows, max_seg, stream);
   prof_mark(FTB_KERNEL_GATE_UP, false, stream);
   if (st) return st;
   prof_mark(FTB_KERNEL_DOWN, true, stream);
-  if (plan.down_rows == 256)
-    st = launch_one<kDown, 1, 16>(P, max_seg * (P.H / 256), stream);
-  else
-    st = launch_one<kDown, 1, 8>(P, max_seg * (P.H / 128), stream);
+  st = launch_rows<kDown>(P, plan.down_rows, max_seg, stream);
   prof_mark(FTB_KERNEL_DOWN, false, stream);
   return st;
 }

@@ -24,6 +24,10 @@ constexpr int kCtlWords = 8;
 // Work segments hold at most this many routes of one expert (one pass of two mma n-tiles);
 // an expert with more routes is split into several segments.
 constexpr int kSegRoutes = 16;
+// Decode calls with at most this many routes skip the sort: each route is a one-route segment
+// (an expert hit twice is then streamed twice; at 32 routes over hundreds of experts that is
+// rare, and the sort's serial block-wide passes cost ~12 us).
+constexpr int64_t kRouteMajorMaxRoutes = 32;
 // Prefill (tensor-core) segments hold up to this many routes: the MMA's N (two accumulators
 // of this many fp32 columns and three 128-k A tiles share the 512 tensor-memory columns).
 constexpr int kPrefillSegRoutes = 160;
@@ -81,6 +85,8 @@ struct SortParams {
   int stage_tpb;       // tokens staged per block (1: the whole block per row; 32: a warp each),
                        // set by launch_sort_stage
   int block_m;         // > 0: also emit the padded (moe_align) outputs
+  int route_major;     // decode with few routes (R <= kRouteMajorMaxRoutes, R <= E): no sort,
+                       // every route is its own segment (see route_major_block)
   // outputs (decode segment table); seg_expert may be null
   int32_t* offsets;    // [E+1] unpadded, required
   int32_t* sorted;     // [R (+T)] route ids sorted by expert; shared routes appended as R+t

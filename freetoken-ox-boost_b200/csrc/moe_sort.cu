@@ -236,6 +236,40 @@ __device__ void sort_block(const SortParams& P, int* hist) {
     sort_block_t<1, false>(P, hist);
 }
 
+// Route-major front (P.route_major): the segment table without a sort. Segment r is route r
+// alone (expert ids[r], sorted position r; an invalid or masked route gets an empty segment,
+// which the GEMVs skip), then the shared expert's segments. A route's GEMV result does not
+// depend on the routes that share its tile, so the output is bit-identical to the sorted
+// layout's.
+__device__ void route_major_block(const SortParams& P) {
+  const int tid = threadIdx.x;
+  if (P.zero_words)
+    for (int64_t i = tid; i < P.n_zero; i += kSortThreads) P.zero_words[i] = 0;
+  __syncthreads();  // the status word is clear before a bad id is flagged in it
+  const int64_t R = P.R;
+  if (tid < R) {
+    int e = P.ids[tid];
+    bool ok = !(P.route_mask && P.route_mask[tid] == 0);
+    if (ok && (e < 0 || e >= P.E)) {
+      if (!(P.skip_neg && e < 0)) atomicOr(P.status, kStatusBadId);
+      ok = false;
+    }
+    P.seg_expert[tid] = ok ? e : 0;
+    P.seg_off[tid] = tid;
+    P.seg_cnt[tid] = ok ? 1 : 0;
+    P.sorted[tid] = tid;
+  }
+  const int64_t nsh = P.has_shared ? ceil_div(P.Ts, (int64_t)P.seg_cap) : 0;
+  if (tid < nsh) {
+    P.seg_expert[R + tid] = P.E;  // marker: the shared expert
+    P.seg_off[R + tid] = (int)(R + tid * P.seg_cap);
+    P.seg_cnt[R + tid] = (int)min((int64_t)P.seg_cap, P.Ts - tid * P.seg_cap);
+  }
+  if (P.has_shared)
+    for (int64_t t = tid; t < P.Ts; t += kSortThreads) P.sorted[R + t] = (int)(R + t);
+  if (tid == 0) *P.n_seg = (int)(R + nsh);
+}
+
 // Stages token t (x16 row t, xscale[t]) from the bf16 row `src` with the whole block (small T:
 // few tokens, each spread over all threads).
 __device__ void stage_token_block(const SortParams& P, int64_t t, const uint16_t* src) {
@@ -414,7 +448,10 @@ __global__ void __launch_bounds__(kSortThreads) k_sort_stage(SortParams P) {
   if (P.ep.world > 0) {
     ep_front(P, hist);
   } else if (blockIdx.x == 0) {
-    sort_block(P, hist);
+    if (P.route_major)
+      route_major_block(P);
+    else
+      sort_block(P, hist);
   } else if (P.stage_tpb == 1) {
     const int64_t t = (int64_t)blockIdx.x - 1;
     stage_token_block(P, t, P.x + t * P.H);
@@ -433,7 +470,7 @@ int launch_sort_stage(const SortParams& P0, cudaStream_t stream) {
   // beyond, a warp per token (T=4096: 128 staging blocks instead of 4096, no block barriers)
   SortParams P = P0;
   P.stage_tpb = P.T <= 2 * (int64_t)sm_count() ? 1 : kSortWarps;
-  const size_t smem = sort_smem_bytes(P.E);
+  const size_t smem = P.route_major ? 0 : sort_smem_bytes(P.E);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(k_sort_stage, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);

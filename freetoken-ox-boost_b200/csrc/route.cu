@@ -12,32 +12,20 @@
 namespace ftb {
 namespace {
 
-// A candidate: selection key, expert index (-1 = padding, loses to everything), and the
-// value its weight is made from (softmax: exp(logit - max); sigmoid: sigmoid(logit)).
-struct Cand {
-  float key;
-  int idx;
-  float val;
-};
-
-// a is selected before b: larger key; equal keys -> lower index; padding last.
-__device__ __forceinline__ bool before(const Cand& a, const Cand& b) {
-  if (a.idx < 0) return false;
-  if (b.idx < 0) return true;
-  return a.key > b.key || (a.key == b.key && a.idx < b.idx);
+// Selection order of the routers: larger key first, the lower expert index on equal keys (-0
+// and +0 equal). A candidate is one 64-bit word: the high half an order-preserving image of
+// the float key, the low half ~index, so "selected first" is "larger word", and 0 (padding)
+// loses to every expert, even one whose key is -inf.
+__device__ __forceinline__ uint64_t cand_word(float key, int idx) {
+  const uint32_t b = __float_as_uint(key + 0.0f);  // -0 -> +0
+  const uint32_t ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return ((uint64_t)ord << 32) | (uint32_t)~(uint32_t)idx;
 }
 
-__device__ __forceinline__ void cswap(Cand& a, Cand& b) {
-  if (before(b, a)) {
-    const Cand t = a;
-    a = b;
-    b = t;
-  }
-}
-
-// Sorts PER candidates (a power of two) in selection order: bitonic network in registers.
+// Sorts PER candidate words (a power of two) in descending order, carrying their values:
+// bitonic network in registers.
 template <int PER>
-__device__ __forceinline__ void sort_lane(Cand (&c)[PER]) {
+__device__ __forceinline__ void sort_lane(uint64_t (&c)[PER], float (&v)[PER]) {
 #pragma unroll
   for (int k = 2; k <= PER; k <<= 1)
 #pragma unroll
@@ -46,17 +34,24 @@ __device__ __forceinline__ void sort_lane(Cand (&c)[PER]) {
       for (int i = 0; i < PER; ++i) {
         const int l = i ^ j;
         if (l > i) {
-          if ((i & k) == 0)
-            cswap(c[i], c[l]);
-          else
-            cswap(c[l], c[i]);
+          const bool desc = (i & k) == 0;
+          const bool swap = desc ? (c[l] > c[i]) : (c[i] > c[l]);
+          if (swap) {
+            const uint64_t tc = c[i];
+            c[i] = c[l];
+            c[l] = tc;
+            const float tv = v[i];
+            v[i] = v[l];
+            v[l] = tv;
+          }
         }
       }
 }
 
 // One warp per token; lane l holds experts l, l+32, ..., sorted in selection order. Each of
-// the top_k rounds takes the warp-wide best of the lanes' heads (shuffle argmax with the
-// same order) and the winning lane pops its head.
+// the top_k rounds finds the warp's best head with two redux.sync max reductions (key image,
+// then ~index among the lanes holding the best key), and the owning lane (index mod 32) pops
+// its head and broadcasts its value. Ids and weights are kept in lane k and stored at the end.
 // n_rank > 0 (sigmoid-family modes): the selection continues to n_rank rounds and writes the
 // ranked list (rank_ids, rank_sc: the raw score, 0 for NaN) beside the top_k routing result.
 template <int PER>
@@ -73,12 +68,14 @@ __global__ void __launch_bounds__(128) k_route_topk(const float* __restrict__ lo
   const int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (t >= T) return;
   const float* row = logits + t * E;
-  Cand c[PER];
+  uint64_t c[PER];
+  float val[PER];
   float m = -INFINITY;
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
     const int e = lane + 32 * i;
-    c[i] = Cand{-INFINITY, -1, 0.f};
+    c[i] = 0;
+    val[i] = 0.f;
     if (e < E) {
       const float l = row[e];
       if (mode != FTB_ROUTE_SOFTMAX) {
@@ -89,9 +86,11 @@ __global__ void __launch_bounds__(128) k_route_topk(const float* __restrict__ lo
                             : 1.0f / (1.0f + expf(-l));
         float k = s + (bias ? bias[e] : 0.f);
         if (k != k) k = -3.4028234663852886e38f;  // NaN -> -FLT_MAX
-        c[i] = Cand{k, e, s};
+        c[i] = cand_word(k, e);
+        val[i] = s;
       } else {
-        c[i] = Cand{(l != l) ? -INFINITY : l, e, l};
+        c[i] = cand_word((l != l) ? -INFINITY : l, e);
+        val[i] = l;
         m = fmaxf(m, l);
       }
     }
@@ -103,43 +102,38 @@ __global__ void __launch_bounds__(128) k_route_topk(const float* __restrict__ lo
     float s = 0.f;
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
-      if (c[i].idx >= 0) {
-        c[i].val = expf(c[i].val - m);
-        s += c[i].val;
+      if (lane + 32 * i < E) {
+        val[i] = expf(val[i] - m);
+        s += val[i];
       }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     denom = s;
   }
-  sort_lane<PER>(c);
+  sort_lane<PER>(c, val);
   float wsum = 0.f;
-  float wk = 0.f;  // this lane keeps the weight of selection k == lane
+  float wk = 0.f;  // lane k keeps the weight and id of selection k
+  int idk = 0;
   const int rounds = n_rank > top_k ? n_rank : top_k;
   for (int k = 0; k < rounds; ++k) {
-    Cand b = c[0];
-    int src = lane;
+    const uint32_t hi = (uint32_t)(c[0] >> 32), lo = (uint32_t)c[0];
+    const uint32_t mhi = __reduce_max_sync(0xffffffffu, hi);
+    const uint32_t mlo = __reduce_max_sync(0xffffffffu, hi == mhi ? lo : 0u);
+    const int win = (int)~mlo;  // the selected expert (every lane agrees)
+    const int owner = win & 31;
+    const float bval = __shfl_sync(0xffffffffu, val[0], owner);
+    if (lane == owner) {
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      Cand o_c;
-      o_c.key = __shfl_xor_sync(0xffffffffu, b.key, o);
-      o_c.idx = __shfl_xor_sync(0xffffffffu, b.idx, o);
-      o_c.val = __shfl_xor_sync(0xffffffffu, b.val, o);
-      const int o_src = __shfl_xor_sync(0xffffffffu, src, o);
-      if (before(o_c, b)) {
-        b = o_c;
-        src = o_src;
+      for (int i = 0; i + 1 < PER; ++i) {
+        c[i] = c[i + 1];
+        val[i] = val[i + 1];
       }
+      c[PER - 1] = 0;
     }
-    // every lane agrees on b (a total order); the owner pops its head
-    if (lane == src) {
-#pragma unroll
-      for (int i = 0; i + 1 < PER; ++i) c[i] = c[i + 1];
-      c[PER - 1] = Cand{-INFINITY, -1, 0.f};
-    }
-    // no candidate left (top_k > experts cannot reach here: checked on the host)
-    const int idx = b.idx < 0 ? 0 : (b.idx > E - 1 ? E - 1 : b.idx);
-    float v = b.val;
+    // no candidate left cannot happen (top_k, n_rank <= E: checked on the host)
+    const int idx = win < 0 ? 0 : (win > E - 1 ? E - 1 : win);
+    float v = bval;
     if (mode == FTB_ROUTE_SOFTMAX) v = v / denom;
     if (k < n_rank && lane == 0) {
       rank_ids[t * n_rank + k] = idx;
@@ -147,8 +141,10 @@ __global__ void __launch_bounds__(128) k_route_topk(const float* __restrict__ lo
     }
     if (k >= top_k) continue;
     wsum += v;
-    if (lane == k) wk = v;
-    if (lane == 0) id_out[t * top_k + k] = idx;
+    if (lane == k) {
+      wk = v;
+      idk = idx;
+    }
   }
   if (lane < top_k) {
     float v = wk;
@@ -159,6 +155,7 @@ __global__ void __launch_bounds__(128) k_route_topk(const float* __restrict__ lo
       v = v * scaling;
     }
     w_out[t * top_k + lane] = v;
+    id_out[t * top_k + lane] = idk;
   }
 }
 

@@ -34,12 +34,14 @@ struct DecodeWs {
   uint16_t* ic3;
   uint16_t* ic3s;
   __half* xs;  // prefill only
+  uint8_t *q4x, *q4x_sf, *q4h, *q4h_sf;  // FP4 prefill only
+  float *q4x_g, *q4h_g;
   size_t bytes;
 };
 
 // Workspace of one decode (cap = kSegRoutes) or prefill (cap = kPrefillSegRoutes) call.
 DecodeWs carve_decode(void* ws, int64_t T, int H, int I, int64_t E, int top_k, int has_shared,
-                      int cap = kSegRoutes) {
+                      int cap = kSegRoutes, bool fp4 = false) {
   const int64_t R = T * top_k;
   const int64_t Rs = R + (has_shared ? T : 0);
   Carver c(ws);
@@ -60,7 +62,17 @@ DecodeWs carve_decode(void* ws, int64_t T, int H, int I, int64_t E, int top_k, i
   w.h16 = c.take<__half>(Rs * I);
   w.ic3 = c.take<uint16_t>(R * H);
   w.ic3s = c.take<uint16_t>(has_shared ? T * H : 1);
-  w.xs = cap == kPrefillSegRoutes ? c.take<__half>(Rs * H) : nullptr;
+  w.xs = cap == kPrefillSegRoutes && !fp4 ? c.take<__half>(Rs * H) : nullptr;
+  w.q4x = w.q4x_sf = w.q4h = w.q4h_sf = nullptr;
+  w.q4x_g = w.q4h_g = nullptr;
+  if (fp4) {
+    w.q4x = c.take<uint8_t>(Rs * H / 2);
+    w.q4x_sf = c.take<uint8_t>(Rs * H / 16);
+    w.q4x_g = c.take<float>(Rs);
+    w.q4h = c.take<uint8_t>(Rs * I / 2);
+    w.q4h_sf = c.take<uint8_t>(Rs * I / 16);
+    w.q4h_g = c.take<float>(Rs);
+  }
   w.bytes = c.off;
   return w;
 }
@@ -154,8 +166,9 @@ int sm_count() {
 // route_mask / phase: one phase of the split decode (routes with mask 0 are not computed; the
 // shared expert only with FTB_PHASE_SHARED; the combine only with FTB_PHASE_COMBINE).
 static int layer_impl(const ftb_moe_args& a, cudaStream_t stream) {
-  const bool prefill = a.path == FTB_PATH_PREFILL;
-  if (a.path != FTB_PATH_DECODE && a.path != FTB_PATH_PREFILL) return FTB_ERR_ARG;
+  const bool fp4 = a.path == FTB_PATH_PREFILL_FP4;
+  const bool prefill = a.path == FTB_PATH_PREFILL || fp4;
+  if (a.path != FTB_PATH_DECODE && a.path != FTB_PATH_PREFILL && !fp4) return FTB_ERR_ARG;
   if (a.activation != FTB_ACT_SILU && a.activation != FTB_ACT_SWIGLU_CLAMP &&
       a.activation != FTB_ACT_SWIGLUOAI)
     return FTB_ERR_ARG;
@@ -168,6 +181,7 @@ static int layer_impl(const ftb_moe_args& a, cudaStream_t stream) {
   const int64_t E = bank->num_experts;
   if (layer_shape_status(T, H, I, E, top_k) != FTB_OK || (shared && shared->num_experts < 1))
     return FTB_ERR_SHAPE;
+  if (fp4 && !prefill_fp4_shape_ok(H, I)) return FTB_ERR_SHAPE;
   const int phase = a.route_mask ? a.phase : (FTB_PHASE_SHARED | FTB_PHASE_COMBINE);
   if (phase & ~(FTB_PHASE_SHARED | FTB_PHASE_COMBINE)) return FTB_ERR_ARG;
   const bool combine = (phase & FTB_PHASE_COMBINE) != 0;
@@ -178,10 +192,10 @@ static int layer_impl(const ftb_moe_args& a, cudaStream_t stream) {
   // this call computes the shared expert's rows (the combine adds them whenever shared != 0)
   const int run_shared = has_shared && (phase & FTB_PHASE_SHARED) ? 1 : 0;
   const int cap = prefill ? kPrefillSegRoutes : kSegRoutes;
-  const DecodeWs need = carve_decode(nullptr, T, H, I, E, top_k, has_shared, cap);
+  const DecodeWs need = carve_decode(nullptr, T, H, I, E, top_k, has_shared, cap, fp4);
   if (!a.workspace || a.workspace_bytes < need.bytes) return FTB_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(a.workspace) & 255u) != 0) return FTB_ERR_ALIGN;
-  const DecodeWs w = carve_decode(a.workspace, T, H, I, E, top_k, has_shared, cap);
+  const DecodeWs w = carve_decode(a.workspace, T, H, I, E, top_k, has_shared, cap, fp4);
   const int64_t R = T * top_k;
   const int64_t Rs = R + (has_shared ? T : 0);
 
@@ -208,7 +222,7 @@ static int layer_impl(const ftb_moe_args& a, cudaStream_t stream) {
   sp.n_seg = w.n_seg;
   sp.status = w.status;
   sp.x = a.x;
-  sp.x16 = w.x16;
+  sp.x16 = fp4 ? nullptr : w.x16;  // the FP4 path quantises x itself
   sp.xscale = w.xscale;
   sp.H = H;
   int st = launch_sort_stage(sp, stream);
@@ -247,12 +261,21 @@ static int layer_impl(const ftb_moe_args& a, cudaStream_t stream) {
   dp.hcount = w.status + kCtlHCount;
   dp.gu_done = w.status + kCtlGuDone;
   dp.hb = w.hb;
+  dp.x_in = a.x;
+  dp.q4x = w.q4x;
+  dp.q4x_sf = w.q4x_sf;
+  dp.q4x_g = w.q4x_g;
+  dp.q4h = w.q4h;
+  dp.q4h_sf = w.q4h_sf;
+  dp.q4h_g = w.q4h_g;
   dp.dbg_ic1 = a.ic1;
   dp.dbg_h = a.h;
   dp.dbg_sic1 = a.shared_ic1;
   dp.dbg_sh = a.shared_h;
   dp.has_shared = has_shared;
-  if (prefill)
+  if (fp4)
+    st = launch_prefill_fp4(dp, stream);
+  else if (prefill)
     st = launch_prefill_gemms(dp, stream);
   else
     st = launch_decode_gemvs_tma(dp, stream);
@@ -467,6 +490,20 @@ int ftb_moe_decode_plan(int64_t T, int H, int I, int E, int top_k, int has_share
 size_t ftb_moe_prefill_workspace_bytes(int64_t T, int H, int I, int E, int top_k,
                                        int has_shared) {
   return carve_decode(nullptr, T, H, I, E, top_k, has_shared, kPrefillSegRoutes).bytes;
+}
+
+size_t ftb_moe_prefill_fp4_workspace_bytes(int64_t T, int H, int I, int E, int top_k,
+                                           int has_shared) {
+  return carve_decode(nullptr, T, H, I, E, top_k, has_shared, kPrefillSegRoutes, true).bytes;
+}
+
+int ftb_quant_nvfp4(const uint16_t* x, int is_bf16, int64_t rows, int K, uint8_t* q,
+                    uint8_t* sf, float* g, ftb_stream_t stream) {
+  if (rows < 0 || K < 512 || K % 512 || K > 4096) return FTB_ERR_SHAPE;
+  if (rows == 0) return FTB_OK;
+  if (!x || !q || !sf || !g) return FTB_ERR_ARG;
+  if (!aligned16(x) || (reinterpret_cast<uintptr_t>(q) & 7u)) return FTB_ERR_ALIGN;
+  return launch_quant_nvfp4(x, is_bf16, rows, K, q, sf, g, (cudaStream_t)stream);
 }
 
 int ftb_moe_layer(const ftb_moe_args* args, ftb_stream_t stream) {

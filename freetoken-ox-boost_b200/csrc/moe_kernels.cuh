@@ -156,6 +156,14 @@ struct DecodeParams {
   int32_t* hcount;         // entries of hlist (zeroed per call)
   int32_t* gu_done;        // gate_up CTAs finished (zeroed per call)
   uint16_t* hb;            // [R + Ts, I] bf16 h of the elements beyond the f16 range
+  // FP4 prefill (FTB_PATH_PREFILL_FP4): NVFP4 activation rows in sorted order
+  const uint16_t* x_in;    // [T, H] bf16 layer input
+  uint8_t* q4x;            // [R + Ts, H/2] e2m1 codes of x
+  uint8_t* q4x_sf;         // [R + Ts, H/16] E4M3 scales
+  float* q4x_g;            // [R + Ts] per-row globals
+  uint8_t* q4h;            // [R + Ts, I/2] e2m1 codes of h
+  uint8_t* q4h_sf;         // [R + Ts, I/16]
+  float* q4h_g;            // [R + Ts]
   // optional debug copies (route order)
   uint16_t* dbg_ic1;       // [R, 2I]
   uint16_t* dbg_h;         // [R, I]
@@ -284,6 +292,12 @@ inline int layer_shape_status(int64_t T, int H, int I, int64_t E, int top_k) {
 int launch_decode_gemvs_tma(const DecodeParams& P, cudaStream_t stream);
 // Tensor-core grouped GEMMs for prefill (moe_prefill.cu): segments of <= kPrefillSegRoutes.
 int launch_prefill_gemms(const DecodeParams& P, cudaStream_t stream);
+// Block-scaled FP4 prefill (moe_prefill_fp4.cu): quantise x, gate_up, quantise h, down.
+bool prefill_fp4_shape_ok(int H, int I);
+int launch_prefill_fp4(const DecodeParams& P, cudaStream_t stream);
+// Rows of bf16 (is_bf16) or f16 values -> NVFP4 codes, E4M3 scales and per-row globals.
+int launch_quant_nvfp4(const uint16_t* x, int is_bf16, int64_t rows, int K, uint8_t* q,
+                       uint8_t* sf, float* g, cudaStream_t stream);
 int launch_combine(const DecodeParams& P, cudaStream_t stream);
 
 // Measurement hook (ftb_profile_begin/end): records an event on `stream` before (start=true)

@@ -58,6 +58,7 @@ FTB_ACT_SWIGLU_CLAMP = 1
 FTB_ACT_SWIGLUOAI = 2
 FTB_PATH_DECODE = 0
 FTB_PATH_PREFILL = 1
+FTB_PATH_PREFILL_FP4 = 2
 
 
 class MoeArgsStruct(ctypes.Structure):
@@ -85,6 +86,8 @@ SIGNATURES = {
     "ftb_moe_decode_workspace_bytes": (_sz, [_i64, _i32, _i32, _i32, _i32, _i32]),
     "ftb_moe_decode": (_i32, [_vp, _BP, _BP, _vp, _vp, _i64, _i32, _i32, _i32, _f32, _vp, _vp,
                               _sz, _vp]),
+    "ftb_moe_prefill_fp4_workspace_bytes": (_sz, [_i64, _i32, _i32, _i32, _i32, _i32]),
+    "ftb_quant_nvfp4": (_i32, [_vp, _i32, _i64, _i32, _vp, _vp, _vp, _vp]),
     "ftb_moe_layer": (_i32, [ctypes.POINTER(MoeArgsStruct), _vp]),
     "ftb_moe_decode_plan": (_i32, [_i64, _i32, _i32, _i32, _i32, _i32, _vp]),
     "ftb_moe_decode_debug": (_i32, [_vp, _BP, _BP, _vp, _vp, _i64, _i32, _i32, _i32, _f32, _vp,
@@ -115,7 +118,7 @@ SIGNATURES = {
 }
 
 KERNEL_NAMES = {0: "sort_stage", 1: "gate_up_gemv", 2: "down_gemv", 3: "combine", 4: "route_topk",
-                5: "ep_publish", 6: "ep_combine", 7: "permute_rows"}
+                5: "ep_publish", 6: "ep_combine", 7: "permute_rows", 8: "quant_h"}
 
 
 class FtbLibraryError(RuntimeError):

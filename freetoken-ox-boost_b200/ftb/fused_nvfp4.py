@@ -107,6 +107,41 @@ def moe_prefill(x: torch.Tensor, bank: Nvfp4Bank, topk_weights: torch.Tensor,
                   act_limit, apply_router_weight_on_input, shared, out, debug, check_status)
 
 
+def prefill_fp4_workspace_bytes(T: int, bank: Nvfp4Bank, top_k: int, has_shared: bool) -> int:
+    return int(_lib.load().ftb_moe_prefill_fp4_workspace_bytes(
+        T, bank.hidden, bank.inter, bank.num_experts, top_k, 1 if has_shared else 0))
+
+
+def moe_prefill_fp4(x: torch.Tensor, bank: Nvfp4Bank, topk_weights: torch.Tensor,
+                    topk_ids: torch.Tensor, *, activation: str = "silu", act_limit: float = 7.0,
+                    act_alpha: float = 1.702, apply_router_weight_on_input: bool = False,
+                    shared: Nvfp4Bank | None = None, out: torch.Tensor | None = None,
+                    debug: bool = False, check_status: bool = False):
+    """Opt-in prefill on the block-scaled FP4 tensor cores (tcgen05 kind::mxf4nvf4): x and h are
+    quantised to NVFP4 (``quant_nvfp4``'s rule) before each GEMM. NOT parity-preserving: the
+    reference keeps activations in bf16, and its error against that arithmetic is ~1e-1
+    (max|d|/max|ref|), not the 1e-2 bar. Needs hidden and inter multiples of 512, <= 4096."""
+    return _layer(_lib.FTB_PATH_PREFILL_FP4, x, bank, topk_weights, topk_ids, activation,
+                  act_alpha, act_limit, apply_router_weight_on_input, shared, out, debug,
+                  check_status)
+
+
+def quant_nvfp4(x: torch.Tensor):
+    """Rows of bf16 / f16 values -> (codes uint8 [rows, K/2], E4M3 scales uint8 [rows, K/16],
+    globals fp32 [rows]): g = amax/2688, s = e4m3((amax_block/g)/6), code = e2m1(v*(1/(s*g)))."""
+    dev = require_cuda(x)
+    if x.dtype not in (torch.bfloat16, torch.float16) or x.dim() != 2 or not x.is_contiguous():
+        raise ValueError("x must be a contiguous [rows, K] bf16 or f16 tensor")
+    rows, K = x.shape
+    q = torch.empty(rows, K // 2, dtype=torch.uint8, device=dev)
+    sf = torch.empty(rows, K // 16, dtype=torch.uint8, device=dev)
+    g = torch.empty(rows, dtype=torch.float32, device=dev)
+    st = _lib.load().ftb_quant_nvfp4(ptr(x), 1 if x.dtype == torch.bfloat16 else 0, rows, K,
+                                     ptr(q), ptr(sf), ptr(g), stream_handle(dev))
+    _lib.check("ftb_quant_nvfp4", st)
+    return q, sf, g
+
+
 def _layer(path: int, x, bank, topk_weights, topk_ids, activation, act_alpha, act_limit,
            weight_on_input, shared, out, debug, check_status, route_mask=None, phase=0,
            ws=None):
@@ -119,8 +154,9 @@ def _layer(path: int, x, bank, topk_weights, topk_ids, activation, act_alpha, ac
         out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
     lib = _lib.load()
     if ws is None:
-        wsb = (prefill_workspace_bytes if path == _lib.FTB_PATH_PREFILL else
-               decode_workspace_bytes)(T, bank, K, shared is not None)
+        wsb = {_lib.FTB_PATH_PREFILL: prefill_workspace_bytes,
+               _lib.FTB_PATH_PREFILL_FP4: prefill_fp4_workspace_bytes}.get(
+            path, decode_workspace_bytes)(T, bank, K, shared is not None)
         ws = workspace(wsb, dev)
     b = bank.struct()
     s = shared.struct() if shared is not None else None

@@ -158,14 +158,19 @@ FTB_API int ftb_moe_decode(const uint16_t* x, const ftb_nvfp4_bank* bank, const 
  *   weight_on_input  apply_router_weight_on_input: the routed weight multiplies the gate_up
  *               output (ic1 = bf16(acc * global * w)) and not the down output, as the
  *               reference's MUL_ROUTED_WEIGHT flags do (patches/moe_fused_nvfp4.patch:138,145).
- *   path        FTB_PATH_DECODE (HBM-streaming GEMVs, ftb_moe_decode_workspace_bytes()) or
- *               FTB_PATH_PREFILL (tensor-core GEMMs, ftb_moe_prefill_workspace_bytes()).
+ *   path        FTB_PATH_DECODE (HBM-streaming GEMVs, ftb_moe_decode_workspace_bytes()),
+ *               FTB_PATH_PREFILL (tensor-core GEMMs, ftb_moe_prefill_workspace_bytes()) or
+ *               FTB_PATH_PREFILL_FP4: an opt-in that is NOT parity-preserving (no counterpart in
+ *               the reference, whose prefill keeps activations in bf16): x and h are quantised
+ *               to NVFP4 (ftb_quant_nvfp4's rule) and both GEMMs run on the block-scaled FP4
+ *               tensor cores (tcgen05 kind::mxf4nvf4); H % 512 == 0, I % 512 == 0, H, I <= 4096;
+ *               ftb_moe_prefill_fp4_workspace_bytes().
  *   route_mask, phase  NULL, or one phase of the split decode as ftb_moe_decode_phase()
  *               (decode path only).
  *   ic1 .. shared_out  debug copies of the intermediates as ftb_moe_decode_debug(), or NULL.
  */
 enum { FTB_ACT_SILU = 0, FTB_ACT_SWIGLU_CLAMP = 1, FTB_ACT_SWIGLUOAI = 2 };
-enum { FTB_PATH_DECODE = 0, FTB_PATH_PREFILL = 1 };
+enum { FTB_PATH_DECODE = 0, FTB_PATH_PREFILL = 1, FTB_PATH_PREFILL_FP4 = 2 };
 typedef struct ftb_moe_args {
   const uint16_t* x;             /* [T, H] bf16 */
   const ftb_nvfp4_bank* bank;    /* routed experts */
@@ -192,6 +197,20 @@ typedef struct ftb_moe_args {
   uint16_t* shared_out;
 } ftb_moe_args;
 FTB_API int ftb_moe_layer(const ftb_moe_args* args, ftb_stream_t stream);
+
+FTB_API size_t ftb_moe_prefill_fp4_workspace_bytes(int64_t T, int H, int I, int E, int top_k,
+                                                   int has_shared);
+
+/*
+ * Rows of activations -> NVFP4, the quantisation the FP4 prefill applies to x and h (no
+ * counterpart in the reference). x [rows, K] bf16 (is_bf16 != 0) or f16; per row:
+ * g = amax / 2688 (1 for an all-zero row), per 16-element block s = e4m3_rn((amax_b / g) / 6),
+ * codes e2m1_rn(v * (1 / (s * g))) (0 where s == 0), all fp32 ops rounded to nearest:
+ * q [rows, K/2] (low nibble = even element), sf [rows, K/16] (E4M3 bits), g [rows] fp32.
+ * K % 512 == 0, 512 <= K <= 4096.
+ */
+FTB_API int ftb_quant_nvfp4(const uint16_t* x, int is_bf16, int64_t rows, int K, uint8_t* q,
+                            uint8_t* sf, float* g, ftb_stream_t stream);
 
 /*
  * Host-only query (launches nothing): the work-tile rows the decode GEMVs of a call with this
@@ -346,7 +365,8 @@ enum {
   FTB_KERNEL_ROUTE = 4,
   FTB_KERNEL_EP_PUBLISH = 5,
   FTB_KERNEL_EP_COMBINE = 6,
-  FTB_KERNEL_PERMUTE = 7
+  FTB_KERNEL_PERMUTE = 7,   /* prefill: permute x rows; FP4 prefill: quantise x rows */
+  FTB_KERNEL_QUANT_H = 8    /* FP4 prefill: quantise h rows */
 };
 FTB_API int ftb_profile_begin(void);
 FTB_API int ftb_profile_end(int32_t* kernel_ids, float* ms, int max_n);

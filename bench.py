@@ -424,6 +424,7 @@ def run_ftb_single(args, torch):
         out["decode_sweep"] = sweep_decode(torch, ftb, layers, args)
     if not args.no_prefill:
         out["prefill"] = bench_prefill(torch, ftb, layers, args)
+        out["prefill_fp4"] = bench_prefill_fp4(torch, ftb, layers, args)
     if not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(torch, layers, args.cpu_seconds)
     return out
@@ -542,6 +543,68 @@ def bench_prefill(torch, ftb, layers: "Layers", args):
         "e2e": {"value": round(T / e2e_dt, 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": T * H * 2 + T * E * 4, "d2h_bytes_per_step": T * H * 2},
         "gpu_launches_per_step": 6,  # route_topk, sort, permute, gate_up, down, combine
+        "clocks": clk,
+    }
+
+
+FP4_DENSE_PEAK_TFLOPS = 9000.0  # nominal dense FP4 per B200 (NVIDIA's 18 PF figure is 2:4 sparse)
+
+
+def bench_prefill_fp4(torch, ftb, layers: "Layers", args):
+    """The opt-in FP4 prefill (ftb.moe_prefill_fp4: x and h quantised to NVFP4, both GEMMs on
+    tcgen05 kind::mxf4nvf4) on the config 2 workload, beside the parity path. Not a parity
+    number: its distance from the bf16-activation result on the same inputs is reported. Two
+    bounds apply: FP4 tensor rate (nominal 9 PFLOP/s dense; no measured FP4 figure exists for
+    this pool) and HBM (the weights every step streams, at the measured copy rate)."""
+    from ftb import _lib, synth
+
+    T = args.prefill_tokens
+    nl = len(layers.banks)
+    inps = [synth.make_inputs(T, H, E, seed=3000 + l, device="cuda") for l in range(nl)]
+    outs = [torch.empty(T, H, dtype=torch.bfloat16, device="cuda") for _ in range(nl)]
+    routes = [ftb.fused_topk(None, inp.logits, TOPK, True) for inp in inps]
+
+    def step(i):
+        l = i % nl
+        w, ids = ftb.fused_topk(None, inps[l].logits, TOPK, True)
+        ftb.moe_prefill_fp4(inps[l].x, layers.banks[l], w, ids, shared=layers.shared[l],
+                            out=outs[l])
+
+    for i in range(max(3, args.warmup)):
+        step(i)
+    steps = min(max(8, args.steps // 4), 60)
+    clocks = ClockSampler(torch, 0)
+    clocks.start()
+    ms = time_steps(torch, step, steps)
+    clk = clocks.stop()
+    kt = kernel_times(_lib, torch, step, 8)
+    rows = T * (TOPK + 1)
+    flops = {"gate_up_gemv": 2.0 * rows * 2 * I * H, "down_gemv": 2.0 * rows * H * I}
+    gemm_ms = sum(statistics.mean(kt[k]) for k in flops)
+    ach = sum(flops.values()) / (gemm_ms * 1e-3) / 1e12
+    hbm, hbm_src = measured_peaks()
+    w_bytes = (statistics.mean(
+        int(torch.unique(r[1]).numel()) for r in routes) + 1) * ftb.bank_bytes_per_expert(H, I)
+    hbm_ms = w_bytes / (hbm * 1e9) * 1e3
+    # error against the parity path (bf16 activations) on layer 0's inputs
+    w0, ids0 = routes[0]
+    ref = ftb.moe_prefill(inps[0].x, layers.banks[0], w0, ids0, shared=layers.shared[0])
+    got = ftb.moe_prefill_fp4(inps[0].x, layers.banks[0], w0, ids0, shared=layers.shared[0])
+    err = float((got.float() - ref.float()).abs().max() / ref.float().abs().max())
+    return {
+        "workload": f"config 2 prefill T={T} as 'prefill', opt-in NVFP4 activations",
+        "parity": "not parity-preserving (activations quantised to NVFP4)",
+        "max_abs_rel_vs_parity_path": round(err, 4),
+        "tokens_per_s": round(T * 1e3 / ms, 1), "ms_per_step": round(ms, 4), "steps": steps,
+        "kernels_ms": {k: round(statistics.mean(v), 4) for k, v in kt.items()},
+        "roofline": {"kernel": "gate_up + down (k_prefill_fp4<0>, <1>), tcgen05 kind::mxf4nvf4",
+                     "bound": "tensor", "achieved": round(ach, 1), "peak": FP4_DENSE_PEAK_TFLOPS,
+                     "unit": "TFLOP/s", "frac": round(ach / FP4_DENSE_PEAK_TFLOPS, 4),
+                     "peak_source": "nominal dense FP4 (9 PFLOP/s per B200), not measured here",
+                     "hbm_bound_ms": round(hbm_ms, 4),
+                     "frac_of_hbm_bound": round(hbm_ms / gemm_ms, 4),
+                     "hbm_peak_source": hbm_src},
+        "gpu_launches_per_step": 7,  # route, sort, quant x, gate_up, quant h, down, combine
         "clocks": clk,
     }
 

@@ -580,7 +580,7 @@ __device__ __forceinline__ void meta_routes(const DecodeParams& P, const Item& i
 
 template <int MODE>
 __device__ __forceinline__ void meta_factors(const DecodeParams& P, const Item& im, int lane,
-                                             Meta& m) {
+                                             bool any_shift, Meta& m) {
 #pragma unroll
   for (int k = 0; k < kMetaK; ++k) {
     const int r = m.r[k];
@@ -592,7 +592,7 @@ __device__ __forceinline__ void meta_factors(const DecodeParams& P, const Item& 
         // routed weight (unless it went on the input) times the row's h shift 2^c (a power of
         // two commutes with the rounding: (acc g) (w 2^c) == ((acc 2^c) g) w)
         if (!im.sh && !P.w_on_input) f = P.topk_w[r];
-        f *= pow2i(P.hshift[im.off + lane + kWarp * k]);
+        if (any_shift) f *= pow2i(P.hshift[im.off + lane + kWarp * k]);
       }
     }
     m.f[k] = f;
@@ -632,11 +632,14 @@ __device__ void pf_epilogue(const DecodeParams& P, const PfSync& sy, int64_t n_i
   int64_t di = 0;
   Meta nx;
   int64_t it = blockIdx.x / kPair;
+  // down: the gate_up launch (complete before this one's dependency wait) shifted some rows of
+  // h iff it listed any; without, every shift is 0 and its loads are skipped
+  const bool any_shift = MODE == kDown && __ldcg(P.hcount) > 0;
   Item im{};
   if (it < n_items) {
     im = item_of<MODE>(P, it, mpairs, sy.rank);
     meta_routes(P, im, lane, nx);
-    meta_factors<MODE>(P, im, lane, nx);
+    meta_factors<MODE>(P, im, lane, any_shift, nx);
   }
   for (; it < n_items; it += gridDim.x / kPair) {
 #pragma unroll
@@ -655,7 +658,7 @@ __device__ void pf_epilogue(const DecodeParams& P, const PfSync& sy, int64_t n_i
     const int buf = (int)(di & 1);
     if (!sy.wait(&sh->full_d[buf], (uint32_t)(di / 2) & 1u)) return;
     tc_fence_after();
-    if (has_next) meta_factors<MODE>(P, im2, lane, nx);
+    if (has_next) meta_factors<MODE>(P, im2, lane, any_shift, nx);
     const uint32_t taddr = tbase + (uint32_t)(buf * kPrefillSegRoutes);
     if (MODE == kGateUp) {
       const int I = P.I;
@@ -668,6 +671,28 @@ __device__ void pf_epilogue(const DecodeParams& P, const PfSync& sy, int64_t n_i
       // receiving the partner's value with one shuffle, so all 32 lanes do useful work.
       const bool upper = (lane & 16) != 0;
       const bool dbg = P.dbg_ic1 || P.dbg_h || P.dbg_sic1 || P.dbg_sh;
+      // the common case (plain SwiGLU, routed weight on the output, no debug copies) has a
+      // loop of its own: this epilogue is on the MMA's critical path, and the general
+      // activation's branches measured ~10% of the gate_up GEMM
+      if (P.act.kind == kActSilu && !P.w_on_input && !dbg) {
+        for (int c0 = 16 * half; c0 < im.n; c0 += 32) {
+          float v[16];
+          tmem_ld16(taddr + (uint32_t)c0, v);
+#pragma unroll
+          for (int p2 = 0; p2 < 8; ++p2) {
+            const float send = upper ? v[2 * p2] : v[2 * p2 + 1];
+            const float recv = __shfl_xor_sync(0xffffffffu, send, 16);
+            const float own = upper ? v[2 * p2 + 1] : v[2 * p2];
+            const float g = upper ? recv : own, u = upper ? own : recv;
+            const int n = c0 + 2 * p2 + (upper ? 1 : 0);
+            if (col_r[n] < 0) continue;
+            const float xs = col_f[n];
+            const float gv = bf16_round((g * xs) * glg);
+            const float uv = bf16_round((u * xs) * glu);
+            store_h(P, im.off + n, j, bf16_round((gv * sigmoid_f32<true>(gv)) * uv));
+          }
+        }
+      } else
       // chunks of 16 columns (im.n % 16 == 0: every column of a chunk is below n)
       for (int c0 = 16 * half; c0 < im.n; c0 += 32) {
         float v[16];

@@ -24,7 +24,8 @@
 //              from shared to tensor memory in the layout the MMA reads (row 32g + r of a
 //              32-row group g at lane r of every quarter, column g, byte = k block), then
 //              arrive on the stage's scale barrier;
-//   warps 6-9  epilogue, one per lane quarter: tcgen05.ld of the accumulator, then the decode
+//   warps 6-13 epilogue, two per lane quarter on alternate 16-column chunks (the items' route
+//              metadata loaded into shared memory before the accumulator wait): tcgen05.ld, then the decode
 //              path's arithmetic with the activation globals in place of the power-of-two x
 //              scales (gate_up -> bf16 ic1, activation -> f16 h in sorted order; down ->
 //              bf16(acc x gh x global x routed weight) per route).
@@ -62,7 +63,7 @@ constexpr int kF4BOff = kF4SfaOff + kF4SfaBytes;     // 18432 (1024-aligned: swi
 constexpr int kF4SfbOff = kF4BOff + kF4BBytes;       // 38912
 constexpr int kF4StageBytes = (kF4SfbOff + kF4SfbBytes + 1023) / 1024 * 1024;
 constexpr int kF4TxBytes = kF4ABytes + kF4SfaBytes + kF4BBytes + kF4SfbBytes;
-constexpr int kF4Header = 4096;
+constexpr int kF4Header = 16384;
 constexpr int kF4Smem = kF4Header + kF4Stages * kF4StageBytes;
 static_assert(kF4BOff % 1024 == 0 && kF4StageBytes % 1024 == 0, "1024-B swizzle atoms");
 static_assert(kF4Smem <= 227 * 1024, "shared memory");
@@ -77,7 +78,8 @@ constexpr int kF4TmemSf = 2 * kF4MaxN;              // 320
 static_assert(kF4SfbGroups <= kF4SfbStride && kF4TmemSf % 16 == 0 && kF4SfSlot % 16 == 0,
               "aligned scale regions");
 static_assert(kF4TmemSf + kF4Stages * kF4SfSlot <= 512, "tensor memory budget");
-constexpr int kF4Warps = 10;
+constexpr int kF4EpiWarps = 8;  // two per tensor-memory lane quarter, alternate 16-column chunks
+constexpr int kF4Warps = 6 + kF4EpiWarps;
 constexpr int kF4WarpTma = 0, kF4WarpMma = 1, kF4WarpSf = 2, kF4WarpEpi = 6;
 
 enum { kGateUp = 0, kDown = 1 };
@@ -89,6 +91,12 @@ struct F4Shared {
   uint32_t tmem_base;
   int abort;
   int last;
+  // per epilogue warp, the current item's columns: route id (-1 past the segment), the
+  // activation global (times the routed weight where it applies) and, for gate_up with the
+  // weight on the input, the routed weight
+  int col_r[kF4EpiWarps][kF4MaxN];
+  float col_f[kF4EpiWarps][kF4MaxN];
+  float col_w[kF4EpiWarps][kF4MaxN];
 };
 static_assert(sizeof(F4Shared) <= kF4Header, "header");
 
@@ -359,11 +367,37 @@ __device__ void f4_epilogue(const DecodeParams& P, const F4Sync& sy, int64_t n_i
                             int mtiles) {
   F4Shared* sh = sy.sh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int q = warp & 3;
+  const int q = warp & 3;                  // tensor-memory lane quarter
+  const int ew = warp - kF4WarpEpi;        // this warp's metadata slice
+  const int half = ew >> 2;                // its 16-column chunks: 16 half + 32 i
+  int* col_r = sh->col_r[ew];
+  float* col_f = sh->col_f[ew];
+  float* col_w = sh->col_w[ew];
   const uint32_t tbase = sh->tmem_base + ((uint32_t)(32 * q) << 16);
   uint32_t di = 0;
   for (int64_t it = blockIdx.x; it < n_items; it += gridDim.x) {
     const F4Item im = f4_item<MODE>(P, it, mtiles);
+    // the item's column metadata, loaded while its MMAs run
+#pragma unroll
+    for (int k = 0; k < kF4MaxN / kWarp; ++k) {
+      const int n = lane + kWarp * k;
+      int r = -1;
+      float f = 1.f, wr = 1.f;
+      if (n < im.cnt) {
+        r = P.sorted[im.off + n];
+        if (MODE == kGateUp) {
+          f = P.q4x_g[im.off + n];
+          if (P.w_on_input && !im.sh) wr = P.topk_w[r];
+        } else {
+          f = P.q4h_g[im.off + n];
+          if (!im.sh && !P.w_on_input) wr = P.topk_w[r];
+        }
+      }
+      col_r[n] = r;
+      col_f[n] = f;
+      col_w[n] = wr;
+    }
+    __syncwarp();
     const int buf = (int)(di & 1);
     if (!sy.wait(&sh->full_d[buf], (di >> 1) & 1u)) return;
     f4_fence_after();
@@ -375,7 +409,27 @@ __device__ void f4_epilogue(const DecodeParams& P, const F4Sync& sy, int64_t n_i
       const float glg = __half2float(__ushort_as_half(glob[j]));
       const float glu = __half2float(__ushort_as_half(glob[I + j]));
       const bool upper = (lane & 16) != 0;
-      for (int c0 = 0; c0 < im.n; c0 += 16) {
+      const bool dbg = P.dbg_ic1 || P.dbg_h || P.dbg_sic1 || P.dbg_sh;
+      if (P.act.kind == kActSilu && !P.w_on_input && !dbg) {  // the common case, branch-free
+        for (int c0 = 16 * half; c0 < im.n; c0 += 32) {
+          float v[16];
+          f4_tmem_ld16(taddr + (uint32_t)c0, v);
+#pragma unroll
+          for (int p2 = 0; p2 < 8; ++p2) {
+            const float send = upper ? v[2 * p2] : v[2 * p2 + 1];
+            const float recv = __shfl_xor_sync(0xffffffffu, send, 16);
+            const float own = upper ? v[2 * p2 + 1] : v[2 * p2];
+            const float g = upper ? recv : own, u = upper ? own : recv;
+            const int n = c0 + 2 * p2 + (upper ? 1 : 0);
+            if (col_r[n] < 0) continue;
+            const float gx = col_f[n];
+            const float gv = bf16_round((g * gx) * glg);
+            const float uv = bf16_round((u * gx) * glu);
+            store_h(P, im.off + n, j, bf16_round((gv * sigmoid_f32<true>(gv)) * uv));
+          }
+        }
+      } else
+      for (int c0 = 16 * half; c0 < im.n; c0 += 32) {
         float v[16];
         f4_tmem_ld16(taddr + (uint32_t)c0, v);
 #pragma unroll
@@ -385,33 +439,34 @@ __device__ void f4_epilogue(const DecodeParams& P, const F4Sync& sy, int64_t n_i
           const float own = upper ? v[2 * p2 + 1] : v[2 * p2];
           const float g = upper ? recv : own, u = upper ? own : recv;
           const int n = c0 + 2 * p2 + (upper ? 1 : 0);
-          if (n >= im.cnt) continue;
-          const int r = P.sorted[im.off + n];
-          const float gx = P.q4x_g[im.off + n];
+          const int r = col_r[n];
+          if (r < 0) continue;
+          const float gx = col_f[n];
           float gv = (g * gx) * glg;
           float uv = (u * gx) * glu;
-          if (P.w_on_input && !im.sh) {
-            const float wr = P.topk_w[r];
-            gv *= wr;
-            uv *= wr;
+          if (P.w_on_input) {
+            gv *= col_w[n];
+            uv *= col_w[n];
           }
           gv = bf16_round(gv);
           uv = bf16_round(uv);
           const float hv = bf16_round(act_f32<true>(gv, uv, P.act));
           store_h(P, im.off + n, j, hv);
-          if (im.sh) {
-            const int64_t tok = (int64_t)r - P.R;
-            if (P.dbg_sic1) {
-              P.dbg_sic1[tok * 2 * I + j] = f32_to_bf16_bits(gv);
-              P.dbg_sic1[tok * 2 * I + I + j] = f32_to_bf16_bits(uv);
+          if (dbg) {
+            if (im.sh) {
+              const int64_t tok = (int64_t)r - P.R;
+              if (P.dbg_sic1) {
+                P.dbg_sic1[tok * 2 * I + j] = f32_to_bf16_bits(gv);
+                P.dbg_sic1[tok * 2 * I + I + j] = f32_to_bf16_bits(uv);
+              }
+              if (P.dbg_sh) P.dbg_sh[tok * I + j] = f32_to_bf16_bits(hv);
+            } else {
+              if (P.dbg_ic1) {
+                P.dbg_ic1[(int64_t)r * 2 * I + j] = f32_to_bf16_bits(gv);
+                P.dbg_ic1[(int64_t)r * 2 * I + I + j] = f32_to_bf16_bits(uv);
+              }
+              if (P.dbg_h) P.dbg_h[(int64_t)r * I + j] = f32_to_bf16_bits(hv);
             }
-            if (P.dbg_sh) P.dbg_sh[tok * I + j] = f32_to_bf16_bits(hv);
-          } else {
-            if (P.dbg_ic1) {
-              P.dbg_ic1[(int64_t)r * 2 * I + j] = f32_to_bf16_bits(gv);
-              P.dbg_ic1[(int64_t)r * 2 * I + I + j] = f32_to_bf16_bits(uv);
-            }
-            if (P.dbg_h) P.dbg_h[(int64_t)r * I + j] = f32_to_bf16_bits(hv);
           }
         }
       }
@@ -420,22 +475,17 @@ __device__ void f4_epilogue(const DecodeParams& P, const F4Sync& sy, int64_t n_i
       const int row = kF4Rows * im.mt + 32 * q + lane;
       const uint16_t* glob = im.sh ? P.dn.s_global : P.dn.global + (int64_t)im.e * H;
       const float gl = __half2float(__ushort_as_half(glob[row]));
-      for (int c0 = 0; c0 < im.n; c0 += 16) {
+      uint16_t* dst = (im.sh ? P.ic3s : P.ic3) + row;
+      const int64_t r0 = im.sh ? P.R : 0;  // shared-expert routes R + t are rows t of ic3s
+      for (int c0 = 16 * half; c0 < im.n; c0 += 32) {
         float v[16];
         f4_tmem_ld16(taddr + (uint32_t)c0, v);
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
           const int n = c0 + k;
-          if (n >= im.cnt) break;
-          const int r = P.sorted[im.off + n];
-          const float gh = P.q4h_g[im.off + n];
-          float f = 1.f;
-          if (!im.sh && !P.w_on_input) f = P.topk_w[r];
-          const float o = ((v[k] * gh) * gl) * f;
-          if (im.sh)
-            P.ic3s[((int64_t)r - P.R) * H + row] = f32_to_bf16_bits(o);
-          else
-            P.ic3[(int64_t)r * H + row] = f32_to_bf16_bits(o);
+          const int r = col_r[n];
+          if (r < 0) continue;
+          dst[((int64_t)r - r0) * H] = f32_to_bf16_bits(((v[k] * col_f[n]) * gl) * col_w[n]);
         }
       }
     }
@@ -461,7 +511,7 @@ __global__ void __launch_bounds__(kF4Warps * kWarp, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sh->full_d[b], 1);
-      mbar_init(&sh->empty_d[b], 4);
+      mbar_init(&sh->empty_d[b], kF4EpiWarps);
     }
     mbar_init(&sh->drain, 1);
     sh->abort = 0;
@@ -497,7 +547,7 @@ __global__ void __launch_bounds__(kF4Warps * kWarp, 1)
   } else {
     f4_epilogue<MODE>(P, sy, n_items, mtiles);
     if (MODE == kGateUp)
-      finish_gate_up(P, 1, 4 * kWarp, threadIdx.x - kF4WarpEpi * kWarp, &sh->last);
+      finish_gate_up(P, 1, kF4EpiWarps * kWarp, threadIdx.x - kF4WarpEpi * kWarp, &sh->last);
   }
   f4_fence_before();
   __syncthreads();

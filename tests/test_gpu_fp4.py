@@ -101,3 +101,23 @@ def test_fp4_prefill_vs_emulation(E, T, K, shared):
     err = compare(to_f32(out), oracle_layer(case)["out"])[0]
     print(f"fp4 prefill max|d|/max|ref| vs parity oracle: {err:.3f}")
     assert err < 0.35
+
+
+def test_fp4_prefill_config2_shape_close_to_parity_path():
+    """BASELINE config-2 shape (H=4096, I=1536, 256 experts, top-8, shared expert; 16 and 6 k
+    stages, all 4D tile coordinates of a 256-expert bank): the FP4 path stays within the NVFP4
+    activation error of the parity path, with status 0."""
+    from ftb import synth
+
+    E, H, I, K, T = 256, 4096, 1536, 8, 512
+    bank = synth.make_bank(E, H, I, seed=33, device=DEV)
+    shared = synth.make_shared(H, I, seed=33, device=DEV)
+    inp = synth.make_inputs(T, H, E, seed=33, device=DEV)
+    w, ids = ftb.fused_topk(inp.x, inp.logits, K, True)
+    ref = ftb.moe_prefill(inp.x, bank, w, ids, shared=shared)
+    got, it = ftb.moe_prefill_fp4(inp.x, bank, w, ids, shared=shared, debug=True)
+    torch.cuda.synchronize()
+    assert it["status"] == 0
+    err = float((got.float() - ref.float()).abs().max() / ref.float().abs().max())
+    print(f"fp4 prefill at config-2 shape, max|d|/max|ref| vs parity path: {err:.3f}")
+    assert err < 0.35

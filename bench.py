@@ -752,6 +752,7 @@ def run_ep(args, torch, rank: int, world: int, local: int):
     nprof = min(args.steps, 32)
     kt = kernel_times(_lib, torch, step, nprof)
     local_experts = [layers[i % len(layers)][0].last_local_experts for i in range(nprof)]
+    phases = ep_phase_trace(torch, dist, group, step, world, dev) if group is not None else None
     status = group.status() if group is not None else 0
     dist.barrier()
     if group is not None:
@@ -800,9 +801,43 @@ def run_ep(args, torch, rank: int, world: int, local: int):
             "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
             "frac": round(achieved / peak, 4), "peak_source": peak_src, "traffic": None},
         "kernels_ms": {k: round(statistics.mean(v), 4) for k, v in kt.items()},
+        "ep_phases_us": phases,
         "gpu_launches": launches * args.steps,
         "clocks": clk,
     }
+
+
+def ep_phase_trace(torch, dist, group, step, world: int, dev, n: int = 16):
+    """Per-phase device timestamps (%globaltimer, ftb_ep_set_trace) of n eager steps on every
+    rank: publish, front wait/work, gate_up, down, combine wait/work. Returns, per phase, the
+    mean over steps of the max over ranks and every rank's mean, plus the step span."""
+    from ftb.ep import EP_TRACE_PHASES, trace_phases_us, trace_reset
+
+    buf = torch.empty(8, dtype=torch.int64, device=dev)
+    group.set_trace(buf)
+    rows = []
+    for i in range(n):
+        trace_reset(buf)
+        step(i)
+        torch.cuda.synchronize()
+        rows.append(buf.clone())
+    group.set_trace(None)
+    mine = torch.stack(rows)  # [n, 8]
+    every = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(every, mine)
+    names = list(EP_TRACE_PHASES) + ["step"]
+    per = [[trace_phases_us(r.tolist()) for r in e.cpu()] for e in every]  # [rank][step]
+    out = {"steps": n, "max_over_ranks": {}, "per_rank_mean": {}}
+    for name in names:
+        out["max_over_ranks"][name] = round(
+            statistics.mean(max(per[q][i][name] for q in range(world)) for i in range(n)), 2)
+        out["per_rank_mean"][name] = [round(statistics.mean(per[q][i][name] for i in range(n)), 2)
+                                      for q in range(world)]
+    out["note"] = ("eager steps, trace on; phase i = slot i+1 - slot i of one rank's trace; "
+                   "front_wait/combine_wait end when the last peer flag is seen. Each GPU's "
+                   "globaltimer has its own offset (seconds apart on this box), so only "
+                   "differences within one rank are reported")
+    return out
 
 
 def run_ep_stack(args, torch, rank: int, world: int, local: int):

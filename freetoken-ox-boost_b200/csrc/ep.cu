@@ -46,6 +46,7 @@ struct ftb_ep {
   bool opened;
   void* ws;
   int64_t wait_ns;
+  unsigned long long* trace;  // device [kEpTraceWords] or null (ftb_ep_set_trace)
 };
 
 namespace ftb {
@@ -134,11 +135,13 @@ struct PublishParams {
   int64_t nr;  // routes
   int32_t* ctl;       // control words: all but the sticky status word are zeroed, and the
   int64_t n_hshift;   // n_hshift per-row h shifts that follow them
+  unsigned long long* trace;
 };
 
 __global__ void __launch_bounds__(256) k_ep_publish(const PublishParams P) {
   pdl_launch_dependents();
   pdl_wait();
+  if (threadIdx.x == 0) trace_start(P.trace ? P.trace + kEpTracePublish : nullptr);
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   for (int64_t i = i0; i < P.nx; i += stride) P.rx[i] = P.x[i];
@@ -166,11 +169,13 @@ __global__ void __launch_bounds__(256) k_ep_combine(const CombineParams C) {
   __shared__ int sm_ok;
   __shared__ uint32_t sm_epoch;
   if (threadIdx.x == 0) {
+    trace_start(L.trace ? L.trace + kEpTraceCombine : nullptr);
     const uint32_t epoch = *L.epoch + 1;
     ep_signal(L.done_sig, L.world, epoch);
     bool ok = true;
     for (int p = 0; p < L.world && ok; ++p) ok = ep_wait(L.done_flag + p, epoch, L.wait_ns);
     if (!ok) atomicOr(C.status, kStatusTimeout);
+    trace_seen(L.trace ? L.trace + kEpTraceCombSeen : nullptr);
     sm_ok = ok;
     sm_epoch = epoch;
   }
@@ -224,6 +229,7 @@ __global__ void __launch_bounds__(256) k_ep_combine(const CombineParams C) {
     if (atomicAdd(L.done_blocks, 1) == (int)gridDim.x - 1) {
       *L.done_blocks = 0;
       *L.epoch = sm_epoch;
+      if (L.trace) L.trace[kEpTraceEnd] = globaltimer_ns();
       __threadfence();
     }
   }
@@ -257,6 +263,7 @@ EpLinks make_links(const ftb_ep& g, const EpWs& w) {
   L.ids_all = w.ids_all;
   L.w_all = w.w_all;
   L.wait_ns = g.wait_ns;
+  L.trace = g.trace;
   return L;
 }
 
@@ -362,6 +369,12 @@ int ftb_ep_set_wait_ns(ftb_ep* g, int64_t ns) {
   return FTB_OK;
 }
 
+int ftb_ep_set_trace(ftb_ep* g, uint64_t* trace) {
+  if (!g || (trace && (reinterpret_cast<uintptr_t>(trace) & 7))) return FTB_ERR_ARG;
+  g->trace = reinterpret_cast<unsigned long long*>(trace);
+  return FTB_OK;
+}
+
 static int ep_forward_impl(ftb_ep* g, const uint16_t* x, const float* topk_w,
                            const int32_t* topk_ids, const ftb_nvfp4_bank* local_bank,
                            const ftb_nvfp4_bank* shared, ActSpec act, int w_on_input,
@@ -384,7 +397,7 @@ static int ep_forward_impl(ftb_ep* g, const uint16_t* x, const float* topk_w,
 
   PublishParams pp{reinterpret_cast<const uint4*>(x), topk_w, topk_ids,
                    reinterpret_cast<uint4*>(own.x), own.w, own.ids, g->T * g->H / 8,
-                   g->T * g->K, w.status, Ra + g->T};
+                   g->T * g->K, w.status, Ra + g->T, g->trace};
   int64_t gp = ceil_div(pp.nx, 256);
   if (gp > sm_count()) gp = sm_count();
   prof_mark(FTB_KERNEL_EP_PUBLISH, true, s);
@@ -451,6 +464,7 @@ static int ep_forward_impl(ftb_ep* g, const uint16_t* x, const float* topk_w,
   dp.gu_done = w.status + kCtlGuDone;
   dp.hb = w.hb;
   dp.has_shared = g->has_shared;
+  dp.trace = g->trace ? g->trace + kEpTraceGateUp : nullptr;
   st = launch_decode_gemvs_tma(dp, s);
   if (st) return st;
 

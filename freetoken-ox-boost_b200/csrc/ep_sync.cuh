@@ -22,12 +22,6 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
-__device__ __forceinline__ uint64_t globaltimer_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
 // One thread: every write this rank made before (earlier launches on the stream included)
 // becomes visible to a rank that observes `epoch` in its slot.
 __device__ inline void ep_signal(uint32_t* const* sig, int world, uint32_t epoch) {

@@ -510,6 +510,7 @@ __global__ void __launch_bounds__((NW + 1) * kWarp, CPS)
   }
   __syncthreads();
   pdl_wait();  // the segment table, activations and work counter come from earlier launches
+  if (P.trace && threadIdx.x == 0) trace_start(P.trace + MODE);
   const Sync sy{full, empty, tile_of, abort_flag, P.status};
   const int K = MODE == kGateUp ? P.H : P.I;
   const int nk = (K + kStageK - 1) / kStageK;

@@ -67,7 +67,38 @@ struct EpLinks {
   int32_t* ids_all;                   // [world*tblk*top_k] gathered ids, local (-1: not owned)
   float* w_all;                       // [world*tblk*top_k] gathered routed weights
   int64_t wait_ns;                    // bound of every flag wait
+  unsigned long long* trace;          // or null: phase timestamps (kEpTrace*, %globaltimer ns)
 };
+
+// Phase timestamps of one expert-parallel step (ftb_ep_set_trace): the earliest start of each
+// launch after its dependency wait (min over CTAs), the latest moment a waiting thread saw
+// every peer's flag (max), and the end of the combine (its last block). Consecutive slots
+// bound the phases publish, front wait, front work, gate_up, down, combine wait, combine work.
+enum {
+  kEpTracePublish = 0,    // min
+  kEpTraceFront = 1,      // min
+  kEpTraceFrontSeen = 2,  // max
+  kEpTraceGateUp = 3,     // min
+  kEpTraceDown = 4,       // min
+  kEpTraceCombine = 5,    // min
+  kEpTraceCombSeen = 6,   // max
+  kEpTraceEnd = 7,        // written once
+  kEpTraceWords = 8
+};
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// One thread per CTA: slot = min(slot, now) (trace_start) or max(slot, now) (trace_seen).
+__device__ __forceinline__ void trace_start(unsigned long long* slot) {
+  if (slot) atomicMin(slot, (unsigned long long)globaltimer_ns());
+}
+__device__ __forceinline__ void trace_seen(unsigned long long* slot) {
+  if (slot) atomicMax(slot, (unsigned long long)globaltimer_ns());
+}
 
 struct SortParams {
   const int32_t* ids;  // [R] flat topk ids
@@ -155,6 +186,7 @@ struct DecodeParams {
   int32_t* hlist;          // [R + Ts] sorted rows whose hshift is set
   int32_t* hcount;         // entries of hlist (zeroed per call)
   int32_t* gu_done;        // gate_up CTAs finished (zeroed per call)
+  unsigned long long* trace;  // or null: [0] gate_up, [1] down start (min over CTAs, ns)
   uint16_t* hb;            // [R + Ts, I] bf16 h of the elements beyond the f16 range
   // FP4 prefill (FTB_PATH_PREFILL_FP4): NVFP4 activation rows in sorted order
   const uint16_t* x_in;    // [T, H] bf16 layer input

@@ -367,6 +367,22 @@ __device__ void stage_token_warp(const SortParams& P, int64_t t, const uint16_t*
   }
 }
 
+// One thread, after the home rank's "inputs published" flag: whether token tl of slot block b
+// (home rank `home`) has a route to an expert this rank owns, or is one of this rank's own
+// tokens and a shared expert runs on them. Other tokens are not staged: no route of this
+// rank's launches reads their rows.
+__device__ __forceinline__ bool ep_token_needed(const SortParams& P, int home, int b,
+                                                int64_t tl) {
+  const EpLinks& L = P.ep;
+  if (b == 0 && P.has_shared) return true;
+  const int32_t* ids = L.ids[home] + tl * L.top_k;
+  for (int k = 0; k < L.top_k; ++k) {
+    const int e = ids[k];
+    if (e >= L.e0 && e < L.e0 + L.per) return true;
+  }
+  return false;
+}
+
 // Expert-parallel front (P.ep.world > 0). Token slots are ordered by rank starting with this
 // one: slot block b (tokens b*tblk .. b*tblk+tblk-1) holds rank (rank + b) % world's tokens,
 // so this rank's own tokens are rows 0..tblk-1 (the shared expert's rows).
@@ -374,38 +390,46 @@ __device__ void stage_token_warp(const SortParams& P, int64_t t, const uint16_t*
 //                before this one), then wait for the ranks whose data it reads;
 //   block 0:     gathers every rank's routes, keeping those of the experts this rank owns
 //                (local ids; others -1) with their weights, then sorts them;
-//   block 1+t:   stages token slot t from its home rank's published row (a peer load).
+//   block 1+t:   stages token slot t from its home rank's published row (a peer load), if
+//                the token routes to an owned expert or feeds the shared expert here.
 __device__ void ep_front(const SortParams& P, int* hist) {
   const EpLinks& L = P.ep;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t epoch = *L.epoch + 1;
+  if (threadIdx.x == 0) trace_start(L.trace ? L.trace + kEpTraceFront : nullptr);
   if (blockIdx.x != 0 && P.stage_tpb == 1) {  // staging: block 1 + t stages token slot t
     __shared__ int sm_ok1;
     const int64_t t = (int64_t)blockIdx.x - 1;
     const int b = (int)(t / L.tblk);
+    const int home = (L.rank + b) % L.world;
+    const int64_t tl = t - b * L.tblk;
     if (threadIdx.x == 0) {
       ep_signal(L.in_sig, L.world, epoch);
-      const bool ok = ep_wait(L.in_flag + (L.rank + b) % L.world, epoch, L.wait_ns);
+      const bool ok = ep_wait(L.in_flag + home, epoch, L.wait_ns);
       if (!ok) atomicOr(P.status, kStatusTimeout);
-      sm_ok1 = ok;
+      trace_seen(L.trace ? L.trace + kEpTraceFrontSeen : nullptr);
+      sm_ok1 = ok && ep_token_needed(P, home, b, tl);
     }
     __syncthreads();
-    if (sm_ok1) stage_token_block(P, t, L.x[(L.rank + b) % L.world] + (t - b * L.tblk) * P.H);
+    if (sm_ok1) stage_token_block(P, t, L.x[home] + tl * P.H);
     return;
   }
   if (blockIdx.x != 0) {  // staging: warp w stages token slot 32 (block - 1) + w
     const int64_t t = ((int64_t)blockIdx.x - 1) * kSortWarps + warp;
     if (t >= P.T) return;
     const int b = (int)(t / L.tblk);
+    const int home = (L.rank + b) % L.world;
+    const int64_t tl = t - b * L.tblk;
     int ok = 1;
     if (lane == 0) {
       if (threadIdx.x == 0) ep_signal(L.in_sig, L.world, epoch);
-      ok = ep_wait(L.in_flag + (L.rank + b) % L.world, epoch, L.wait_ns);
+      ok = ep_wait(L.in_flag + home, epoch, L.wait_ns);
       if (!ok) atomicOr(P.status, kStatusTimeout);
+      trace_seen(L.trace ? L.trace + kEpTraceFrontSeen : nullptr);
+      ok = ok && ep_token_needed(P, home, b, tl);
     }
     if (!__shfl_sync(0xffffffffu, ok, 0)) return;
-    const uint16_t* src = L.x[(L.rank + b) % L.world] + (t - b * L.tblk) * P.H;
-    stage_token_warp(P, t, src);
+    stage_token_warp(P, t, L.x[home] + tl * P.H);
     return;
   }
   __shared__ int sm_ok;
@@ -414,6 +438,7 @@ __device__ void ep_front(const SortParams& P, int* hist) {
     bool ok = true;
     for (int p = 0; p < L.world && ok; ++p) ok = ep_wait(L.in_flag + p, epoch, L.wait_ns);
     if (!ok) atomicOr(P.status, kStatusTimeout);
+    trace_seen(L.trace ? L.trace + kEpTraceFrontSeen : nullptr);
     sm_ok = ok;
   }
   __syncthreads();

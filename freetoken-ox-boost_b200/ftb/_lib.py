@@ -108,6 +108,7 @@ SIGNATURES = {
     "ftb_ep_handle": (_i32, [_vp, _vp]),
     "ftb_ep_open": (_i32, [_vp, _vp]),
     "ftb_ep_set_wait_ns": (_i32, [_vp, _i64]),
+    "ftb_ep_set_trace": (_i32, [_vp, _vp]),
     "ftb_ep_forward": (_i32, [_vp, _vp, _vp, _vp, _BP, _BP, _f32, _vp, _vp]),
     "ftb_ep_forward_act": (_i32, [_vp, _vp, _vp, _vp, _BP, _BP, _i32, _f32, _f32, _i32, _vp,
                                   _vp]),

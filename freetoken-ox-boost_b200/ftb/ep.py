@@ -40,6 +40,30 @@ from ._runtime import ptr, require, require_cuda, stream_handle
 from .banks import Nvfp4Bank
 
 
+# ftb_ep_set_trace slots, in step order, and the phases between consecutive slots
+EP_TRACE_WORDS = 8
+EP_TRACE_PHASES = ("publish", "front_wait", "front_work", "gate_up", "down", "combine_wait",
+                   "combine_work")
+_U64_MAX = (1 << 64) - 1
+
+
+def trace_reset(trace: torch.Tensor) -> torch.Tensor:
+    """Initialise a [EP_TRACE_WORDS] int64 device tensor for one traced step: the min slots to
+    UINT64_MAX (all bits set), the max and end slots to 0."""
+    init = torch.tensor([-1, -1, 0, -1, -1, -1, 0, 0], dtype=torch.int64)
+    trace.copy_(init.to(trace.device), non_blocking=True)
+    return trace
+
+
+def trace_phases_us(words) -> dict:
+    """A traced step's slots (8 unsigned ns timestamps, e.g. ``trace.tolist()``) -> phase
+    durations in microseconds, plus ``step`` (publish start to combine end)."""
+    t = [int(v) & _U64_MAX for v in words]
+    out = {name: (t[i + 1] - t[i]) / 1e3 for i, name in enumerate(EP_TRACE_PHASES)}
+    out["step"] = (t[7] - t[0]) / 1e3
+    return out
+
+
 def shard_range(num_experts: int, rank: int, world: int):
     if num_experts % world:
         raise ValueError(f"{num_experts} experts do not shard evenly over {world} ranks")
@@ -114,6 +138,19 @@ class EpGroup:
                                             ptr(out), stream_handle(dev))
         _lib.check("ftb_ep_forward_act", st)
         return out
+
+    def set_trace(self, trace: torch.Tensor | None):
+        """Record phase timestamps of the following steps into ``trace`` (a contiguous int64
+        CUDA tensor of ``EP_TRACE_WORDS``, initialised by ``trace_reset`` before each traced
+        step), or stop recording (None). See ``trace_phases_us``."""
+        if trace is not None:
+            if (trace.dtype != torch.int64 or not trace.is_cuda or trace.numel() != EP_TRACE_WORDS
+                    or not trace.is_contiguous()):
+                raise ValueError(f"trace must be a contiguous int64 CUDA tensor of "
+                                 f"{EP_TRACE_WORDS} words")
+        st = _lib.load().ftb_ep_set_trace(self._h, ptr(trace) if trace is not None else None)
+        _lib.check("ftb_ep_set_trace", st)
+        self._trace = trace
 
     def status(self, clear: bool = True) -> int:
         """The sticky device status word (synchronises the current stream)."""

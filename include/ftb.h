@@ -336,6 +336,17 @@ FTB_API int ftb_ep_create(int rank, int world, int64_t tokens_per_rank, int H, i
 FTB_API int ftb_ep_handle(const ftb_ep* ep, void* handle);
 FTB_API int ftb_ep_open(ftb_ep* ep, const void* handles);
 FTB_API int ftb_ep_set_wait_ns(ftb_ep* ep, int64_t ns);
+/*
+ * Phase timestamps (%globaltimer, ns) of the steps that follow, into `trace`, a device array of
+ * FTB_EP_TRACE_WORDS u64 that the caller initialises before a step: slots 0, 1, 3, 4, 5 to
+ * UINT64_MAX (each takes the earliest start of a launch after its dependency wait: publish,
+ * front, gate_up, down, combine), slots 2 and 6 to 0 (the latest moment a thread of the front /
+ * the combine saw every peer's flag), slot 7 (the combine's end) to 0. Consecutive slots bound
+ * the phases publish, front wait, front work, gate_up, down, combine wait, combine work.
+ * NULL turns tracing off (the default). 8-byte aligned; no counterpart in the reference.
+ */
+#define FTB_EP_TRACE_WORDS 8
+FTB_API int ftb_ep_set_trace(ftb_ep* ep, uint64_t* trace);
 FTB_API int ftb_ep_forward(ftb_ep* ep, const uint16_t* x, const float* topk_w,
                            const int32_t* topk_ids, const ftb_nvfp4_bank* local_bank,
                            const ftb_nvfp4_bank* shared, float act_limit, uint16_t* out,

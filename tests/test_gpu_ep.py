@@ -1,9 +1,12 @@
 """Expert parallelism on the GPU.
 
 * 1 GPU: an ``EpGroup`` of world 1 (the peer-memory path with no peers) returns the
-  single-GPU decode bit for bit, over several steps and two layers sharing the group.
+  single-GPU decode bit for bit, over several steps and two layers sharing the group; a
+  traced step fills the phase timestamps in step order.
 * 2 GPUs, both transports (NCCL all_to_all and peer memory): each rank's output equals the
-  single-GPU decode of the same tokens with the full bank, bit for bit, over several steps.
+  single-GPU decode of the same tokens with the full bank, bit for bit, over several steps
+  (one of them with tokens that route to one rank's experts only, which the other does not
+  stage).
 * 2 GPUs, peer memory: a rank that stops stepping makes its peer's bounded flag waits give
   up and report the timeout bit, with the peer's process and GPU still usable.
 Multi-GPU cases are skipped with fewer than 2 GPUs.
@@ -66,6 +69,38 @@ def test_ep_world1_p2p_bit_exact():
         group.close()
 
 
+def test_ep_world1_phase_trace():
+    """ftb_ep_set_trace: the eight slots of a traced step are filled and in step order."""
+    import ftb
+    from ftb import synth
+    from ftb.ep import EP_TRACE_PHASES, EpGroup, trace_phases_us, trace_reset
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    bank = synth.make_bank(E, H, I, seed=13, device=dev)
+    shared = synth.make_shared(H, I, seed=13, device=dev)
+    group = EpGroup(T, H, I, E, K, True, 0, 1)
+    try:
+        inp = synth.make_inputs(T, H, E, seed=7, device=dev)
+        w, ids = ftb.fused_topk(inp.x, inp.logits, K, True)
+        buf = torch.empty(8, dtype=torch.int64, device=dev)
+        group.set_trace(buf)
+        trace_reset(buf)
+        out = group.forward(inp.x, w, ids, bank, shared)
+        torch.cuda.synchronize()
+        group.set_trace(None)
+        words = [int(v) & ((1 << 64) - 1) for v in buf.tolist()]
+        assert all(0 < v < (1 << 63) for v in words), words
+        assert words == sorted(words), words
+        ph = trace_phases_us(buf.tolist())
+        assert set(EP_TRACE_PHASES) <= set(ph) and 0 < ph["step"] < 1e6, ph
+        ref = ftb.moe_decode(inp.x, bank, w, ids, shared=shared)
+        assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+        assert group.status() == 0
+    finally:
+        group.close()
+
+
 def _worker(rank, port, out_dir, transport, mode):
     _paths()
     import torch.distributed as dist
@@ -105,6 +140,9 @@ def _worker(rank, port, out_dir, transport, mode):
             same = True
             for step in range(3):
                 inp = synth.make_inputs(T, H, E, seed=5 + step, stream=rank, device=dev)
+                if step == 2:
+                    # tokens 0-3 route to rank 0's experts only: rank 1 must not need them
+                    inp.logits[:4, E // 2:] -= 50.0
                 out = ep.forward(inp.x, inp.logits)
                 w, ids = ftb.fused_topk(inp.x, inp.logits, K, True)
                 ref = ftb.moe_decode(inp.x, full, w, ids, shared=shared)

@@ -173,6 +173,8 @@ static int layer_impl(const ftb_moe_args& a, cudaStream_t stream) {
       a.activation != FTB_ACT_SWIGLUOAI)
     return FTB_ERR_ARG;
   if (prefill && a.route_mask) return FTB_ERR_ARG;  // the split decode runs the GEMVs only
+  if (a.h_quant != FTB_HQUANT_NONE && (a.h_quant != FTB_HQUANT_FP8_BLOCK128 || fp4))
+    return FTB_ERR_ARG;
   const ftb_nvfp4_bank* bank = a.bank;
   const ftb_nvfp4_bank* shared = a.shared;
   if (!bank_ok(bank) || (shared && !bank_ok(shared))) return FTB_ERR_ARG;
@@ -240,6 +242,7 @@ static int layer_impl(const ftb_moe_args& a, cudaStream_t stream) {
   dp.Ts = T;
   dp.act = ActSpec{a.activation, a.act_alpha, a.act_limit};
   dp.w_on_input = a.weight_on_input ? 1 : 0;
+  dp.h_quant = a.h_quant;
   dp.topk_w = a.topk_w;
   dp.topk_ids = a.topk_ids;
   dp.sorted = w.sorted;

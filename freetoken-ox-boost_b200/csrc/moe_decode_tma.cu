@@ -403,21 +403,25 @@ __device__ void epi_gate_up(const DecodeParams& P, const float (&acc)[MT][NT][4]
         }
         gv = bf16_round(gv);
         uv = bf16_round(uv);
-        const float hv = bf16_round(act_f32(gv, uv, P.act));
-        store_h(P, off + j, hp, hv);
+        const float av = act_f32(gv, uv, P.act);
+        const float hv = bf16_round(av);
+        if (P.h_quant)
+          store_act32(P, off + j, hp, av);
+        else
+          store_h(P, off + j, hp, hv);
         if (sh) {
           const int64_t t = (int64_t)r - P.R;
           if (P.dbg_sic1) {
             P.dbg_sic1[t * 2 * I + ng] = f32_to_bf16_bits(gv);
             P.dbg_sic1[t * 2 * I + I + ng] = f32_to_bf16_bits(uv);
           }
-          if (P.dbg_sh) P.dbg_sh[t * I + ng] = f32_to_bf16_bits(hv);
+          if (P.dbg_sh && !P.h_quant) P.dbg_sh[t * I + ng] = f32_to_bf16_bits(hv);
         } else {
           if (P.dbg_ic1) {
             P.dbg_ic1[(int64_t)r * 2 * I + ng] = f32_to_bf16_bits(gv);
             P.dbg_ic1[(int64_t)r * 2 * I + I + ng] = f32_to_bf16_bits(uv);
           }
-          if (P.dbg_h) P.dbg_h[(int64_t)r * I + ng] = f32_to_bf16_bits(hv);
+          if (P.dbg_h && !P.h_quant) P.dbg_h[(int64_t)r * I + ng] = f32_to_bf16_bits(hv);
         }
       }
     }
@@ -768,6 +772,10 @@ int launch_decode_gemvs_tma(const DecodeParams& P, cudaStream_t stream) {
   int st = launch_rows<kGateUp>(P, plan.gate_up_rows, max_seg, stream);
   prof_mark(FTB_KERNEL_GATE_UP, false, stream);
   if (st) return st;
+  if (P.h_quant) {
+    st = launch_h_fp8(P, true, max_seg, stream);
+    if (st) return st;
+  }
   prof_mark(FTB_KERNEL_DOWN, true, stream);
   st = launch_rows<kDown>(P, plan.down_rows, max_seg, stream);
   prof_mark(FTB_KERNEL_DOWN, false, stream);

@@ -162,6 +162,8 @@ struct DecodeParams {
   int64_t Ts;              // shared-expert tokens (rows 0..Ts-1 of x16)
   ActSpec act;             // activation between the GEMVs
   int w_on_input;          // apply_router_weight_on_input: the routed weight scales ic1, not ic3
+  int h_quant;             // FTB_HQUANT_*: FP8 round trip of h (the gate_up epilogue leaves the
+                           // fp32 activation in h16 / hb for launch_h_fp8)
   const float* topk_w;     // [R]
   const int32_t* topk_ids; // [R]
   // sort results
@@ -225,6 +227,16 @@ __device__ __forceinline__ void store_h(const DecodeParams& P, int64_t sp, int64
     }
   }
   P.h16[idx] = h;
+}
+
+// FTB_HQUANT_FP8_BLOCK128: the unrounded fp32 activation a of element pos of sorted row sp,
+// high 16 bits into the h16 slot and low 16 into the hb slot (launch_h_fp8 reads them back).
+__device__ __forceinline__ void store_act32(const DecodeParams& P, int64_t sp, int64_t pos,
+                                            float a) {
+  const uint32_t b = __float_as_uint(a);
+  const int64_t idx = sp * P.I + pos;
+  reinterpret_cast<uint16_t*>(P.h16)[idx] = (uint16_t)(b >> 16);
+  P.hb[idx] = (uint16_t)(b & 0xFFFFu);
 }
 
 // 2^c for an integer c in [-126, 127].
@@ -324,6 +336,10 @@ inline int layer_shape_status(int64_t T, int H, int I, int64_t E, int top_k) {
 int launch_decode_gemvs_tma(const DecodeParams& P, cudaStream_t stream);
 // Tensor-core grouped GEMMs for prefill (moe_prefill.cu): segments of <= kPrefillSegRoutes.
 int launch_prefill_gemms(const DecodeParams& P, cudaStream_t stream);
+// FP8 round trip of h between the GEMMs (h_quant.cu): one CTA per work segment (max_seg of
+// them); h16 round-interleaved (the GEMVs) or plain (the grouped GEMMs).
+int launch_h_fp8(const DecodeParams& P, bool round_interleaved, int64_t max_seg,
+                 cudaStream_t stream);
 // Block-scaled FP4 prefill (moe_prefill_fp4.cu): quantise x, gate_up, quantise h, down.
 bool prefill_fp4_shape_ok(int H, int I);
 int launch_prefill_fp4(const DecodeParams& P, cudaStream_t stream);

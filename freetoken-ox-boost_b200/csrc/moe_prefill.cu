@@ -633,8 +633,9 @@ __device__ void pf_epilogue(const DecodeParams& P, const PfSync& sy, int64_t n_i
   Meta nx;
   int64_t it = blockIdx.x / kPair;
   // down: the gate_up launch (complete before this one's dependency wait) shifted some rows of
-  // h iff it listed any; without, every shift is 0 and its loads are skipped
-  const bool any_shift = MODE == kDown && __ldcg(P.hcount) > 0;
+  // h iff it listed any, and the FP8 round trip shifts every row; otherwise every shift is 0
+  // and its loads are skipped
+  const bool any_shift = MODE == kDown && (P.h_quant || __ldcg(P.hcount) > 0);
   Item im{};
   if (it < n_items) {
     im = item_of<MODE>(P, it, mpairs, sy.rank);
@@ -674,7 +675,7 @@ __device__ void pf_epilogue(const DecodeParams& P, const PfSync& sy, int64_t n_i
       // the common case (plain SwiGLU, routed weight on the output, no debug copies) has a
       // loop of its own: this epilogue is on the MMA's critical path, and the general
       // activation's branches measured ~10% of the gate_up GEMM
-      if (P.act.kind == kActSilu && !P.w_on_input && !dbg) {
+      if (P.act.kind == kActSilu && !P.w_on_input && !P.h_quant && !dbg) {
         for (int c0 = 16 * half; c0 < im.n; c0 += 32) {
           float v[16];
           tmem_ld16(taddr + (uint32_t)c0, v);
@@ -716,8 +717,12 @@ __device__ void pf_epilogue(const DecodeParams& P, const PfSync& sy, int64_t n_i
           }
           gv = bf16_round(gv);
           uv = bf16_round(uv);
-          const float hv = bf16_round(act_f32<true>(gv, uv, P.act));
-          store_h(P, im.off + n, j, hv);
+          const float av = act_f32<true>(gv, uv, P.act);
+          const float hv = bf16_round(av);
+          if (P.h_quant)
+            store_act32(P, im.off + n, j, av);
+          else
+            store_h(P, im.off + n, j, hv);
           if (dbg) {
             if (im.sh) {
               const int64_t tok = (int64_t)r - P.R;
@@ -725,13 +730,13 @@ __device__ void pf_epilogue(const DecodeParams& P, const PfSync& sy, int64_t n_i
                 P.dbg_sic1[tok * 2 * I + j] = f32_to_bf16_bits(gv);
                 P.dbg_sic1[tok * 2 * I + I + j] = f32_to_bf16_bits(uv);
               }
-              if (P.dbg_sh) P.dbg_sh[tok * I + j] = f32_to_bf16_bits(hv);
+              if (P.dbg_sh && !P.h_quant) P.dbg_sh[tok * I + j] = f32_to_bf16_bits(hv);
             } else {
               if (P.dbg_ic1) {
                 P.dbg_ic1[(int64_t)r * 2 * I + j] = f32_to_bf16_bits(gv);
                 P.dbg_ic1[(int64_t)r * 2 * I + I + j] = f32_to_bf16_bits(uv);
               }
-              if (P.dbg_h) P.dbg_h[(int64_t)r * I + j] = f32_to_bf16_bits(hv);
+              if (P.dbg_h && !P.h_quant) P.dbg_h[(int64_t)r * I + j] = f32_to_bf16_bits(hv);
             }
           }
         }
@@ -974,6 +979,10 @@ int launch_prefill_gemms(const DecodeParams& P, cudaStream_t stream) {
   st = launch_pf<kGateUp>(P, max_seg * (P.I / 64 / kPair), stream);
   prof_mark(FTB_KERNEL_GATE_UP, false, stream);
   if (st) return st;
+  if (P.h_quant) {
+    st = launch_h_fp8(P, false, max_seg, stream);
+    if (st) return st;
+  }
   prof_mark(FTB_KERNEL_DOWN, true, stream);
   st = launch_pf<kDown>(P, max_seg * (P.H / kPfRows / kPair), stream);
   prof_mark(FTB_KERNEL_DOWN, false, stream);

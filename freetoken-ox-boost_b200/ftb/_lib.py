@@ -59,6 +59,8 @@ FTB_ACT_SWIGLUOAI = 2
 FTB_PATH_DECODE = 0
 FTB_PATH_PREFILL = 1
 FTB_PATH_PREFILL_FP4 = 2
+FTB_HQUANT_NONE = 0
+FTB_HQUANT_FP8_BLOCK128 = 1
 
 
 class MoeArgsStruct(ctypes.Structure):
@@ -70,7 +72,7 @@ class MoeArgsStruct(ctypes.Structure):
         ("weight_on_input", _i32), ("path", _i32), ("route_mask", _vp), ("phase", _i32),
         ("out", _vp), ("workspace", _vp), ("workspace_bytes", _sz),
         ("ic1", _vp), ("h", _vp), ("ic3", _vp), ("shared_ic1", _vp), ("shared_h", _vp),
-        ("shared_out", _vp),
+        ("shared_out", _vp), ("h_quant", _i32),
     ]
 
 SIGNATURES = {

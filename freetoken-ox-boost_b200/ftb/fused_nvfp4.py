@@ -31,6 +31,9 @@ from .banks import Nvfp4Bank
 
 _ACTS = {"silu": _lib.FTB_ACT_SILU, "swiglu_clamp": _lib.FTB_ACT_SWIGLU_CLAMP,
          "swigluoai": _lib.FTB_ACT_SWIGLUOAI}
+# rounding of h before the down GEMM: None = bf16 (NVFP4 layers), "fp8_block128" = the FP8
+# round trip per 128 elements of the reference's ds_fp4 layers (fused_swiglu(..., quant=True))
+_HQUANT = {None: _lib.FTB_HQUANT_NONE, "fp8_block128": _lib.FTB_HQUANT_FP8_BLOCK128}
 
 
 def _act_spec(activation: str, act_alpha: float, act_limit: float):
@@ -90,21 +93,24 @@ def moe_decode(x: torch.Tensor, bank: Nvfp4Bank, topk_weights: torch.Tensor,
                topk_ids: torch.Tensor, *, activation: str = "silu", act_limit: float = 7.0,
                act_alpha: float = 1.702, apply_router_weight_on_input: bool = False,
                shared: Nvfp4Bank | None = None, out: torch.Tensor | None = None,
-               debug: bool = False, check_status: bool = False):
-    """Decode layer on a bank object. ``debug=True`` returns (out, intermediates dict)."""
+               debug: bool = False, check_status: bool = False, h_quant: str | None = None):
+    """Decode layer on a bank object. ``debug=True`` returns (out, intermediates dict).
+    ``h_quant="fp8_block128"``: h takes the ds_fp4 layers' FP8 round trip (per 128 elements)."""
     return _layer(_lib.FTB_PATH_DECODE, x, bank, topk_weights, topk_ids, activation, act_alpha,
-                  act_limit, apply_router_weight_on_input, shared, out, debug, check_status)
+                  act_limit, apply_router_weight_on_input, shared, out, debug, check_status,
+                  h_quant=h_quant)
 
 
 def moe_prefill(x: torch.Tensor, bank: Nvfp4Bank, topk_weights: torch.Tensor,
                 topk_ids: torch.Tensor, *, activation: str = "silu", act_limit: float = 7.0,
                 act_alpha: float = 1.702, apply_router_weight_on_input: bool = False,
                 shared: Nvfp4Bank | None = None, out: torch.Tensor | None = None,
-                debug: bool = False, check_status: bool = False):
+                debug: bool = False, check_status: bool = False, h_quant: str | None = None):
     """The same layer on the tensor-core grouped GEMMs (large T). Same contract and result
     as ``moe_decode``; ``debug=True`` returns (out, intermediates dict)."""
     return _layer(_lib.FTB_PATH_PREFILL, x, bank, topk_weights, topk_ids, activation, act_alpha,
-                  act_limit, apply_router_weight_on_input, shared, out, debug, check_status)
+                  act_limit, apply_router_weight_on_input, shared, out, debug, check_status,
+                  h_quant=h_quant)
 
 
 def prefill_fp4_workspace_bytes(T: int, bank: Nvfp4Bank, top_k: int, has_shared: bool) -> int:
@@ -144,9 +150,13 @@ def quant_nvfp4(x: torch.Tensor):
 
 def _layer(path: int, x, bank, topk_weights, topk_ids, activation, act_alpha, act_limit,
            weight_on_input, shared, out, debug, check_status, route_mask=None, phase=0,
-           ws=None):
+           ws=None, h_quant=None):
     dev = _check_inputs(x, bank, topk_weights, topk_ids, shared)
     kind, alpha, limit = _act_spec(activation, act_alpha, act_limit)
+    if h_quant not in _HQUANT:
+        raise ValueError(f"h_quant {h_quant!r} is not one of {list(_HQUANT)}")
+    if h_quant is not None and path == _lib.FTB_PATH_PREFILL_FP4:
+        raise ValueError("the FP4 prefill quantises h to NVFP4 itself; h_quant does not apply")
     T, H = x.shape
     K = topk_ids.shape[1]
     I = bank.inter
@@ -170,6 +180,7 @@ def _layer(path: int, x, bank, topk_weights, topk_ids, activation, act_alpha, ac
     a.path = path
     a.route_mask = route_mask.data_ptr() if route_mask is not None else None
     a.phase = phase
+    a.h_quant = _HQUANT[h_quant]
     a.out = out.data_ptr() if out is not None else None
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
     inter = None

@@ -94,3 +94,31 @@ def make_inputs(tokens: int, hidden: int, experts: int, *, seed: int = 0, stream
         logp = logp - torch.logsumexp(logp, 0)
         logits = logits + logp[None, :]
     return Inputs(x, logits.contiguous(), None)
+
+
+def ds_fp4_matrix(rows: int, cols: int, gen: torch.Generator, device, w_std: float = 0.02):
+    """(packed u8 [rows, cols/2], e8m0 scale u8 [rows, cols/32]): uniform codes as in
+    ``nvfp4_matrix``; one e8m0 scale per 32-element block = 2^ceil(log2(absmax / 6)) of an
+    underlying W ~ N(0, w_std) block (the MXFP4 power-of-two rule)."""
+    packed = torch.randint(0, 256, (rows, cols // 2), dtype=torch.uint8, device=device,
+                           generator=gen)
+    w = torch.randn(rows, cols // 32, 32, device=device, generator=gen) * w_std
+    e = torch.ceil(torch.log2(w.abs().amax(dim=-1) / 6.0)).clamp(-127, 127)
+    return packed, (e + 127).to(torch.uint8).contiguous()
+
+
+def make_ds_fp4_bank(num_experts: int, hidden: int, inter: int, *, seed: int = 0, device="cpu",
+                     w_std: float = 0.02):
+    """A ds_fp4 layer's routed experts (``ds_fp4.DsFp4Bank``), experts drawn in order."""
+    from .ds_fp4 import DsFp4Bank
+
+    E, H, I = num_experts, hidden, inter
+    gen = _gen(device, seed)
+    gu_p = torch.empty(E, 2 * I, H // 2, dtype=torch.uint8, device=device)
+    gu_s = torch.empty(E, 2 * I, H // 32, dtype=torch.uint8, device=device)
+    dn_p = torch.empty(E, H, I // 2, dtype=torch.uint8, device=device)
+    dn_s = torch.empty(E, H, I // 32, dtype=torch.uint8, device=device)
+    for e in range(E):
+        gu_p[e], gu_s[e] = ds_fp4_matrix(2 * I, H, gen, device, w_std)
+        dn_p[e], dn_s[e] = ds_fp4_matrix(H, I, gen, device, w_std)
+    return DsFp4Bank(gu_p, gu_s, dn_p, dn_s)

@@ -171,6 +171,13 @@ FTB_API int ftb_moe_decode(const uint16_t* x, const ftb_nvfp4_bank* bank, const 
  */
 enum { FTB_ACT_SILU = 0, FTB_ACT_SWIGLU_CLAMP = 1, FTB_ACT_SWIGLUOAI = 2 };
 enum { FTB_PATH_DECODE = 0, FTB_PATH_PREFILL = 1, FTB_PATH_PREFILL_FP4 = 2 };
+/* h_quant: FTB_HQUANT_NONE keeps h = bf16(act) (the NVFP4 layers); FTB_HQUANT_FP8_BLOCK128
+ * rounds the fp32 activation through FP8 per 128 elements of a row as the reference's ds_fp4
+ * layers do (patches/kernel_triton_dsv4_fused_moe.patch:25-35): amax = max(max|a|, 1e-4),
+ * e = ceil(log2(amax / 448)), h = e4m3_rn(clamp(a / 2^e, +-448)) * 2^e. Paths DECODE and
+ * PREFILL (not PREFILL_FP4); the debug copy h then holds the rounded h. */
+#define FTB_HQUANT_NONE 0
+#define FTB_HQUANT_FP8_BLOCK128 1
 typedef struct ftb_moe_args {
   const uint16_t* x;             /* [T, H] bf16 */
   const ftb_nvfp4_bank* bank;    /* routed experts */
@@ -195,6 +202,7 @@ typedef struct ftb_moe_args {
   uint16_t* shared_ic1;
   uint16_t* shared_h;
   uint16_t* shared_out;
+  int h_quant;                   /* FTB_HQUANT_*: rounding of h before the down GEMM */
 } ftb_moe_args;
 FTB_API int ftb_moe_layer(const ftb_moe_args* args, ftb_stream_t stream);
 
@@ -377,7 +385,7 @@ enum {
   FTB_KERNEL_EP_PUBLISH = 5,
   FTB_KERNEL_EP_COMBINE = 6,
   FTB_KERNEL_PERMUTE = 7,   /* prefill: permute x rows; FP4 prefill: quantise x rows */
-  FTB_KERNEL_QUANT_H = 8    /* FP4 prefill: quantise h rows */
+  FTB_KERNEL_QUANT_H = 8    /* FP4 prefill: quantise h rows; FTB_HQUANT_FP8_BLOCK128: round h */
 };
 FTB_API int ftb_profile_begin(void);
 FTB_API int ftb_profile_end(int32_t* kernel_ids, float* ms, int max_n);

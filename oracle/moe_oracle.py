@@ -171,6 +171,42 @@ def swiglu(gate: np.ndarray, up: np.ndarray, limit: float = float("inf"), rnd=No
     return (rnd or bf16_round)((g * f32_sigmoid(g)) * u)
 
 
+def f32_log2_ceil(x: np.ndarray) -> np.ndarray:
+    """ceil(log2(x)) of positive normal fp32 values, exactly (``_log2_ceil``, imported at
+    ``patches/kernel_triton_dsv4_fused_moe.patch:10`` from the DSV4 FP8 linear module; its body
+    is upstream and absent, so this DEFINES it as the exact mathematical ceiling)."""
+    m, e = np.frexp(np.asarray(x, np.float64))  # x = m 2^e, m in [0.5, 1)
+    return np.where(m == 0.5, e - 1, e).astype(np.int64)
+
+
+def e4m3_rn(v: np.ndarray) -> np.ndarray:
+    """fp32 -> the nearest E4M3 (fn) value, ties to even mantissa, for |v| <= 448 (the callers
+    clamp first), as fp32: normal binades [2^k, 2^k+1) for k >= -6 step 2^(k-3), below 2^-6
+    the subnormal step 2^-9 (``.to(tl.float8e4nv)``)."""
+    v = np.asarray(v, np.float64)
+    a = np.abs(v)
+    _, e = np.frexp(a)
+    k = np.maximum(e - 1, -6)
+    step = np.ldexp(1.0, k - 3)
+    q = np.minimum(np.rint(a / step) * step, 448.0)
+    return np.copysign(q, v).astype(F32)
+
+
+def fp8_block128_roundtrip(act: np.ndarray) -> np.ndarray:
+    """The ds_fp4 layers' FP8 round trip of the fp32 activation, per 128 consecutive elements of
+    a row (``_swiglu_kernel`` with QUANT, ``patches/kernel_triton_dsv4_fused_moe.patch:25-35``):
+    amax = max(max|a|, 1e-4); e = _log2_ceil(amax * (1/448)) (fp32 multiply); sc = 2^e;
+    q = fp8e4nv(clamp(a / sc, -448, 448)); result q * sc (fp32; exact in bf16)."""
+    a = np.asarray(act, F32)
+    shp = a.shape
+    b = a.reshape(-1, shp[-1] // 128, 128)
+    amax = np.maximum(np.abs(b).max(-1), F32(1e-4)).astype(F32)
+    e = f32_log2_ceil((amax * F32(1.0 / 448.0)).astype(F32))
+    sc = np.ldexp(1.0, e)[..., None]
+    q = e4m3_rn(np.clip(b.astype(np.float64) / sc, -448.0, 448.0))
+    return (q.astype(np.float64) * sc).astype(F32).reshape(shp)
+
+
 # ----------------------------------------------------------------------------------------
 # Router
 # ----------------------------------------------------------------------------------------
@@ -311,7 +347,8 @@ def _f16_to_f32(g) -> np.ndarray:
 
 
 def expert_forward(a: np.ndarray, bank: dict, e: int, limit: float, route_w=None, rnd=None,
-                   act: str | None = None, alpha: float = 1.702, w_on_input: bool = False):
+                   act: str | None = None, alpha: float = 1.702, w_on_input: bool = False,
+                   h_quant: str | None = None):
     """One expert for the rows ``a`` [R, H]: gate_up GEMV -> ic1 (bf16, x global) ->
     SwiGLU -> h (bf16) -> down GEMV -> ic3 = bf16(acc * global * w) (``route_w`` None = no
     routed weight, the shared-expert case).
@@ -322,7 +359,9 @@ def expert_forward(a: np.ndarray, bank: dict, e: int, limit: float, route_w=None
     (``nvfp4_marlin_swiglu.py:120-129``). Rows 0..I-1 of gate_up are gate, I..2I-1 up.
     ``w_on_input`` (``apply_router_weight_on_input=True``) moves the routed weight to the
     gate_up GEMV's epilogue, as the driver's ``mul_routed_weight`` arguments do
-    (``patches/moe_fused_nvfp4.patch:138,145``)."""
+    (``patches/moe_fused_nvfp4.patch:138,145``). ``h_quant="fp8_block128"``: the activation
+    takes ``fp8_block128_roundtrip`` before its bf16 store, as the ds_fp4 decode does
+    (``fused_swiglu(gate_up, swiglu_limit, quant=True)``, ``patches/moe_fused_ds_fp4.patch:33``)."""
     gu_p, gu_s, gu_g = bank["gate_up_packed"][e], bank["gate_up_scale"][e], bank["gate_up_global"][e]
     dn_p, dn_s, dn_g = bank["down_packed"][e], bank["down_scale"][e], bank["down_global"][e]
     rnd = rnd or bf16_round
@@ -332,7 +371,13 @@ def expert_forward(a: np.ndarray, bank: dict, e: int, limit: float, route_w=None
     if w_on_input and rw is not None:
         acc1 = acc1 * rw
     ic1 = rnd(acc1)
-    h = swiglu(ic1[:, :I], ic1[:, I:], limit, rnd, act, alpha)
+    if h_quant == "fp8_block128":
+        h = rnd(fp8_block128_roundtrip(swiglu(ic1[:, :I], ic1[:, I:], limit, lambda v: v, act,
+                                              alpha)))
+    elif h_quant is None:
+        h = swiglu(ic1[:, :I], ic1[:, I:], limit, rnd, act, alpha)
+    else:
+        raise ValueError(f"h_quant {h_quant!r}")
     acc3 = nvfp4_gemv(h, dn_p, dn_s) * _f16_to_f32(dn_g)[None, :]
     if rw is not None and not w_on_input:
         acc3 = acc3 * rw
@@ -341,7 +386,7 @@ def expert_forward(a: np.ndarray, bank: dict, e: int, limit: float, route_w=None
 
 def moe_layer(x: np.ndarray, bank: dict, topk_w: np.ndarray, topk_ids: np.ndarray,
               shared: dict | None = None, limit: float = float("inf"), act: str | None = None,
-              alpha: float = 1.702, w_on_input: bool = False) -> dict:
+              alpha: float = 1.702, w_on_input: bool = False, h_quant: str | None = None) -> dict:
     """Full decode/prefill layer on bf16-valued fp32 inputs.
 
     routed = ``moe_sum_reduce_triton(ic3)`` = bf16(sum over k of fp32(ic3[t,k]), k in order)
@@ -359,7 +404,8 @@ def moe_layer(x: np.ndarray, bank: dict, topk_w: np.ndarray, topk_ids: np.ndarra
     for e in np.unique(ids):
         tt, kk = np.nonzero(ids == e)
         a, b, c = expert_forward(x[tt], bank, int(e), limit, np.asarray(topk_w, F32)[tt, kk],
-                                 act=act, alpha=alpha, w_on_input=w_on_input)
+                                 act=act, alpha=alpha, w_on_input=w_on_input,
+                                 h_quant=h_quant)
         ic1[tt, kk], h[tt, kk], ic3[tt, kk] = a, b, c
     s = ic3[:, 0, :].copy()
     for k in range(1, K):
@@ -367,7 +413,8 @@ def moe_layer(x: np.ndarray, bank: dict, topk_w: np.ndarray, topk_ids: np.ndarra
     routed = bf16_round(s)
     out = {"ic1": ic1, "h": h, "ic3": ic3, "routed": routed, "out": routed}
     if shared is not None:
-        s1, sh, s3 = expert_forward(x, shared, 0, limit, None, act=act, alpha=alpha)
+        s1, sh, s3 = expert_forward(x, shared, 0, limit, None, act=act, alpha=alpha,
+                                    h_quant=h_quant)
         out.update(shared_ic1=s1, shared_h=sh, shared_out=s3, out=bf16_round(routed + s3))
     return out
 

@@ -425,6 +425,8 @@ def run_ftb_single(args, torch):
     if not args.no_prefill:
         out["prefill"] = bench_prefill(torch, ftb, layers, args)
         out["prefill_fp4"] = bench_prefill_fp4(torch, ftb, layers, args)
+    if not args.no_sweep:
+        out["ds_fp4_decode"] = bench_ds_fp4(torch, ftb, args)
     if not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(torch, layers, args.cpu_seconds)
     return out
@@ -606,6 +608,52 @@ def bench_prefill_fp4(torch, ftb, layers: "Layers", args):
                      "hbm_peak_source": hbm_src},
         "gpu_launches_per_step": 7,  # route, sort, quant x, gate_up, quant h, down, combine
         "clocks": clk,
+    }
+
+
+def bench_ds_fp4(torch, ftb, args, T: int = 64, n_layers: int = 2):
+    """ds_fp4 decode (ftb.fused_experts_ds_fp4) at the reference's DSV4-Flash GEMV geometry
+    (gate_up K = 4096, down K = 2048: K_BYTES 2048 / 1024 in patches/moe_fused_ds_fp4.patch:
+    14-21), 256 experts, top-8, no shared expert, T tokens: seeded ds_fp4 banks (e8m0 per 32)
+    converted once to the NVFP4 bank, FP8 round trip of h. HBM roofline of the layer: bytes of
+    the converted experts hit + activations, at the measured copy rate."""
+    from ftb import _lib, synth
+    from ftb.ds_fp4 import nvfp4_from_ds_fp4
+
+    Hd, Id = 4096, 2048
+    banks, inps = [], []
+    for l in range(n_layers):
+        banks.append(nvfp4_from_ds_fp4(synth.make_ds_fp4_bank(E, Hd, Id, seed=500 + l,
+                                                             device="cuda"))[0])
+        inps.append(synth.make_inputs(T, Hd, E, seed=600 + l, device="cuda"))
+    routes = [ftb.fused_topk(None, inp.logits, TOPK, True) for inp in inps]
+    outs = [torch.empty(T, Hd, dtype=torch.bfloat16, device="cuda") for _ in range(n_layers)]
+
+    def step(i):
+        l = i % n_layers
+        w, ids = ftb.fused_topk(None, inps[l].logits, TOPK, True)
+        ftb.fused_experts_ds_fp4(inps[l].x, banks[l], w, ids, 0.0, out=outs[l], prefill=False)
+
+    for i in range(3):
+        step(i)
+    timed = graph_steps(torch, step, n_layers) if args.graphs else step
+    for i in range(3):
+        timed(i)
+    ms = time_steps(torch, timed, min(max(8, args.steps), 200))
+    kt = kernel_times(_lib, torch, step, 16)
+    hbm, hbm_src = measured_peaks()
+    uniq = statistics.mean(int(torch.unique(r[1]).numel()) for r in routes)
+    layer_bytes = uniq * ftb.bank_bytes_per_expert(Hd, Id) + 2 * T * Hd * 2
+    gbs = layer_bytes / (ms * 1e-3) / 1e9
+    return {
+        "workload": f"ds_fp4 decode T={T}: H{Hd} I{Id} E{E} top{TOPK}, no shared expert, "
+                    "e8m0/32 banks converted to NVFP4, FP8 round trip of h",
+        "tokens_per_s": round(T * 1e3 / ms, 1), "ms_per_step": round(ms, 4),
+        "experts_hit_per_step": round(uniq, 1),
+        "kernels_ms": {k: round(statistics.mean(v), 4) for k, v in kt.items()},
+        "layer_hbm_gbs": round(gbs, 1), "hbm_frac": round(gbs / hbm, 4),
+        "hbm_peak_source": hbm_src,
+        "gpu_launches_per_step": 6,  # route, sort_stage, gate_up, h round trip, down, combine
     }
 
 

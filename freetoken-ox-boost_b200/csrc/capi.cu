@@ -33,7 +33,7 @@ struct DecodeWs {
   __half* h16;
   uint16_t* ic3;
   uint16_t* ic3s;
-  __half* xs;  // prefill only
+  __half* xs;  // prefill, and decode when decode_gathers_x
   uint8_t *q4x, *q4x_sf, *q4h, *q4h_sf;  // FP4 prefill only
   float *q4x_g, *q4h_g;
   size_t bytes;
@@ -62,7 +62,8 @@ DecodeWs carve_decode(void* ws, int64_t T, int H, int I, int64_t E, int top_k, i
   w.h16 = c.take<__half>(Rs * I);
   w.ic3 = c.take<uint16_t>(R * H);
   w.ic3s = c.take<uint16_t>(has_shared ? T * H : 1);
-  w.xs = cap == kPrefillSegRoutes && !fp4 ? c.take<__half>(Rs * H) : nullptr;
+  const bool xs = cap == kPrefillSegRoutes ? !fp4 : decode_gathers_x(R, E);
+  w.xs = xs ? c.take<__half>(Rs * H) : nullptr;
   w.q4x = w.q4x_sf = w.q4h = w.q4h_sf = nullptr;
   w.q4x_g = w.q4h_g = nullptr;
   if (fp4) {

@@ -6,29 +6,33 @@
 // shared expert; every rank runs steps of exactly tblk tokens. Each rank holds one exchange
 // region (cudaMalloc, mapped into every other rank with CUDA IPC):
 //   in_flag[8], done_flag[8] u32                 step flags (ep_sync.cuh)
-//   x   [tblk, H] bf16                           this rank's published activations
 //   ids [tblk, top_k] i32, w [tblk, top_k] f32   its routes (global expert ids)
-//   ic3 [W*tblk*top_k, H] bf16                   outputs of the routes this rank computed
-// A step (ftb_ep_forward), all on the caller's stream, with no host synchronisation and
-// fixed launch shapes (CUDA-graph capturable):
-//   1. publish: copy x / ids / w into the region; clear the GEMV work counters;
-//   2. front (k_sort_stage in EP mode): signal "inputs published", wait for every rank;
-//      gather every rank's routes, keep those of the owned experts, sort them; stage the
-//      W*tblk token rows (peer loads) as f16. Slot block b holds rank (rank+b)%W's tokens;
+//   x16 [W*tblk, H] f16, xscale [W*tblk] f32     token rows staged for its experts; slot block
+//                                                b holds rank (rank+b)%W's tokens
+//   ic3 [tblk*top_k, H] bf16                     outputs of its own routes
+// Data moves by stores into the consumer's region, each inside the kernel that produces it:
+//   1. publish: copy ids / w into the region; stage every own token (bf16 -> f16, scale) and
+//      store the row into the x16 of each rank that owns one of its experts (this rank
+//      itself too when a shared expert runs); clear the GEMV work counters;
+//   2. front (k_sort_stage in EP mode, one block): signal "inputs of step n published", wait
+//      for every rank; gather every rank's routes, keep those of the owned experts, sort them;
 //   3. gate_up + down GEMVs (moe_decode_tma.cu) over the owned experts' routes, plus the
-//      shared expert on this rank's own tokens (slots 0..tblk-1); route outputs land in this
-//      rank's ic3 at their slot-order route index;
-//   4. combine: signal "outputs ready", wait for every rank; each own token pulls its top_k
-//      route outputs from the ranks that computed them (peer loads), sums them in k order
-//      (fp32) and adds the shared expert, exactly as the single-GPU combine.
+//      shared expert on this rank's own tokens (slots 0..tblk-1); the down epilogue stores each
+//      route's output straight into its home rank's ic3;
+//   4. combine: signal "outputs ready", wait for every rank; sum each own token's top_k
+//      outputs (now local) in k order (fp32) and add the shared expert, exactly as the
+//      single-GPU combine.
 // A route's output does not depend on which other routes share its launch, so a W-rank step
 // returns the single-GPU layer's bits.
 //
-// Buffer reuse needs no extra barrier: a rank overwrites its published inputs (publish of
-// step n+1) only after its combine of step n saw every rank's "outputs ready" of step n, which
-// each raises after it finished reading those inputs; it overwrites its ic3 (GEMVs of step
-// n+1) only after every rank announced step n+1's inputs, which each does after its own
-// combine of step n, the last reader of ic3.
+// Buffer reuse needs no extra barrier. Rank p writes rank q's x16 for step n+1 (publish) only
+// after p's combine of step n saw every rank's "outputs ready" of step n, which q raises after
+// its GEMVs of step n, the readers of x16; p writes q's ic3 for step n+1 (down) only after p's
+// front of step n+1 saw q's "inputs published" of step n+1, which q raises after its combine
+// of step n, the reader of ic3. The same two facts cover ids / w (read by the fronts) and the
+// flags' visibility: each signal is a system-scope release after a system fence, issued after
+// the stores it covers (earlier kernels on the stream included).
+
 #include <cuda_runtime.h>
 
 #include <cstring>
@@ -57,9 +61,10 @@ constexpr int64_t kEpDefaultWaitNs = 5'000'000'000LL;  // 5 s
 struct EpRegion {
   uint32_t* in_flag;
   uint32_t* done_flag;
-  uint16_t* x;
   int32_t* ids;
   float* w;
+  __half* x16;
+  float* xscale;
   uint16_t* ic3;
   size_t bytes;
 };
@@ -69,10 +74,11 @@ EpRegion carve_region(void* base, int W, int64_t T, int H, int K) {
   EpRegion r;
   r.in_flag = c.take<uint32_t>(kEpMaxWorld);
   r.done_flag = c.take<uint32_t>(kEpMaxWorld);
-  r.x = c.take<uint16_t>(T * H);
   r.ids = c.take<int32_t>(T * K);
   r.w = c.take<float>(T * K);
-  r.ic3 = c.take<uint16_t>((int64_t)W * T * K * H);
+  r.x16 = c.take<__half>((int64_t)W * T * H);
+  r.xscale = c.take<float>((int64_t)W * T);
+  r.ic3 = c.take<uint16_t>(T * K * H);
   r.bytes = c.off;
   return r;
 }
@@ -85,8 +91,6 @@ struct EpWs {
   uint32_t* epoch;
   int32_t* ids_all;
   float* w_all;
-  __half* x16;
-  float* xscale;
   int32_t* offsets;
   int32_t* sorted;
   int32_t* seg_expert;
@@ -95,6 +99,7 @@ struct EpWs {
   int32_t* n_seg;
   __half* h16;
   uint16_t* ic3s;
+  __half* xs;  // x rows in segment order when decode_gathers_x (else null)
   size_t bytes;
 };
 
@@ -109,8 +114,6 @@ EpWs carve_ws(void* base, const ftb_ep& g) {
   w.epoch = c.take<uint32_t>(1);
   w.ids_all = c.take<int32_t>(Ra);
   w.w_all = c.take<float>(Ra);
-  w.x16 = c.take<__half>(Ta * g.H);
-  w.xscale = c.take<float>(Ta);
   w.offsets = c.take<int32_t>(g.per + 1);
   w.sorted = c.take<int32_t>(Ra + g.T);
   const int64_t S = max_segments(Ra, g.per, g.T, g.has_shared);
@@ -120,36 +123,104 @@ EpWs carve_ws(void* base, const ftb_ep& g) {
   w.n_seg = c.take<int32_t>(1);
   w.h16 = c.take<__half>((Ra + g.T) * g.I);
   w.ic3s = c.take<uint16_t>(g.has_shared ? g.T * g.H : 1);
+  w.xs = decode_gathers_x(Ra / g.world, g.per) ? c.take<__half>((Ra + g.T) * g.H) : nullptr;
   w.bytes = c.off;
   return w;
 }
 
 struct PublishParams {
-  const uint4* x;
-  const float* w;
-  const int32_t* ids;
-  uint4* rx;
-  float* rw;
+  EpLinks ep;               // every rank's x16 / xscale (peer memory), this rank's place
+  const uint16_t* x;        // [tblk, H] bf16: this step's tokens
+  const float* w;           // [tblk, top_k]
+  const int32_t* ids;       // [tblk, top_k] global expert ids
+  float* rw;                // this rank's region: published weights and ids
   int32_t* rids;
-  int64_t nx;  // 16-byte vectors of x
-  int64_t nr;  // routes
-  int32_t* ctl;       // control words: all but the sticky status word are zeroed, and the
-  int64_t n_hshift;   // n_hshift per-row h shifts that follow them
-  unsigned long long* trace;
+  int32_t* ctl;             // control words: all but the sticky status word are zeroed, and the
+  int64_t n_hshift;         // n_hshift per-row h shifts that follow them
+  int has_shared;
+  int tpb;                  // tokens per block: 1 (the whole block on a token) or kPubWarps
 };
+
+constexpr int kPubWarps = 8;
+
+// Ranks that need token t's row: the owners of its experts, and this rank for the shared
+// expert. One thread.
+__device__ __forceinline__ uint32_t need_mask(const PublishParams& P, int64_t t) {
+  const EpLinks& L = P.ep;
+  uint32_t mask = P.has_shared ? 1u << L.rank : 0u;
+  for (int k = 0; k < L.top_k; ++k) {
+    const int e = P.ids[t * L.top_k + k];
+    if (e >= 0 && e < L.E) mask |= 1u << (e / L.per);
+  }
+  return mask;
+}
+
+// Stores token t's staged row (f16, x 2^-s, round-interleaved) and scale 2^s into the x16 /
+// xscale of every rank in `mask`, at its slot block for this rank. `lo`, `step`: this thread's
+// 16-byte chunks of the row.
+__device__ __forceinline__ void push_row(const PublishParams& P, int64_t t, uint32_t mask, int s,
+                                         int lo, int step, bool leader) {
+  const EpLinks& L = P.ep;
+  const uint4* xr = reinterpret_cast<const uint4*>(P.x + t * L.H);
+  const int nv = L.H / 8;
+  const float down = exp2f((float)-s);
+  for (uint32_t m = mask; m; m &= m - 1) {
+    const int q = __ffs(m) - 1;
+    const int64_t slot = (int64_t)((L.rank - q + L.world) % L.world) * L.tblk + t;
+    if (leader) L.xscale[q][slot] = exp2f((float)s);
+    uint4* dst = reinterpret_cast<uint4*>(L.x16[q] + slot * L.H);
+    for (int i = lo; i < nv; i += step) dst[ri_chunk(i)] = stage_chunk(xr[i], down);
+  }
+}
 
 __global__ void __launch_bounds__(256) k_ep_publish(const PublishParams P) {
   pdl_launch_dependents();
   pdl_wait();
-  if (threadIdx.x == 0) trace_start(P.trace ? P.trace + kEpTracePublish : nullptr);
+  const EpLinks& L = P.ep;
+  if (threadIdx.x == 0) trace_start(L.trace ? L.trace + kEpTracePublish : nullptr);
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  for (int64_t i = i0; i < P.nx; i += stride) P.rx[i] = P.x[i];
-  for (int64_t i = i0; i < P.nr; i += stride) {
+  const int64_t nr = L.tblk * L.top_k;
+  for (int64_t i = i0; i < nr; i += stride) {
     P.rw[i] = P.w[i];
     P.rids[i] = P.ids[i];
   }
   for (int64_t i = i0 + 1; i < kCtlWords + P.n_hshift; i += stride) P.ctl[i] = 0;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nv = L.H / 8;
+  if (P.tpb == 1) {  // block per token
+    __shared__ float sm_max[32];
+    __shared__ uint32_t sm_mask;
+    const int64_t t = blockIdx.x;
+    if (threadIdx.x == 0) sm_mask = need_mask(P, t);
+    const uint4* xr = reinterpret_cast<const uint4*>(P.x + t * L.H);
+    float m = 0.f;
+    for (int i = threadIdx.x; i < nv; i += blockDim.x) m = chunk_absmax(xr[i], m);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) sm_max[warp] = m;
+    __syncthreads();
+    if (warp == 0) {
+      m = lane < (int)(blockDim.x >> 5) ? sm_max[lane] : 0.f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if (lane == 0) sm_max[0] = m;
+    }
+    __syncthreads();
+    push_row(P, t, sm_mask, stage_exp(sm_max[0]), threadIdx.x, blockDim.x, threadIdx.x == 0);
+  } else {  // warp per token
+    const int64_t t = (int64_t)blockIdx.x * kPubWarps + warp;
+    if (t < L.tblk) {
+      const uint32_t mask = __shfl_sync(0xffffffffu, lane == 0 ? need_mask(P, t) : 0u, 0);
+      const uint4* xr = reinterpret_cast<const uint4*>(P.x + t * L.H);
+      float m = 0.f;
+      for (int i = lane; i < nv; i += kWarp) m = chunk_absmax(xr[i], m);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      push_row(P, t, mask, stage_exp(m), lane, kWarp, lane == 0);
+    }
+  }
+  __threadfence_system();  // the pushed rows before the front's "inputs published" signal
 }
 
 struct CombineParams {
@@ -160,8 +231,9 @@ struct CombineParams {
   int32_t* status;
 };
 
-// out[t] = bf16(f32(bf16(sum_k ic3[t,k])) + f32(shared[t])), k in order, fp32; ic3[t,k] read
-// from the rank that owns expert ids[t,k] (the same arithmetic as k_combine).
+// out[t] = bf16(f32(bf16(sum_k ic3[t,k])) + f32(shared[t])), k in order, fp32; ic3[t,k] was
+// stored into this rank's region by the rank that owns expert ids[t,k] (the same arithmetic as
+// k_combine).
 __global__ void __launch_bounds__(256) k_ep_combine(const CombineParams C) {
   pdl_launch_dependents();
   pdl_wait();
@@ -184,6 +256,7 @@ __global__ void __launch_bounds__(256) k_ep_combine(const CombineParams C) {
     const int H = L.H, K = L.top_k;
     const int64_t nv = H / 8, total = L.tblk * nv;
     const int32_t* ids = L.ids[L.rank];
+    const uint16_t* ic3 = L.ic3[L.rank];
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
       const int64_t t = i / nv, v = i % nv;
@@ -194,10 +267,7 @@ __global__ void __launch_bounds__(256) k_ep_combine(const CombineParams C) {
       for (int k = 0; k < K; ++k) {
         const int e = ids[t * K + k];
         if (e < 0 || e >= L.E) continue;
-        const int o = e / L.per;
-        const int b = (L.rank - o + L.world) % L.world;  // slot block of our tokens on rank o
-        const int64_t r = ((int64_t)b * L.tblk + t) * K + k;
-        const uint4 u = *reinterpret_cast<const uint4*>(L.ic3[o] + r * H + v * 8);
+        const uint4 u = *reinterpret_cast<const uint4*>(ic3 + (t * K + k) * H + v * 8);
         const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -248,9 +318,10 @@ EpLinks make_links(const ftb_ep& g, const EpWs& w) {
   L.H = g.H;
   for (int p = 0; p < g.world; ++p) {
     const EpRegion r = carve_region(g.base[p], g.world, g.T, g.H, g.K);
-    L.x[p] = r.x;
     L.ids[p] = r.ids;
     L.w[p] = r.w;
+    L.x16[p] = r.x16;
+    L.xscale[p] = r.xscale;
     L.ic3[p] = r.ic3;
     L.in_sig[p] = r.in_flag + g.rank;
     L.done_sig[p] = r.done_flag + g.rank;
@@ -395,11 +466,19 @@ static int ep_forward_impl(ftb_ep* g, const uint16_t* x, const float* topk_w,
   const EpLinks L = make_links(*g, w);
   const int64_t Ta = (int64_t)g->world * g->T, Ra = Ta * g->K;
 
-  PublishParams pp{reinterpret_cast<const uint4*>(x), topk_w, topk_ids,
-                   reinterpret_cast<uint4*>(own.x), own.w, own.ids, g->T * g->H / 8,
-                   g->T * g->K, w.status, Ra + g->T, g->trace};
-  int64_t gp = ceil_div(pp.nx, 256);
-  if (gp > sm_count()) gp = sm_count();
+  PublishParams pp{};
+  pp.ep = L;
+  pp.x = x;
+  pp.w = topk_w;
+  pp.ids = topk_ids;
+  pp.rw = own.w;
+  pp.rids = own.ids;
+  pp.ctl = w.status;
+  pp.n_hshift = Ra + g->T;
+  pp.has_shared = g->has_shared;
+  // up to two tokens per SM: a block per token (the shortest latency); beyond, a warp per token
+  pp.tpb = g->T <= 2 * (int64_t)sm_count() ? 1 : kPubWarps;
+  const int64_t gp = ceil_div(g->T, (int64_t)pp.tpb);
   prof_mark(FTB_KERNEL_EP_PUBLISH, true, s);
   st = cuda_status(launch_pdl(k_ep_publish, dim3((unsigned)gp), dim3(256), 0, s, pp));
   prof_mark(FTB_KERNEL_EP_PUBLISH, false, s);
@@ -425,8 +504,8 @@ static int ep_forward_impl(ftb_ep* g, const uint16_t* x, const float* topk_w,
   sp.n_seg = w.n_seg;
   sp.status = w.status;
   sp.x = nullptr;
-  sp.x16 = w.x16;
-  sp.xscale = w.xscale;
+  sp.x16 = nullptr;  // staged by the publish kernels: the front is the sort alone
+  sp.xscale = nullptr;
   sp.H = g->H;
   st = launch_sort_stage(sp, s);
   if (st) return st;
@@ -440,6 +519,8 @@ static int ep_forward_impl(ftb_ep* g, const uint16_t* x, const float* topk_w,
   dp.top_k = g->K;
   dp.T = Ta;
   dp.R = Ra;
+  dp.R_plan = Ra / g->world;  // the routes of the owned experts, on average
+  dp.xs = w.xs;
   dp.Ts = g->T;
   dp.act = act;
   dp.w_on_input = w_on_input ? 1 : 0;
@@ -450,10 +531,12 @@ static int ep_forward_impl(ftb_ep* g, const uint16_t* x, const float* topk_w,
   dp.seg_off = w.seg_off;
   dp.seg_cnt = w.seg_cnt;
   dp.n_seg = w.n_seg;
-  dp.x16 = w.x16;
-  dp.xscale = w.xscale;
+  dp.x16 = own.x16;
+  dp.xscale = own.xscale;
   dp.h16 = w.h16;
-  dp.ic3 = own.ic3;
+  dp.ic3 = nullptr;
+  dp.ic3_block = (int)(g->T * g->K);
+  for (int b = 0; b < g->world; ++b) dp.ic3_home[b] = L.ic3[(g->rank + b) % g->world];
   dp.ic3s = w.ic3s;
   dp.out = nullptr;
   dp.status = w.status;

@@ -68,7 +68,18 @@ enum { kGateUp = 0, kDown = 1 };
 // Tensor maps of one matrix family: routed bank and shared expert, packed rows and scales.
 struct GemvMaps {
   CUtensorMap w, s, sw, ss;
+  CUtensorMap x;  // activation rows in segment order (xs / h16), kXBoxK x kSegRoutes boxes
+  int xbox_min;   // tiles of segments with at least this many routes load x by boxes
 };
+
+// Activation boxes: a segment's (up to) kSegRoutes rows of one stage as kStageK / kXBoxK TMA
+// boxes of kXBoxK f16 (128 bytes, 128-byte swizzle) x kSegRoutes rows, instead of one bulk
+// copy per route (a TMA issue each: at 16 routes those copies, not the weight stream, bounded
+// the GEMV). Rows past the segment are loaded and ignored (past the buffer: zero fill).
+constexpr int kXBoxK = 64;
+constexpr int kXBoxBytes = kXBoxK * 2 * kSegRoutes;              // one box
+constexpr int kXBoxStageBytes = kXBoxBytes * (kStageK / kXBoxK);  // a stage's boxes
+constexpr int kXBoxMinRoutes = 6;  // per-route copies below (fewer copies than boxes' bytes)
 
 struct Layout {
   int RT;            // rows per tile
@@ -139,9 +150,9 @@ __device__ __forceinline__ int tile_rows_total(const DecodeParams& P) {
 
 // Producer warp: claims tiles, and for each stage of a tile waits for the slot to be free,
 // arms the full barrier with the stage's byte count, publishes the tile id and issues the
-// copies (lane 0: the TMA boxes; lanes j < cnt: activation row j). Ends with one sentinel
-// stage (tile -1) that all consumer warps read.
-template <int MODE>
+// copies (lane 0: the TMA boxes; lanes j < cnt: activation row j, or lane 0 the activation
+// boxes, see kXBoxK). Ends with one sentinel stage (tile -1) that all consumer warps read.
+template <int MODE, bool BOXOK>
 __device__ void producer(const DecodeParams& P, const GemvMaps& M, const Layout& L,
                          uint8_t* stages, const Sync& sy, int64_t ntiles, int tpe, int nk,
                          int* work_counter) {
@@ -159,7 +170,7 @@ __device__ void producer(const DecodeParams& P, const GemvMaps& M, const Layout&
     t = __shfl_sync(0xffffffffu, t, 0);
     // tile -> segment, rows, activation sources
     int cnt = 0, e = 0, p = 0, off = 0;
-    bool sh = false;
+    bool sh = false, box = false;
     const uint16_t* xsrc = nullptr;  // lane j's activation row (j < cnt)
     if (t >= 0) {
       const int a = (int)(t / tpe);
@@ -169,7 +180,8 @@ __device__ void producer(const DecodeParams& P, const GemvMaps& M, const Layout&
       cnt = P.seg_cnt[a];
       if (cnt == 0) continue;  // an empty segment (a skipped route of the route-major front)
       sh = (e == P.E);
-      if (lane < cnt) {
+      box = BOXOK && cnt >= M.xbox_min;
+      if (lane < cnt && !box) {
         if (MODE == kGateUp) {
           const int r = P.sorted[off + lane];
           const int64_t tok = sh ? (int64_t)r - P.R : (int64_t)r / P.top_k;
@@ -194,8 +206,8 @@ __device__ void producer(const DecodeParams& P, const GemvMaps& M, const Layout&
           if (t < 0) {
             mbar_arrive(&sy.full[s]);  // sentinel: no bytes
           } else {
-            mbar_arrive_expect_tx(&sy.full[s],
-                                  (uint32_t)(L.wbytes + L.sbytes + cnt * xbytes));
+            mbar_arrive_expect_tx(&sy.full[s], (uint32_t)(L.wbytes + L.sbytes +
+                                                          (box ? kXBoxStageBytes : cnt * xbytes)));
           }
         }
       }
@@ -224,9 +236,16 @@ __device__ void producer(const DecodeParams& P, const GemvMaps& M, const Layout&
           tma_2d(smem_u32(st + L.s_off), sm, kc * 16, y, bar);
         }
       }
-      if (lane < cnt)
+      if (box) {
+        if (lane == 0)
+#pragma unroll
+          for (int j = 0; j < kStageK / kXBoxK; ++j)
+            tma_2d(smem_u32(st + L.x_off + j * kXBoxBytes), &M.x, kc * kStageK + j * kXBoxK,
+                   off, bar);
+      } else if (lane < cnt) {
         bulk_g2s(st + L.x_off + lane * kXPitch, xsrc + (int64_t)kc * kStageK, xbytes,
                  &sy.full[s]);
+      }
     }
     if (aborted || t < 0) break;
   }
@@ -273,8 +292,11 @@ __device__ __forceinline__ void a_lines(int w, int m, int g, int& l0, int& l1) {
   }
 }
 
-// One 128-k round (kh = 0/1 of the stage) for the warp's MT m16 tiles and NT n-tiles.
-template <int MODE, int MT, int NW, int NT>
+// One 128-k round (kh = 0/1 of the stage) for the warp's MT m16 tiles and NT n-tiles. The
+// activation chunk of lane (g, tig) for q is chunk 4q + tig (16 bytes) of the round in row
+// 8nt + g: at that row's kXPitch slot (per-route copies), or (BOX) in box 2kh + q/2, chunk
+// (4q + tig) % 8 of the box's 128-byte line 8nt + g, 128-byte swizzled.
+template <int MODE, int MT, int NW, int NT, bool BOX>
 __device__ __forceinline__ void stage_round(const uint8_t* st, const Layout& L, int w, int lane,
                                             int kh, float (&acc)[MT][NT][4]) {
   const int g = lane >> 2, tig = lane & 3;
@@ -282,9 +304,11 @@ __device__ __forceinline__ void stage_round(const uint8_t* st, const Layout& L, 
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-    for (int q = 0; q < 4; ++q)
-      xb[nt][q] = *reinterpret_cast<const uint4*>(st + L.x_off + (8 * nt + g) * kXPitch +
-                                                  256 * kh + (4 * q + tig) * 16);
+    for (int q = 0; q < 4; ++q) {
+      const int off = BOX ? (2 * kh + (q >> 1)) * kXBoxBytes + swz(8 * nt + g, 4 * (q & 1) + tig)
+                          : (8 * nt + g) * kXPitch + 256 * kh + (4 * q + tig) * 16;
+      xb[nt][q] = *reinterpret_cast<const uint4*>(st + L.x_off + off);
+    }
 #pragma unroll
   for (int m = 0; m < MT; ++m) {
     int l0, l1;
@@ -446,7 +470,15 @@ __device__ void epi_down(const DecodeParams& P, const float (&acc)[MT][NT][4],
         if (r < 0) continue;
         // f = routed weight x 2^hshift (shared expert: 2^hshift); x 1.0 is exact
         const float f = q.f[nt][jj];
-        uint16_t* dst = sh ? P.ic3s + ((int64_t)r - P.R) * H : P.ic3 + (int64_t)r * H;
+        uint16_t* dst;
+        if (sh) {
+          dst = P.ic3s + ((int64_t)r - P.R) * H;
+        } else if (P.ic3_block > 0) {  // expert parallel: straight into the home rank's buffer
+          const int b = r / P.ic3_block;
+          dst = P.ic3_home[b] + (int64_t)(r - b * P.ic3_block) * H;
+        } else {
+          dst = P.ic3 + (int64_t)r * H;
+        }
         dst[na] = f32_to_bf16_bits((acc[m][nt][jj] * q.g0[m]) * f);
         dst[nb] = f32_to_bf16_bits((acc[m][nt][2 + jj] * q.g1[m]) * f);
       }
@@ -456,7 +488,7 @@ __device__ void epi_down(const DecodeParams& P, const float (&acc)[MT][NT][4],
 
 // The warp's share of one tile: nk stages starting at ring position i (whose full barrier
 // the caller has already waited on). Returns the next ring position, or -1 on abort.
-template <int MODE, int MT, int NW, int NT>
+template <int MODE, int MT, int NW, int NT, bool BOX>
 __device__ int64_t warp_tile(const DecodeParams& P, const Layout& L, uint8_t* stages,
                              const Sync& sy, int64_t i, int nk, int K, int w, int lane, int p,
                              int e, int off, int cnt) {
@@ -471,8 +503,8 @@ __device__ int64_t warp_tile(const DecodeParams& P, const Layout& L, uint8_t* st
     const int s = (int)(i % L.stages);
     if (kc > 0 && !sy.wait(&sy.full[s], (uint32_t)(i / L.stages) & 1u)) return -1;
     const uint8_t* st = stages + (size_t)s * L.stage_bytes;
-    stage_round<MODE, MT, NW, NT>(st, L, w, lane, 0, acc);
-    if (K - kc * kStageK > 128) stage_round<MODE, MT, NW, NT>(st, L, w, lane, 1, acc);
+    stage_round<MODE, MT, NW, NT, BOX>(st, L, w, lane, 0, acc);
+    if (K - kc * kStageK > 128) stage_round<MODE, MT, NW, NT, BOX>(st, L, w, lane, 1, acc);
     __syncwarp();
     if (lane == 0) mbar_arrive(&sy.empty[s]);
   }
@@ -492,6 +524,8 @@ __global__ void __launch_bounds__((NW + 1) * kWarp, CPS)
     k_gemv_tma(const __grid_constant__ DecodeParams P, const __grid_constant__ GemvMaps M) {
   extern __shared__ __align__(1024) uint8_t smem[];
   constexpr Layout L = make_layout(MT, NW, XR, CPS);
+  // activation boxes need a kSegRoutes-row x area on a swizzle-atom (1024-byte) boundary
+  constexpr bool kBoxOk = XR == kSegRoutes && L.x_off % 1024 == 0 && XR * kXPitch >= kXBoxStageBytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + kMaxStages;
   int64_t* tile_of = reinterpret_cast<int64_t*>(empty + kMaxStages);
@@ -521,7 +555,7 @@ __global__ void __launch_bounds__((NW + 1) * kWarp, CPS)
   const int tpe = tile_rows_total<MODE>(P) / L.RT;
   const int64_t ntiles = (int64_t)(*P.n_seg) * tpe;
   if (warp == NW) {
-    producer<MODE>(P, M, L, stages, sy, ntiles, tpe, nk, P.work_counter + MODE);
+    producer<MODE, kBoxOk>(P, M, L, stages, sy, ntiles, tpe, nk, P.work_counter + MODE);
     return;
   }
   int64_t i = 0;
@@ -532,10 +566,17 @@ __global__ void __launch_bounds__((NW + 1) * kWarp, CPS)
     if (tile < 0) break;  // sentinel
     const int a = (int)(tile / tpe), p = (int)(tile % tpe);
     const int e = P.seg_expert[a], off = P.seg_off[a], cnt = P.seg_cnt[a];
-    if (cnt > 8)
-      i = warp_tile<MODE, MT, NW, 2>(P, L, stages, sy, i, nk, K, warp, lane, p, e, off, cnt);
+    if (kBoxOk && cnt >= M.xbox_min)  // the producer loaded this tile's x by boxes
+      i = cnt > 8 ? warp_tile<MODE, MT, NW, 2, kBoxOk>(P, L, stages, sy, i, nk, K, warp, lane, p,
+                                                       e, off, cnt)
+                  : warp_tile<MODE, MT, NW, 1, kBoxOk>(P, L, stages, sy, i, nk, K, warp, lane, p,
+                                                       e, off, cnt);
+    else if (cnt > 8)
+      i = warp_tile<MODE, MT, NW, 2, false>(P, L, stages, sy, i, nk, K, warp, lane, p, e, off,
+                                            cnt);
     else
-      i = warp_tile<MODE, MT, NW, 1>(P, L, stages, sy, i, nk, K, warp, lane, p, e, off, cnt);
+      i = warp_tile<MODE, MT, NW, 1, false>(P, L, stages, sy, i, nk, K, warp, lane, p, e, off,
+                                            cnt);
     if (i < 0) break;
   }
   // every consumer warp gets here (aborts break out of the loop too)
@@ -679,8 +720,10 @@ int get_map(CUtensorMap* out, const void* base, uint64_t inner, uint64_t rows,
                     box_rows, swizzle128);
 }
 
+// xbox: the launch may load activations by boxes (its layout has room; gate_up: P.xs holds the
+// gathered rows).
 template <int MODE>
-int make_maps(const DecodeParams& P, int RT, GemvMaps* M) {
+int make_maps(const DecodeParams& P, int RT, bool xbox, GemvMaps* M) {
   const BankView& b = MODE == kGateUp ? P.gu : P.dn;
   const uint64_t K = MODE == kGateUp ? P.H : P.I;
   const uint64_t rows_e = MODE == kGateUp ? 2 * (uint64_t)P.I : (uint64_t)P.H;
@@ -695,15 +738,25 @@ int make_maps(const DecodeParams& P, int RT, GemvMaps* M) {
     M->sw = M->w;
     M->ss = M->s;
   }
+  M->x = M->w;  // unused unless set below
+  M->xbox_min = INT_MAX;
+  const void* xbase = MODE == kGateUp ? static_cast<const void*>(P.xs) : P.h16;
+  if (!st && xbox && xbase) {
+    const uint64_t rows = (uint64_t)P.R + (P.has_shared ? (uint64_t)P.Ts : 0);
+    st = get_map_2d(&M->x, xbase, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, K, rows, kXBoxK,
+                    kSegRoutes, true);
+    M->xbox_min = kXBoxMinRoutes;
+  }
   return st;
 }
 
 template <int MODE, int MT, int NW, int XR, int CPS>
-int launch_one(const DecodeParams& P, int64_t est_tiles, cudaStream_t stream) {
+int launch_one(const DecodeParams& P, int64_t est_tiles, bool gather_x, cudaStream_t stream) {
   constexpr Layout L = make_layout(MT, NW, XR, CPS);
   static_assert(L.stages >= 2, "at least two stages per CTA");
+  constexpr bool kBoxOk = XR == kSegRoutes && L.x_off % 1024 == 0 && XR * kXPitch >= kXBoxStageBytes;
   GemvMaps M;
-  int st = make_maps<MODE>(P, L.RT, &M);
+  int st = make_maps<MODE>(P, L.RT, kBoxOk && (MODE == kDown || gather_x), &M);
   if (st) return st;
   cudaError_t err = cudaFuncSetAttribute(k_gemv_tma<MODE, MT, NW, XR, CPS>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, L.total);
@@ -715,25 +768,46 @@ int launch_one(const DecodeParams& P, int64_t est_tiles, cudaStream_t stream) {
                                 dim3((NW + 1) * kWarp), (size_t)L.total, stream, P, M));
 }
 
-// One launch of the chosen tile rows: 256-row tiles (16 consumer warps) one CTA per SM;
-// 96- and 128-row tiles two CTAs per SM (one wave more often at small T, twice the copies in
-// flight per SM); 8 activation rows per stage when T <= 8 (no segment holds more routes).
+// One launch of the chosen tile rows: 128-row tiles (8 consumer warps) or, for gate_up at
+// small T, 96-row tiles; two CTAs per SM (twice the copies in flight per SM; 128-row tiles
+// measured 4-5% faster than one 256-row CTA per SM at 2.25 to 16 routes per expert); 8
+// activation rows per stage when T <= 8 (no segment holds more routes).
 template <int MODE>
-int launch_rows(const DecodeParams& P, int rows, int64_t max_seg, cudaStream_t stream) {
+int launch_rows(const DecodeParams& P, int rows, int64_t max_seg, bool gather_x,
+                cudaStream_t stream) {
   const int64_t per_e = MODE == kGateUp ? 2 * (int64_t)P.I : P.H;
   const int64_t tiles = max_seg * (per_e / rows);
   const bool x8 = P.T <= 8;
   switch (rows) {
-    case 256: return launch_one<MODE, 1, 16, kSegRoutes, 1>(P, tiles, stream);
     case 128:
-      return x8 ? launch_one<MODE, 1, 8, 8, 2>(P, tiles, stream)
-                : launch_one<MODE, 1, 8, kSegRoutes, 2>(P, tiles, stream);
+      return x8 ? launch_one<MODE, 1, 8, 8, 2>(P, tiles, gather_x, stream)
+                : launch_one<MODE, 1, 8, kSegRoutes, 2>(P, tiles, gather_x, stream);
     case 96:
       if constexpr (MODE == kGateUp)
-        return x8 ? launch_one<MODE, 1, 6, 8, 2>(P, tiles, stream)
-                  : launch_one<MODE, 1, 6, kSegRoutes, 2>(P, tiles, stream);
+        return x8 ? launch_one<MODE, 1, 6, 8, 2>(P, tiles, gather_x, stream)
+                  : launch_one<MODE, 1, 6, kSegRoutes, 2>(P, tiles, gather_x, stream);
       return FTB_ERR_SHAPE;
     default: return FTB_ERR_SHAPE;
+  }
+}
+
+// x rows into segment order for the gate_up's activation boxes: block a copies the rows of
+// segment a (route r: token r / top_k; shared-expert row R + t: token t) from x16 to xs at
+// their sorted positions, a warp per row.
+__global__ void __launch_bounds__(256) k_gather_x(const DecodeParams P) {
+  pdl_launch_dependents();
+  pdl_wait();  // the segment table and x16 come from the front
+  const int a = blockIdx.x;
+  if (a >= *P.n_seg) return;
+  const int off = P.seg_off[a], cnt = P.seg_cnt[a];
+  const bool sh = P.seg_expert[a] == P.E;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nv = P.H / 8;
+  for (int j = warp; j < cnt; j += 8) {
+    const int r = P.sorted[off + j];
+    const int64_t tok = sh ? (int64_t)r - P.R : (int64_t)r / P.top_k;
+    const uint4* src = reinterpret_cast<const uint4*>(P.x16 + tok * P.H);
+    uint4* dst = reinterpret_cast<uint4*>(P.xs + (int64_t)(off + j) * P.H);
+    for (int i = lane; i < nv; i += kWarp) dst[i] = src[i];
   }
 }
 
@@ -742,34 +816,38 @@ int launch_rows(const DecodeParams& P, int rows, int64_t max_seg, cudaStream_t s
 DecodePlan decode_tile_plan(int64_t R, int64_t E, int64_t Ts, int has_shared, int H, int I,
                             int sms) {
   // Expected segments: at least one per distinct expert (<= min(R, E)), at least
-  // R / kSegRoutes when experts hold more routes than a segment (expert-parallel ranks), plus
-  // the shared expert's. 256-row tiles (16 consumer warps) when that still gives every SM
-  // several tiles, else 128-row tiles (8 warps) for balance.
+  // R / kSegRoutes when experts hold more routes than a segment, plus the shared expert's.
+  // 96-row gate_up tiles when the call has few tiles (T of a few tokens) and their makespan
+  // (ceil(tiles / SMs) x tile rows, in weight rows per SM) beats 128-row tiles, else 128.
   const int64_t distinct = R < E ? R : E;
   const int64_t routed_seg = distinct > R / kSegRoutes ? distinct : R / kSegRoutes;
   const int64_t est_seg = routed_seg + (has_shared ? (Ts + kSegRoutes - 1) / kSegRoutes : 0);
-  const int64_t many = 4 * (int64_t)sms;
-  // makespan estimate in weight rows per SM: ceil(tiles / SMs) x tile rows
   auto span = [&](int64_t rows_e, int64_t rt) {
     return ceil_div(est_seg * (rows_e / rt), (int64_t)sms) * rt;
   };
+  // (with several tiles per SM anyway, the wider tiles' lower per-byte overhead wins)
+  const bool few = est_seg * (2 * (int64_t)I / 256) < 4 * (int64_t)sms;
   DecodePlan p;
-  if (est_seg * (2 * (int64_t)I / 256) >= many)
-    p.gate_up_rows = 256;
-  else if ((2 * I) % 96 == 0 && span(2 * I, 96) < span(2 * I, 128))
-    p.gate_up_rows = 96;  // few tiles (T of a few tokens): 96-row tiles even out the last wave
-  else
-    p.gate_up_rows = 128;
-  p.down_rows = est_seg * (H / 256) >= many ? 256 : 128;
+  p.gate_up_rows = few && (2 * I) % 96 == 0 && span(2 * I, 96) < span(2 * I, 128) ? 96 : 128;
+  p.down_rows = 128;
+  p.gather_x = decode_gathers_x(R, E) && p.gate_up_rows == 128 ? 1 : 0;  // 96-row: no boxes
+  (void)H;
   return p;
 }
 
 int launch_decode_gemvs_tma(const DecodeParams& P, cudaStream_t stream) {
   if (P.H % 256 || P.I % 256) return FTB_ERR_SHAPE;
   const int64_t max_seg = max_segments(P.R, P.E, P.Ts, P.has_shared);
-  const DecodePlan plan = decode_tile_plan(P.R, P.E, P.Ts, P.has_shared, P.H, P.I, sm_count());
+  const DecodePlan plan = decode_tile_plan(P.R_plan > 0 ? P.R_plan : P.R, P.E, P.Ts,
+                                           P.has_shared, P.H, P.I, sm_count());
+  const bool gather = plan.gather_x && P.xs;
+  if (gather) {
+    const int st = cuda_status(launch_pdl(k_gather_x, dim3((unsigned)max_seg), dim3(256), 0,
+                                          stream, P));
+    if (st) return st;
+  }
   prof_mark(FTB_KERNEL_GATE_UP, true, stream);
-  int st = launch_rows<kGateUp>(P, plan.gate_up_rows, max_seg, stream);
+  int st = launch_rows<kGateUp>(P, plan.gate_up_rows, max_seg, gather, stream);
   prof_mark(FTB_KERNEL_GATE_UP, false, stream);
   if (st) return st;
   if (P.h_quant) {
@@ -777,7 +855,7 @@ int launch_decode_gemvs_tma(const DecodeParams& P, cudaStream_t stream) {
     if (st) return st;
   }
   prof_mark(FTB_KERNEL_DOWN, true, stream);
-  st = launch_rows<kDown>(P, plan.down_rows, max_seg, stream);
+  st = launch_rows<kDown>(P, plan.down_rows, max_seg, false, stream);
   prof_mark(FTB_KERNEL_DOWN, false, stream);
   return st;
 }

@@ -54,10 +54,13 @@ struct EpLinks {
   int64_t tblk;                       // tokens per rank per step
   int e0, per, E;                     // first owned global expert, experts per rank, all experts
   int top_k, H;
-  const uint16_t* x[kEpMaxWorld];     // rank p's published activations [tblk, H] bf16
   const int32_t* ids[kEpMaxWorld];    // rank p's published top-k ids [tblk, top_k] (global)
   const float* w[kEpMaxWorld];        // rank p's published routed weights [tblk, top_k]
-  const uint16_t* ic3[kEpMaxWorld];   // rank p's route outputs [world*tblk*top_k, H] bf16
+  __half* x16[kEpMaxWorld];           // rank p's staged token rows [world*tblk, H] f16: slot
+                                      // block b holds rank (p + b) % world's tokens (pushed)
+  float* xscale[kEpMaxWorld];         // rank p's staged rows' scales [world*tblk]
+  uint16_t* ic3[kEpMaxWorld];         // rank p's route outputs [tblk*top_k, H] bf16 (pushed by
+                                      // the ranks that own the experts)
   uint32_t* in_sig[kEpMaxWorld];      // rank p's in_flag[this rank]
   uint32_t* done_sig[kEpMaxWorld];    // rank p's done_flag[this rank]
   const uint32_t* in_flag;            // this rank's in_flag[world]: "inputs of step n published"
@@ -162,6 +165,7 @@ struct DecodeParams {
   int64_t Ts;              // shared-expert tokens (rows 0..Ts-1 of x16)
   ActSpec act;             // activation between the GEMVs
   int w_on_input;          // apply_router_weight_on_input: the routed weight scales ic1, not ic3
+  int64_t R_plan;          // routes the launch expects to compute (tile planning); 0 = R
   int h_quant;             // FTB_HQUANT_*: FP8 round trip of h (the gate_up epilogue leaves the
                            // fp32 activation in h16 / hb for launch_h_fp8)
   const float* topk_w;     // [R]
@@ -175,7 +179,8 @@ struct DecodeParams {
   // staged activations
   const __half* x16;
   const float* xscale;
-  __half* xs;              // prefill: x16 rows in sorted (route) order [(R+Ts), H]
+  __half* xs;              // x16 rows in sorted (route) order [(R+Ts), H]: the prefill GEMMs,
+                           // and the decode GEMVs when decode_gathers_x (else null)
   // intermediates
   __half* h16;             // [(R+T), I] sorted order
   uint16_t* ic3;           // [R, H] route order
@@ -189,6 +194,10 @@ struct DecodeParams {
   int32_t* hcount;         // entries of hlist (zeroed per call)
   int32_t* gu_done;        // gate_up CTAs finished (zeroed per call)
   unsigned long long* trace;  // or null: [0] gate_up, [1] down start (min over CTAs, ns)
+  // expert parallelism: the down GEMV stores route r's output at
+  // ic3_home[r / ic3_block] + (r % ic3_block) H (the home rank's buffer, peer memory); 0 = P.ic3
+  int ic3_block;
+  uint16_t* ic3_home[kEpMaxWorld];
   uint16_t* hb;            // [R + Ts, I] bf16 h of the elements beyond the f16 range
   // FP4 prefill (FTB_PATH_PREFILL_FP4): NVFP4 activation rows in sorted order
   const uint16_t* x_in;    // [T, H] bf16 layer input
@@ -237,6 +246,44 @@ __device__ __forceinline__ void store_act32(const DecodeParams& P, int64_t sp, i
   const int64_t idx = sp * P.I + pos;
   reinterpret_cast<uint16_t*>(P.h16)[idx] = (uint16_t)(b >> 16);
   P.hb[idx] = (uint16_t)(b & 0xFFFFu);
+}
+
+// Staging of activation rows (bf16 -> f16 scaled by 2^-s): s from the row's largest magnitude
+// m = f 2^ex (f in [0.5, 1)) is ex - 15, so that max|x| 2^-s lies in [2^14, 2^15); 0 for an
+// all-zero or non-finite row; clamped to [-100, 100].
+__device__ __forceinline__ int stage_exp(float m) {
+  int s = 0;
+  if (m > 0.f && m <= 3.0e38f) {
+    int ex;
+    frexpf(m, &ex);
+    s = ex - 1 - 14;
+    s = s < -100 ? -100 : (s > 100 ? 100 : s);
+  }
+  return s;
+}
+
+// Largest magnitude of the 8 bf16 values of a 16-byte chunk, folded into m.
+__device__ __forceinline__ float chunk_absmax(const uint4& v, float m) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    m = fmaxf(m, fabsf(__uint_as_float(w[j] << 16)));
+    m = fmaxf(m, fabsf(__uint_as_float(w[j] & 0xffff0000u)));
+  }
+  return m;
+}
+
+// 8 bf16 values -> 8 f16 values times `down` (= 2^-s).
+__device__ __forceinline__ uint4 stage_chunk(const uint4& v, float down) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const __half2 h = __floats2half2_rn(__uint_as_float(w[j] << 16) * down,
+                                        __uint_as_float(w[j] & 0xffff0000u) * down);
+    o[j] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 // 2^c for an integer c in [-126, 127].
@@ -319,7 +366,16 @@ inline BankView view_dn(const ftb_nvfp4_bank* b, const ftb_nvfp4_bank* s) {
 struct DecodePlan {
   int gate_up_rows;
   int down_rows;
+  int gather_x;  // gate_up reads x rows gathered into segment order (xs), by TMA boxes
 };
+
+// Decode calls whose segments are expected to hold several routes (at least 4 per distinct
+// expert: expert-parallel ranks, large T) gather the x rows into segment order (P.xs) so the
+// gate_up GEMV can load a segment's rows with a few TMA boxes instead of a copy per route.
+inline bool decode_gathers_x(int64_t R, int64_t E) {
+  const int64_t distinct = R < E ? R : E;
+  return R > kRouteMajorMaxRoutes && R >= 4 * distinct;
+}
 DecodePlan decode_tile_plan(int64_t R, int64_t E, int64_t Ts, int has_shared, int H, int I,
                             int sms);
 

@@ -8,7 +8,8 @@
 //                from the row's max exponent so that max|x|*2^-s lies in [2^14, 2^15): the
 //                f16 tensor-core operand is then exact for every element within 2^-31 of the
 //                row max), stored round-interleaved (ri_chunk) for the GEMV's fragment loads
-//                (plain order for the prefill GEMMs).
+//                (plain order for the prefill GEMMs). Expert-parallel calls stage in the
+//                publish kernel instead (ep.cu) and run block 0 only.
 //
 // The sort is single-CTA: 32 warps each own a contiguous chunk of routes; __match_any_sync
 // ranks equal experts inside a 32-route group, so the result is the same on every run
@@ -278,15 +279,7 @@ __device__ void stage_token_block(const SortParams& P, int64_t t, const uint16_t
   const uint4* xr = reinterpret_cast<const uint4*>(src);
   const int nv = P.H / 8;
   float m = 0.f;
-  for (int i = tid; i < nv; i += blockDim.x) {
-    const uint4 v = xr[i];
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      m = fmaxf(m, fabsf(__uint_as_float(w[j] << 16)));
-      m = fmaxf(m, fabsf(__uint_as_float(w[j] & 0xffff0000u)));
-    }
-  }
+  for (int i = tid; i < nv; i += blockDim.x) m = chunk_absmax(xr[i], m);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
   if (lane == 0) sm_max[warp] = m;
@@ -298,29 +291,12 @@ __device__ void stage_token_block(const SortParams& P, int64_t t, const uint16_t
     if (lane == 0) sm_max[0] = m;
   }
   __syncthreads();
-  m = sm_max[0];
-  int s = 0;
-  if (m > 0.f && m <= 3.0e38f) {
-    int ex;
-    frexpf(m, &ex);  // m = f * 2^ex, f in [0.5, 1)
-    s = ex - 1 - 14;
-    s = s < -100 ? -100 : (s > 100 ? 100 : s);
-  }
+  const int s = stage_exp(sm_max[0]);
   const float down = exp2f((float)-s);
   if (tid == 0) P.xscale[t] = exp2f((float)s);
   uint4* yr = reinterpret_cast<uint4*>(P.x16 + t * P.H);
-  for (int i = tid; i < nv; i += blockDim.x) {
-    const uint4 v = xr[i];
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-    uint32_t o[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const __half2 h = __floats2half2_rn(__uint_as_float(w[j] << 16) * down,
-                                          __uint_as_float(w[j] & 0xffff0000u) * down);
-      o[j] = *reinterpret_cast<const uint32_t*>(&h);
-    }
-    yr[P.x_plain ? i : ri_chunk(i)] = make_uint4(o[0], o[1], o[2], o[3]);
-  }
+  for (int i = tid; i < nv; i += blockDim.x)
+    yr[P.x_plain ? i : ri_chunk(i)] = stage_chunk(xr[i], down);
 }
 
 // The same with one warp per token (large T; H % 256 == 0: 16-byte chunks in whole rounds of
@@ -331,109 +307,29 @@ __device__ void stage_token_warp(const SortParams& P, int64_t t, const uint16_t*
   const int nv = P.H / 8;
   float m = 0.f;
 #pragma unroll 4
-  for (int i = lane; i < nv; i += kWarp) {
-    const uint4 v = xr[i];
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      m = fmaxf(m, fabsf(__uint_as_float(w[j] << 16)));
-      m = fmaxf(m, fabsf(__uint_as_float(w[j] & 0xffff0000u)));
-    }
-  }
+  for (int i = lane; i < nv; i += kWarp) m = chunk_absmax(xr[i], m);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  int s = 0;
-  if (m > 0.f && m <= 3.0e38f) {
-    int ex;
-    frexpf(m, &ex);  // m = f * 2^ex, f in [0.5, 1)
-    s = ex - 1 - 14;
-    s = s < -100 ? -100 : (s > 100 ? 100 : s);
-  }
+  const int s = stage_exp(m);
   const float down = exp2f((float)-s);
   if (lane == 0) P.xscale[t] = exp2f((float)s);
   uint4* yr = reinterpret_cast<uint4*>(P.x16 + t * P.H);
 #pragma unroll 4
-  for (int i = lane; i < nv; i += kWarp) {
-    const uint4 v = xr[i];
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-    uint32_t o[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const __half2 h = __floats2half2_rn(__uint_as_float(w[j] << 16) * down,
-                                          __uint_as_float(w[j] & 0xffff0000u) * down);
-      o[j] = *reinterpret_cast<const uint32_t*>(&h);
-    }
-    yr[P.x_plain ? i : ri_chunk(i)] = make_uint4(o[0], o[1], o[2], o[3]);
-  }
+  for (int i = lane; i < nv; i += kWarp) yr[P.x_plain ? i : ri_chunk(i)] = stage_chunk(xr[i], down);
 }
 
-// One thread, after the home rank's "inputs published" flag: whether token tl of slot block b
-// (home rank `home`) has a route to an expert this rank owns, or is one of this rank's own
-// tokens and a shared expert runs on them. Other tokens are not staged: no route of this
-// rank's launches reads their rows.
-__device__ __forceinline__ bool ep_token_needed(const SortParams& P, int home, int b,
-                                                int64_t tl) {
-  const EpLinks& L = P.ep;
-  if (b == 0 && P.has_shared) return true;
-  const int32_t* ids = L.ids[home] + tl * L.top_k;
-  for (int k = 0; k < L.top_k; ++k) {
-    const int e = ids[k];
-    if (e >= L.e0 && e < L.e0 + L.per) return true;
-  }
-  return false;
-}
-
-// Expert-parallel front (P.ep.world > 0). Token slots are ordered by rank starting with this
-// one: slot block b (tokens b*tblk .. b*tblk+tblk-1) holds rank (rank + b) % world's tokens,
-// so this rank's own tokens are rows 0..tblk-1 (the shared expert's rows).
-//   every block: announce "inputs of step n published" to every rank (the publish kernel ran
-//                before this one), then wait for the ranks whose data it reads;
-//   block 0:     gathers every rank's routes, keeping those of the experts this rank owns
-//                (local ids; others -1) with their weights, then sorts them;
-//   block 1+t:   stages token slot t from its home rank's published row (a peer load), if
-//                the token routes to an owned expert or feeds the shared expert here.
+// Expert-parallel front (P.ep.world > 0), one block. The publish kernels of every rank have
+// pushed the token rows this rank's experts need into its x16 (slot block b = rank
+// (rank + b) % world's tokens, so this rank's own tokens are rows 0..tblk-1, the shared
+// expert's rows). Announces "inputs of step n published" to every rank, waits for every
+// rank's announcement, gathers every rank's routes, keeping those of the experts this rank
+// owns (local ids; others -1) with their weights, and sorts them.
 __device__ void ep_front(const SortParams& P, int* hist) {
   const EpLinks& L = P.ep;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t epoch = *L.epoch + 1;
-  if (threadIdx.x == 0) trace_start(L.trace ? L.trace + kEpTraceFront : nullptr);
-  if (blockIdx.x != 0 && P.stage_tpb == 1) {  // staging: block 1 + t stages token slot t
-    __shared__ int sm_ok1;
-    const int64_t t = (int64_t)blockIdx.x - 1;
-    const int b = (int)(t / L.tblk);
-    const int home = (L.rank + b) % L.world;
-    const int64_t tl = t - b * L.tblk;
-    if (threadIdx.x == 0) {
-      ep_signal(L.in_sig, L.world, epoch);
-      const bool ok = ep_wait(L.in_flag + home, epoch, L.wait_ns);
-      if (!ok) atomicOr(P.status, kStatusTimeout);
-      trace_seen(L.trace ? L.trace + kEpTraceFrontSeen : nullptr);
-      sm_ok1 = ok && ep_token_needed(P, home, b, tl);
-    }
-    __syncthreads();
-    if (sm_ok1) stage_token_block(P, t, L.x[home] + tl * P.H);
-    return;
-  }
-  if (blockIdx.x != 0) {  // staging: warp w stages token slot 32 (block - 1) + w
-    const int64_t t = ((int64_t)blockIdx.x - 1) * kSortWarps + warp;
-    if (t >= P.T) return;
-    const int b = (int)(t / L.tblk);
-    const int home = (L.rank + b) % L.world;
-    const int64_t tl = t - b * L.tblk;
-    int ok = 1;
-    if (lane == 0) {
-      if (threadIdx.x == 0) ep_signal(L.in_sig, L.world, epoch);
-      ok = ep_wait(L.in_flag + home, epoch, L.wait_ns);
-      if (!ok) atomicOr(P.status, kStatusTimeout);
-      trace_seen(L.trace ? L.trace + kEpTraceFrontSeen : nullptr);
-      ok = ok && ep_token_needed(P, home, b, tl);
-    }
-    if (!__shfl_sync(0xffffffffu, ok, 0)) return;
-    stage_token_warp(P, t, L.x[home] + tl * P.H);
-    return;
-  }
   __shared__ int sm_ok;
   if (threadIdx.x == 0) {
+    trace_start(L.trace ? L.trace + kEpTraceFront : nullptr);
     ep_signal(L.in_sig, L.world, epoch);
     bool ok = true;
     for (int p = 0; p < L.world && ok; ++p) ok = ep_wait(L.in_flag + p, epoch, L.wait_ns);
@@ -443,27 +339,25 @@ __device__ void ep_front(const SortParams& P, int* hist) {
   }
   __syncthreads();
   const bool ok = sm_ok != 0;
-  {
-    const int64_t per_rank = L.tblk * L.top_k;
-    const int64_t n = (int64_t)L.world * per_rank;
-    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
-      const int b = (int)(i / per_rank);
-      const int64_t j = i - b * per_rank;
-      int loc = -1;
-      float w = 0.f;
-      if (ok) {
-        const int p = (L.rank + b) % L.world;
-        const int e = L.ids[p][j];
-        w = L.w[p][j];
-        if (e >= L.e0 && e < L.e0 + L.per) loc = e - L.e0;
-        if (b == 0 && (e < 0 || e >= L.E)) atomicOr(P.status, kStatusBadId);
-      }
-      L.ids_all[i] = loc;
-      L.w_all[i] = w;
+  const int64_t per_rank = L.tblk * L.top_k;
+  const int64_t n = (int64_t)L.world * per_rank;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const int b = (int)(i / per_rank);
+    const int64_t j = i - b * per_rank;
+    int loc = -1;
+    float w = 0.f;
+    if (ok) {
+      const int p = (L.rank + b) % L.world;
+      const int e = L.ids[p][j];
+      w = L.w[p][j];
+      if (e >= L.e0 && e < L.e0 + L.per) loc = e - L.e0;
+      if (b == 0 && (e < 0 || e >= L.E)) atomicOr(P.status, kStatusBadId);
     }
-    __syncthreads();
-    sort_block(P, hist);  // P.ids == L.ids_all, P.skip_neg set
+    L.ids_all[i] = loc;
+    L.w_all[i] = w;
   }
+  __syncthreads();
+  sort_block(P, hist);  // P.ids == L.ids_all, P.skip_neg set
 }
 
 __global__ void __launch_bounds__(kSortThreads) k_sort_stage(SortParams P) {

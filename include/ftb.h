@@ -222,8 +222,8 @@ FTB_API int ftb_quant_nvfp4(const uint16_t* x, int is_bf16, int64_t rows, int K,
 
 /*
  * Host-only query (launches nothing): the work-tile rows the decode GEMVs of a call with this
- * shape use on the current device, plan[0] = gate_up (96, 128 or 256), plan[1] = down (128 or
- * 256). Returns FTB_ERR_SHAPE for a shape ftb_moe_decode() rejects. No counterpart in the
+ * shape use on the current device, plan[0] = gate_up (96 or 128), plan[1] = down (128).
+ * Returns FTB_ERR_SHAPE for a shape ftb_moe_decode() rejects. No counterpart in the
  * reference (its Triton launch configuration is fixed per kernel,
  * patches/moe_fused_nvfp4.patch:66-82); it lets tests and callers see which tile variant runs.
  */
@@ -327,7 +327,7 @@ FTB_API int ftb_moe_decode_noalloc(const uint16_t* x, const ftb_nvfp4_bank* bank
  * in rank order (maps every peer's region with CUDA IPC). world == 1 needs no open.
  * ftb_ep_forward(): one layer step on `stream`, the same result as ftb_moe_decode() of the
  * full layer on this rank's tokens (topk ids are global expert ids; local_bank holds the
- * owned experts, num_experts == E/world). It launches four kernels with fixed shapes and no
+ * owned experts, num_experts == E/world). It launches five kernels with fixed shapes and no
  * host synchronisation; ranks order their steps with device-side flags. Every rank must call
  * it the same number of times, in the same layer order. A flag wait that exceeds the wait
  * bound (default 5 s, ftb_ep_set_wait_ns) gives up and sets bit 2 of the status word;

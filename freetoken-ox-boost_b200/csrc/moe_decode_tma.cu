@@ -68,18 +68,19 @@ enum { kGateUp = 0, kDown = 1 };
 // Tensor maps of one matrix family: routed bank and shared expert, packed rows and scales.
 struct GemvMaps {
   CUtensorMap w, s, sw, ss;
-  CUtensorMap x;  // activation rows in segment order (xs / h16), kXBoxK x kSegRoutes boxes
-  int xbox_min;   // tiles of segments with at least this many routes load x by boxes
+  CUtensorMap x;  // box launches: activation rows in segment order (xs / h16), kXBoxK x
+                  // kSegRoutes boxes
 };
 
-// Activation boxes: a segment's (up to) kSegRoutes rows of one stage as kStageK / kXBoxK TMA
-// boxes of kXBoxK f16 (128 bytes, 128-byte swizzle) x kSegRoutes rows, instead of one bulk
-// copy per route (a TMA issue each: at 16 routes those copies, not the weight stream, bounded
-// the GEMV). Rows past the segment are loaded and ignored (past the buffer: zero fill).
+// Activation boxes (launches whose segments are expected to hold several routes): a segment's
+// kSegRoutes rows of one stage as kStageK / kXBoxK TMA boxes of kXBoxK f16 (128 bytes,
+// 128-byte swizzle) x kSegRoutes rows, instead of one bulk copy per route (a TMA issue each: at
+// 16 routes those copies, not the weight stream, bounded the GEMV). Rows past the segment are
+// loaded and ignored (past the buffer: zero fill). A launch uses one kind for all its tiles:
+// both kinds in one kernel doubled the consumer's code and cost 6% at 2 routes per segment.
 constexpr int kXBoxK = 64;
 constexpr int kXBoxBytes = kXBoxK * 2 * kSegRoutes;              // one box
 constexpr int kXBoxStageBytes = kXBoxBytes * (kStageK / kXBoxK);  // a stage's boxes
-constexpr int kXBoxMinRoutes = 6;  // per-route copies below (fewer copies than boxes' bytes)
 
 struct Layout {
   int RT;            // rows per tile
@@ -152,7 +153,7 @@ __device__ __forceinline__ int tile_rows_total(const DecodeParams& P) {
 // arms the full barrier with the stage's byte count, publishes the tile id and issues the
 // copies (lane 0: the TMA boxes; lanes j < cnt: activation row j, or lane 0 the activation
 // boxes, see kXBoxK). Ends with one sentinel stage (tile -1) that all consumer warps read.
-template <int MODE, bool BOXOK>
+template <int MODE, bool BOX>
 __device__ void producer(const DecodeParams& P, const GemvMaps& M, const Layout& L,
                          uint8_t* stages, const Sync& sy, int64_t ntiles, int tpe, int nk,
                          int* work_counter) {
@@ -180,7 +181,7 @@ __device__ void producer(const DecodeParams& P, const GemvMaps& M, const Layout&
       cnt = P.seg_cnt[a];
       if (cnt == 0) continue;  // an empty segment (a skipped route of the route-major front)
       sh = (e == P.E);
-      box = BOXOK && cnt >= M.xbox_min;
+      box = BOX;
       if (lane < cnt && !box) {
         if (MODE == kGateUp) {
           const int r = P.sorted[off + lane];
@@ -519,13 +520,17 @@ __device__ int64_t warp_tile(const DecodeParams& P, const Layout& L, uint8_t* st
   return i;
 }
 
-template <int MODE, int MT, int NW, int XR, int CPS>
+// Activation boxes need a kSegRoutes-row x area on a swizzle-atom (1024-byte) boundary.
+__host__ __device__ constexpr bool box_ok(const Layout& L, int XR) {
+  return XR == kSegRoutes && L.x_off % 1024 == 0 && XR * kXPitch >= kXBoxStageBytes;
+}
+
+template <int MODE, int MT, int NW, int XR, int CPS, bool BOX>
 __global__ void __launch_bounds__((NW + 1) * kWarp, CPS)
     k_gemv_tma(const __grid_constant__ DecodeParams P, const __grid_constant__ GemvMaps M) {
   extern __shared__ __align__(1024) uint8_t smem[];
   constexpr Layout L = make_layout(MT, NW, XR, CPS);
-  // activation boxes need a kSegRoutes-row x area on a swizzle-atom (1024-byte) boundary
-  constexpr bool kBoxOk = XR == kSegRoutes && L.x_off % 1024 == 0 && XR * kXPitch >= kXBoxStageBytes;
+  static_assert(!BOX || box_ok(L, XR), "activation boxes need this layout");
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + kMaxStages;
   int64_t* tile_of = reinterpret_cast<int64_t*>(empty + kMaxStages);
@@ -555,7 +560,7 @@ __global__ void __launch_bounds__((NW + 1) * kWarp, CPS)
   const int tpe = tile_rows_total<MODE>(P) / L.RT;
   const int64_t ntiles = (int64_t)(*P.n_seg) * tpe;
   if (warp == NW) {
-    producer<MODE, kBoxOk>(P, M, L, stages, sy, ntiles, tpe, nk, P.work_counter + MODE);
+    producer<MODE, BOX>(P, M, L, stages, sy, ntiles, tpe, nk, P.work_counter + MODE);
     return;
   }
   int64_t i = 0;
@@ -566,17 +571,10 @@ __global__ void __launch_bounds__((NW + 1) * kWarp, CPS)
     if (tile < 0) break;  // sentinel
     const int a = (int)(tile / tpe), p = (int)(tile % tpe);
     const int e = P.seg_expert[a], off = P.seg_off[a], cnt = P.seg_cnt[a];
-    if (kBoxOk && cnt >= M.xbox_min)  // the producer loaded this tile's x by boxes
-      i = cnt > 8 ? warp_tile<MODE, MT, NW, 2, kBoxOk>(P, L, stages, sy, i, nk, K, warp, lane, p,
-                                                       e, off, cnt)
-                  : warp_tile<MODE, MT, NW, 1, kBoxOk>(P, L, stages, sy, i, nk, K, warp, lane, p,
-                                                       e, off, cnt);
-    else if (cnt > 8)
-      i = warp_tile<MODE, MT, NW, 2, false>(P, L, stages, sy, i, nk, K, warp, lane, p, e, off,
-                                            cnt);
+    if (cnt > 8)
+      i = warp_tile<MODE, MT, NW, 2, BOX>(P, L, stages, sy, i, nk, K, warp, lane, p, e, off, cnt);
     else
-      i = warp_tile<MODE, MT, NW, 1, false>(P, L, stages, sy, i, nk, K, warp, lane, p, e, off,
-                                            cnt);
+      i = warp_tile<MODE, MT, NW, 1, BOX>(P, L, stages, sy, i, nk, K, warp, lane, p, e, off, cnt);
     if (i < 0) break;
   }
   // every consumer warp gets here (aborts break out of the loop too)
@@ -739,32 +737,30 @@ int make_maps(const DecodeParams& P, int RT, bool xbox, GemvMaps* M) {
     M->ss = M->s;
   }
   M->x = M->w;  // unused unless set below
-  M->xbox_min = INT_MAX;
-  const void* xbase = MODE == kGateUp ? static_cast<const void*>(P.xs) : P.h16;
-  if (!st && xbox && xbase) {
+  if (!st && xbox) {
+    const void* xbase = MODE == kGateUp ? static_cast<const void*>(P.xs) : P.h16;
     const uint64_t rows = (uint64_t)P.R + (P.has_shared ? (uint64_t)P.Ts : 0);
-    st = get_map_2d(&M->x, xbase, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, K, rows, kXBoxK,
-                    kSegRoutes, true);
-    M->xbox_min = kXBoxMinRoutes;
+    st = xbase ? get_map_2d(&M->x, xbase, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, K, rows, kXBoxK,
+                            kSegRoutes, true)
+               : FTB_ERR_ARG;
   }
   return st;
 }
 
-template <int MODE, int MT, int NW, int XR, int CPS>
-int launch_one(const DecodeParams& P, int64_t est_tiles, bool gather_x, cudaStream_t stream) {
+template <int MODE, int MT, int NW, int XR, int CPS, bool BOX>
+int launch_one(const DecodeParams& P, int64_t est_tiles, cudaStream_t stream) {
   constexpr Layout L = make_layout(MT, NW, XR, CPS);
   static_assert(L.stages >= 2, "at least two stages per CTA");
-  constexpr bool kBoxOk = XR == kSegRoutes && L.x_off % 1024 == 0 && XR * kXPitch >= kXBoxStageBytes;
   GemvMaps M;
-  int st = make_maps<MODE>(P, L.RT, kBoxOk && (MODE == kDown || gather_x), &M);
+  int st = make_maps<MODE>(P, L.RT, BOX, &M);
   if (st) return st;
-  cudaError_t err = cudaFuncSetAttribute(k_gemv_tma<MODE, MT, NW, XR, CPS>,
+  cudaError_t err = cudaFuncSetAttribute(k_gemv_tma<MODE, MT, NW, XR, CPS, BOX>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, L.total);
   if (err != cudaSuccess) return cuda_status(err);
   int64_t grid = (int64_t)CPS * sm_count();
   if (est_tiles < grid) grid = est_tiles;
   if (grid < 1) grid = 1;
-  return cuda_status(launch_pdl(k_gemv_tma<MODE, MT, NW, XR, CPS>, dim3((unsigned)grid),
+  return cuda_status(launch_pdl(k_gemv_tma<MODE, MT, NW, XR, CPS, BOX>, dim3((unsigned)grid),
                                 dim3((NW + 1) * kWarp), (size_t)L.total, stream, P, M));
 }
 
@@ -772,20 +768,23 @@ int launch_one(const DecodeParams& P, int64_t est_tiles, bool gather_x, cudaStre
 // small T, 96-row tiles; two CTAs per SM (twice the copies in flight per SM; 128-row tiles
 // measured 4-5% faster than one 256-row CTA per SM at 2.25 to 16 routes per expert); 8
 // activation rows per stage when T <= 8 (no segment holds more routes).
+// box: activation boxes (128-row tiles with kSegRoutes rows per stage only).
 template <int MODE>
-int launch_rows(const DecodeParams& P, int rows, int64_t max_seg, bool gather_x,
+int launch_rows(const DecodeParams& P, int rows, int64_t max_seg, bool box,
                 cudaStream_t stream) {
   const int64_t per_e = MODE == kGateUp ? 2 * (int64_t)P.I : P.H;
   const int64_t tiles = max_seg * (per_e / rows);
   const bool x8 = P.T <= 8;
   switch (rows) {
     case 128:
-      return x8 ? launch_one<MODE, 1, 8, 8, 2>(P, tiles, gather_x, stream)
-                : launch_one<MODE, 1, 8, kSegRoutes, 2>(P, tiles, gather_x, stream);
+      if (box) return launch_one<MODE, 1, 8, kSegRoutes, 2, true>(P, tiles, stream);
+      return x8 ? launch_one<MODE, 1, 8, 8, 2, false>(P, tiles, stream)
+                : launch_one<MODE, 1, 8, kSegRoutes, 2, false>(P, tiles, stream);
     case 96:
       if constexpr (MODE == kGateUp)
-        return x8 ? launch_one<MODE, 1, 6, 8, 2>(P, tiles, gather_x, stream)
-                  : launch_one<MODE, 1, 6, kSegRoutes, 2>(P, tiles, gather_x, stream);
+        if (!box)
+          return x8 ? launch_one<MODE, 1, 6, 8, 2, false>(P, tiles, stream)
+                    : launch_one<MODE, 1, 6, kSegRoutes, 2, false>(P, tiles, stream);
       return FTB_ERR_SHAPE;
     default: return FTB_ERR_SHAPE;
   }
@@ -855,7 +854,8 @@ int launch_decode_gemvs_tma(const DecodeParams& P, cudaStream_t stream) {
     if (st) return st;
   }
   prof_mark(FTB_KERNEL_DOWN, true, stream);
-  st = launch_rows<kDown>(P, plan.down_rows, max_seg, false, stream);
+  // down reads h in segment order already: boxes whenever segments are expected to be large
+  st = launch_rows<kDown>(P, plan.down_rows, max_seg, plan.gather_x != 0, stream);
   prof_mark(FTB_KERNEL_DOWN, false, stream);
   return st;
 }

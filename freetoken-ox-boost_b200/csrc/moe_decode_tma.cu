@@ -830,6 +830,7 @@ DecodePlan decode_tile_plan(int64_t R, int64_t E, int64_t Ts, int has_shared, in
   p.gate_up_rows = few && (2 * I) % 96 == 0 && span(2 * I, 96) < span(2 * I, 128) ? 96 : 128;
   p.down_rows = 128;
   p.gather_x = decode_gathers_x(R, E) && p.gate_up_rows == 128 ? 1 : 0;  // 96-row: no boxes
+  p.down_box = decode_routes_per_expert_at_least(R, E, 4) ? 1 : 0;
   (void)H;
   return p;
 }
@@ -855,7 +856,7 @@ int launch_decode_gemvs_tma(const DecodeParams& P, cudaStream_t stream) {
   }
   prof_mark(FTB_KERNEL_DOWN, true, stream);
   // down reads h in segment order already: boxes whenever segments are expected to be large
-  st = launch_rows<kDown>(P, plan.down_rows, max_seg, plan.gather_x != 0, stream);
+  st = launch_rows<kDown>(P, plan.down_rows, max_seg, plan.down_box != 0, stream);
   prof_mark(FTB_KERNEL_DOWN, false, stream);
   return st;
 }

@@ -367,14 +367,23 @@ struct DecodePlan {
   int gate_up_rows;
   int down_rows;
   int gather_x;  // gate_up reads x rows gathered into segment order (xs), by TMA boxes
+  int down_box;  // down reads its h rows (already in segment order) by TMA boxes
 };
 
-// Decode calls whose segments are expected to hold several routes (at least 4 per distinct
-// expert: expert-parallel ranks, large T) gather the x rows into segment order (P.xs) so the
-// gate_up GEMV can load a segment's rows with a few TMA boxes instead of a copy per route.
-inline bool decode_gathers_x(int64_t R, int64_t E) {
+// Expected routes per distinct expert of a decode call with R routes over E experts, times 4
+// (>= 4 * m <=> at least m routes per expert on average).
+inline bool decode_routes_per_expert_at_least(int64_t R, int64_t E, int64_t m) {
   const int64_t distinct = R < E ? R : E;
-  return R > kRouteMajorMaxRoutes && R >= 4 * distinct;
+  return R > kRouteMajorMaxRoutes && R >= m * distinct;
+}
+
+// Decode calls whose segments are expected to hold many routes (>= 12 per distinct expert:
+// expert-parallel ranks at 8 GPUs, large T) gather the x rows into segment order (P.xs) so the
+// gate_up GEMV loads a segment's rows with a few TMA boxes instead of a copy per route (below
+// that the gather costs more than the copies it saves). The down GEMV's rows are in segment
+// order already: it uses boxes from 4 routes per expert.
+inline bool decode_gathers_x(int64_t R, int64_t E) {
+  return decode_routes_per_expert_at_least(R, E, 12);
 }
 DecodePlan decode_tile_plan(int64_t R, int64_t E, int64_t Ts, int has_shared, int H, int I,
                             int sms);

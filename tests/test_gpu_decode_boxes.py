@@ -1,7 +1,7 @@
 """Decode GEMVs whose segments hold many routes: the activation rows of a segment are loaded by
-TMA boxes (segments of >= 6 routes; gate_up from the x rows gathered into segment order when
-the call expects >= 4 routes per distinct expert, down from h), beside per-route copies for
-the small segments of the same launch. Against the oracle (oracle/moe_oracle.py) with the
+TMA boxes (gate_up from the x rows gathered into segment order when the call expects >= 12
+routes per distinct expert, down from h from 4), for every segment of the launch, the small
+ones included. Against the oracle (oracle/moe_oracle.py) with the
 north star's tolerance, max|d| / max|ref| <= 1e-2, for every intermediate and the output;
 and bit for bit against the same routes computed one token at a time (T = 1: one route per
 segment, per-route copies only), since a route's result does not depend on its segment.

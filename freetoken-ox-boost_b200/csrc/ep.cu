@@ -130,9 +130,9 @@ EpWs carve_ws(void* base, const ftb_ep& g) {
 
 struct PublishParams {
   EpLinks ep;               // every rank's x16 / xscale (peer memory), this rank's place
-  const uint16_t* x;        // [tblk, H] bf16: this step's tokens
-  const float* w;           // [tblk, top_k]
-  const int32_t* ids;       // [tblk, top_k] global expert ids
+  const uint16_t* x;        // [n_own, H] bf16: this step's tokens
+  const float* w;           // [n_own, top_k]
+  const int32_t* ids;       // [n_own, top_k] global expert ids
   float* rw;                // this rank's region: published weights and ids
   int32_t* rids;
   int32_t* ctl;             // control words: all but the sticky status word are zeroed, and the
@@ -180,10 +180,11 @@ __global__ void __launch_bounds__(256) k_ep_publish(const PublishParams P) {
   if (threadIdx.x == 0) trace_start(L.trace ? L.trace + kEpTracePublish : nullptr);
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t nr = L.tblk * L.top_k;
+  // the step's routes, then -1 (no expert) in the slots of the tokens this step does not have
+  const int64_t nr = L.tblk * L.top_k, nown = L.n_own * L.top_k;
   for (int64_t i = i0; i < nr; i += stride) {
-    P.rw[i] = P.w[i];
-    P.rids[i] = P.ids[i];
+    P.rw[i] = i < nown ? P.w[i] : 0.f;
+    P.rids[i] = i < nown ? P.ids[i] : -1;
   }
   for (int64_t i = i0 + 1; i < kCtlWords + P.n_hshift; i += stride) P.ctl[i] = 0;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -192,6 +193,7 @@ __global__ void __launch_bounds__(256) k_ep_publish(const PublishParams P) {
     __shared__ float sm_max[32];
     __shared__ uint32_t sm_mask;
     const int64_t t = blockIdx.x;
+    if (t >= L.n_own) return;  // (uniform: a launch without tokens still publishes)
     if (threadIdx.x == 0) sm_mask = need_mask(P, t);
     const uint4* xr = reinterpret_cast<const uint4*>(P.x + t * L.H);
     float m = 0.f;
@@ -210,7 +212,7 @@ __global__ void __launch_bounds__(256) k_ep_publish(const PublishParams P) {
     push_row(P, t, sm_mask, stage_exp(sm_max[0]), threadIdx.x, blockDim.x, threadIdx.x == 0);
   } else {  // warp per token
     const int64_t t = (int64_t)blockIdx.x * kPubWarps + warp;
-    if (t < L.tblk) {
+    if (t < L.n_own) {
       const uint32_t mask = __shfl_sync(0xffffffffu, lane == 0 ? need_mask(P, t) : 0u, 0);
       const uint4* xr = reinterpret_cast<const uint4*>(P.x + t * L.H);
       float m = 0.f;
@@ -254,7 +256,7 @@ __global__ void __launch_bounds__(256) k_ep_combine(const CombineParams C) {
   __syncthreads();
   if (sm_ok) {
     const int H = L.H, K = L.top_k;
-    const int64_t nv = H / 8, total = L.tblk * nv;
+    const int64_t nv = H / 8, total = L.n_own * nv;
     const int32_t* ids = L.ids[L.rank];
     const uint16_t* ic3 = L.ic3[L.rank];
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
@@ -305,10 +307,11 @@ __global__ void __launch_bounds__(256) k_ep_combine(const CombineParams C) {
   }
 }
 
-EpLinks make_links(const ftb_ep& g, const EpWs& w) {
+EpLinks make_links(const ftb_ep& g, const EpWs& w, int64_t n_own) {
   EpLinks L;
   std::memset(&L, 0, sizeof(L));
   L.world = g.world;
+  L.n_own = n_own;
   L.rank = g.rank;
   L.tblk = g.T;
   L.e0 = g.rank * g.per;
@@ -446,14 +449,16 @@ int ftb_ep_set_trace(ftb_ep* g, uint64_t* trace) {
   return FTB_OK;
 }
 
-static int ep_forward_impl(ftb_ep* g, const uint16_t* x, const float* topk_w,
+// n_tokens: this rank's tokens this step (0..tokens_per_rank); the launches keep their shapes.
+static int ep_forward_impl(ftb_ep* g, int64_t n_tokens, const uint16_t* x, const float* topk_w,
                            const int32_t* topk_ids, const ftb_nvfp4_bank* local_bank,
                            const ftb_nvfp4_bank* shared, ActSpec act, int w_on_input,
                            uint16_t* out, ftb_stream_t stream) {
   if (!g || !g->opened) return FTB_ERR_ARG;
   if (act.kind != kActSilu && act.kind != kActSwigluClamp && act.kind != kActSwigluOai)
     return FTB_ERR_ARG;
-  if (!x || !topk_w || !topk_ids || !out) return FTB_ERR_ARG;
+  if (n_tokens < 0 || n_tokens > g->T) return FTB_ERR_SHAPE;
+  if (n_tokens > 0 && (!x || !topk_w || !topk_ids || !out)) return FTB_ERR_ARG;
   if (!bank_ok(local_bank) || local_bank->num_experts != g->per) return FTB_ERR_ARG;
   if ((shared != nullptr) != (g->has_shared != 0) || (shared && !bank_ok(shared)))
     return FTB_ERR_ARG;
@@ -463,7 +468,7 @@ static int ep_forward_impl(ftb_ep* g, const uint16_t* x, const float* topk_w,
   cudaStream_t s = (cudaStream_t)stream;
   const EpWs w = carve_ws(g->ws, *g);
   const EpRegion own = carve_region(g->region, g->world, g->T, g->H, g->K);
-  const EpLinks L = make_links(*g, w);
+  const EpLinks L = make_links(*g, w, n_tokens);
   const int64_t Ta = (int64_t)g->world * g->T, Ra = Ta * g->K;
 
   PublishParams pp{};
@@ -488,7 +493,7 @@ static int ep_forward_impl(ftb_ep* g, const uint16_t* x, const float* topk_w,
   sp.ids = w.ids_all;
   sp.R = Ra;
   sp.T = Ta;
-  sp.Ts = g->T;
+  sp.Ts = n_tokens;  // the shared expert runs on this step's own tokens
   sp.skip_neg = 1;
   sp.ep = L;
   sp.E = g->per;
@@ -568,8 +573,8 @@ static int ep_forward_impl(ftb_ep* g, const uint16_t* x, const float* topk_w,
 int ftb_ep_forward(ftb_ep* g, const uint16_t* x, const float* topk_w, const int32_t* topk_ids,
                    const ftb_nvfp4_bank* local_bank, const ftb_nvfp4_bank* shared,
                    float act_limit, uint16_t* out, ftb_stream_t stream) {
-  return ep_forward_impl(g, x, topk_w, topk_ids, local_bank, shared, act_from_limit(act_limit),
-                         0, out, stream);
+  return ep_forward_impl(g, g ? g->T : 0, x, topk_w, topk_ids, local_bank, shared,
+                         act_from_limit(act_limit), 0, out, stream);
 }
 
 int ftb_ep_forward_act(ftb_ep* g, const uint16_t* x, const float* topk_w,
@@ -577,7 +582,16 @@ int ftb_ep_forward_act(ftb_ep* g, const uint16_t* x, const float* topk_w,
                        const ftb_nvfp4_bank* shared, int activation, float act_alpha,
                        float act_limit, int weight_on_input, uint16_t* out,
                        ftb_stream_t stream) {
-  return ep_forward_impl(g, x, topk_w, topk_ids, local_bank, shared,
+  return ep_forward_impl(g, g ? g->T : 0, x, topk_w, topk_ids, local_bank, shared,
+                         ActSpec{activation, act_alpha, act_limit}, weight_on_input, out, stream);
+}
+
+int ftb_ep_forward_tokens(ftb_ep* g, int64_t n_tokens, const uint16_t* x, const float* topk_w,
+                          const int32_t* topk_ids, const ftb_nvfp4_bank* local_bank,
+                          const ftb_nvfp4_bank* shared, int activation, float act_alpha,
+                          float act_limit, int weight_on_input, uint16_t* out,
+                          ftb_stream_t stream) {
+  return ep_forward_impl(g, n_tokens, x, topk_w, topk_ids, local_bank, shared,
                          ActSpec{activation, act_alpha, act_limit}, weight_on_input, out, stream);
 }
 

@@ -51,7 +51,8 @@ __host__ __device__ inline int64_t max_segments(int64_t R, int64_t E, int64_t T,
 constexpr int kEpMaxWorld = 8;
 struct EpLinks {
   int world, rank;
-  int64_t tblk;                       // tokens per rank per step
+  int64_t tblk;                       // token slots per rank per step (the group's maximum)
+  int64_t n_own;                      // this rank's tokens this step (<= tblk)
   int e0, per, E;                     // first owned global expert, experts per rank, all experts
   int top_k, H;
   const int32_t* ids[kEpMaxWorld];    // rank p's published top-k ids [tblk, top_k] (global)

@@ -351,7 +351,8 @@ __device__ void ep_front(const SortParams& P, int* hist) {
       const int e = L.ids[p][j];
       w = L.w[p][j];
       if (e >= L.e0 && e < L.e0 + L.per) loc = e - L.e0;
-      if (b == 0 && (e < 0 || e >= L.E)) atomicOr(P.status, kStatusBadId);
+      // this rank's own routes (b == 0) past its step's tokens are padding
+      if (b == 0 && j < L.n_own * L.top_k && (e < 0 || e >= L.E)) atomicOr(P.status, kStatusBadId);
     }
     L.ids_all[i] = loc;
     L.w_all[i] = w;

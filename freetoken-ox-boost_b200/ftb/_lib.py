@@ -114,6 +114,8 @@ SIGNATURES = {
     "ftb_ep_forward": (_i32, [_vp, _vp, _vp, _vp, _BP, _BP, _f32, _vp, _vp]),
     "ftb_ep_forward_act": (_i32, [_vp, _vp, _vp, _vp, _BP, _BP, _i32, _f32, _f32, _i32, _vp,
                                   _vp]),
+    "ftb_ep_forward_tokens": (_i32, [_vp, _i64, _vp, _vp, _vp, _BP, _BP, _i32, _f32, _f32, _i32,
+                                     _vp, _vp]),
     "ftb_ep_status": (_i32, [_vp, _i32, _vp]),
     "ftb_ep_destroy": (_i32, [_vp]),
     "ftb_profile_begin": (_i32, []),

@@ -108,22 +108,26 @@ class EpGroup:
                 out: torch.Tensor | None = None, *, activation: str | None = None,
                 act_alpha: float = 1.702, apply_router_weight_on_input: bool = False
                 ) -> torch.Tensor:
-        """One layer step. ``activation=None`` picks silu for an infinite ``act_limit`` and
-        swiglu_clamp otherwise (the reference's two GLM activations); "swigluoai" takes
-        ``act_alpha``."""
+        """One layer step of this rank's tokens: x holds up to ``tokens_per_rank`` rows (a
+        varying serving batch needs no padding; ranks may differ). ``activation=None`` picks
+        silu for an infinite ``act_limit`` and swiglu_clamp otherwise (the reference's two GLM
+        activations); "swigluoai" takes ``act_alpha``."""
         if self._h is None:
             raise RuntimeError("EpGroup is closed")
         dev = require_cuda(x, topk_weights, topk_ids, bank.gate_up_packed)
-        require(x, "hidden_states", torch.bfloat16, (self.T, self.H))
-        require(topk_weights, "topk_weights", torch.float32, (self.T, self.K))
-        require(topk_ids, "topk_ids", torch.int32, (self.T, self.K))
+        n = x.shape[0] if x.dim() == 2 else -1
+        if not 0 <= n <= self.T:
+            raise ValueError(f"hidden_states must be [n, {self.H}] with n <= {self.T}")
+        require(x, "hidden_states", torch.bfloat16, (n, self.H))
+        require(topk_weights, "topk_weights", torch.float32, (n, self.K))
+        require(topk_ids, "topk_ids", torch.int32, (n, self.K))
         bank.validate()
         if bank.num_experts != self.per or bank.hidden != self.H or bank.inter != self.I:
             raise ValueError(f"local bank must hold {self.per} experts of H{self.H} I{self.I}")
         if (shared is not None) != self.has_shared:
             raise ValueError("shared expert presence differs from the group's")
         if out is None:
-            out = torch.empty(self.T, self.H, dtype=torch.bfloat16, device=dev)
+            out = torch.empty(n, self.H, dtype=torch.bfloat16, device=dev)
         from .fused_nvfp4 import _act_spec
 
         if activation is None:
@@ -131,12 +135,13 @@ class EpGroup:
         kind, alpha, limit = _act_spec(activation, act_alpha, act_limit)
         b = bank.struct()
         s = shared.struct() if shared is not None else None
-        st = _lib.load().ftb_ep_forward_act(self._h, ptr(x), ptr(topk_weights), ptr(topk_ids),
-                                            ctypes.byref(b),
-                                            ctypes.byref(s) if s is not None else None, kind,
-                                            alpha, limit, 1 if apply_router_weight_on_input else 0,
-                                            ptr(out), stream_handle(dev))
-        _lib.check("ftb_ep_forward_act", st)
+        st = _lib.load().ftb_ep_forward_tokens(self._h, n, ptr(x), ptr(topk_weights),
+                                               ptr(topk_ids), ctypes.byref(b),
+                                               ctypes.byref(s) if s is not None else None, kind,
+                                               alpha, limit,
+                                               1 if apply_router_weight_on_input else 0,
+                                               ptr(out), stream_handle(dev))
+        _lib.check("ftb_ep_forward_tokens", st)
         return out
 
     def set_trace(self, trace: torch.Tensor | None):

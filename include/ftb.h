@@ -319,8 +319,9 @@ FTB_API int ftb_moe_decode_noalloc(const uint16_t* x, const ftb_nvfp4_bank* bank
  * Expert-parallel decode layer over peer memory (no counterpart in the reference, which streams
  * host-resident experts through an offload cache; here the expert set is resident and sharded).
  * One process per GPU; rank r of `world` (<= 8) owns experts [r*E/world, (r+1)*E/world) and a
- * replica of the shared expert (has_shared). Every step of every rank has exactly
- * tokens_per_rank tokens.
+ * replica of the shared expert (has_shared). A step of a rank has at most tokens_per_rank
+ * tokens (exactly that many through ftb_ep_forward / _act; any count through
+ * ftb_ep_forward_tokens).
  * Setup, collective over the group: ftb_ep_create() on each rank (current device = its GPU;
  * allocates its exchange region and workspace), exchange the FTB_EP_HANDLE_BYTES-byte
  * ftb_ep_handle() of every rank on the host (any channel), then ftb_ep_open() with the handles
@@ -366,6 +367,17 @@ FTB_API int ftb_ep_forward_act(ftb_ep* ep, const uint16_t* x, const float* topk_
                                const ftb_nvfp4_bank* shared, int activation, float act_alpha,
                                float act_limit, int weight_on_input, uint16_t* out,
                                ftb_stream_t stream);
+/* ftb_ep_forward_act() for a step in which this rank has n_tokens tokens, 0 <= n_tokens <=
+ * tokens_per_rank (x, topk_w, topk_ids and out hold n_tokens rows; they may be NULL when
+ * n_tokens is 0): a serving batch of varying size needs no padding, and ranks may differ. The
+ * launches keep the shapes of a full step; n_tokens is a launch argument (a captured graph
+ * replays the count it was captured with). The result for each token equals the full
+ * step's. No counterpart in the reference. */
+FTB_API int ftb_ep_forward_tokens(ftb_ep* ep, int64_t n_tokens, const uint16_t* x,
+                                  const float* topk_w, const int32_t* topk_ids,
+                                  const ftb_nvfp4_bank* local_bank, const ftb_nvfp4_bank* shared,
+                                  int activation, float act_alpha, float act_limit,
+                                  int weight_on_input, uint16_t* out, ftb_stream_t stream);
 FTB_API int ftb_ep_status(ftb_ep* ep, int clear, ftb_stream_t stream);
 FTB_API int ftb_ep_destroy(ftb_ep* ep);
 

@@ -1,12 +1,14 @@
 """Expert parallelism on the GPU.
 
 * 1 GPU: an ``EpGroup`` of world 1 (the peer-memory path with no peers) returns the
-  single-GPU decode bit for bit, over several steps and two layers sharing the group; a
-  traced step fills the phase timestamps in step order.
+  single-GPU decode bit for bit, over several steps and two layers sharing the group, and over
+  steps with fewer tokens than the group's slots (an empty one included); a traced step fills
+  the phase timestamps in step order.
 * 2 GPUs, both transports (NCCL all_to_all and peer memory): each rank's output equals the
   single-GPU decode of the same tokens with the full bank, bit for bit, over several steps
   (one of them with tokens that route to one rank's experts only, which the other does not
-  stage).
+  stage; on the peer-memory transport also steps in which the ranks have different numbers of
+  tokens, below the group's slots).
 * 2 GPUs, peer memory: a rank that stops stepping makes its peer's bounded flag waits give
   up and report the timeout bit, with the peer's process and GPU still usable.
 Multi-GPU cases are skipped with fewer than 2 GPUs.
@@ -65,6 +67,36 @@ def test_ep_world1_p2p_bit_exact():
             assert torch.equal(out.view(torch.int16), ref.view(torch.int16)), step
         assert group.status() == 1  # the planted bad id, nothing else
         assert group.status() == 0  # cleared
+    finally:
+        group.close()
+
+
+def test_ep_world1_fewer_tokens_than_slots():
+    """Steps with fewer tokens than the group's slots (a varying serving batch, no padding):
+    each step's output equals the single-GPU decode of its tokens, bit for bit; an empty step
+    takes part and returns nothing."""
+    import ftb
+    from ftb import synth
+    from ftb.ep import EpGroup
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    bank = synth.make_bank(E, H, I, seed=17, device=dev)
+    shared = synth.make_shared(H, I, seed=17, device=dev)
+    group = EpGroup(T, H, I, E, K, True, 0, 1)
+    try:
+        for step, n in enumerate((T, 4, 1, 0, 7)):
+            inp = synth.make_inputs(max(n, 1), H, E, seed=200 + step, device=dev)
+            x, logits = inp.x[:n].contiguous(), inp.logits[:n].contiguous()
+            w, ids = ftb.fused_topk(x, logits, K, True)
+            out = group.forward(x, w, ids, bank, shared)
+            torch.cuda.synchronize()
+            assert out.shape == (n, H)
+            if n:
+                ref = ftb.moe_decode(x, bank, w, ids, shared=shared)
+                torch.cuda.synchronize()
+                assert torch.equal(out.view(torch.int16), ref.view(torch.int16)), (step, n)
+        assert group.status() == 0
     finally:
         group.close()
 
@@ -138,11 +170,18 @@ def _worker(rank, port, out_dir, transport, mode):
                 result = "idle"
         else:
             same = True
-            for step in range(3):
+            # tokens per step on (rank 0, rank 1): full, then ragged (a serving batch of
+            # varying size on the p2p transport)
+            counts = [(T, T), (T, T), (T, T)]
+            if transport == "p2p":
+                counts += [(T, 5), (3, T), (1, 2)]
+            for step, nt in enumerate(counts):
+                n = nt[rank]
                 inp = synth.make_inputs(T, H, E, seed=5 + step, stream=rank, device=dev)
                 if step == 2:
                     # tokens 0-3 route to rank 0's experts only: rank 1 must not need them
                     inp.logits[:4, E // 2:] -= 50.0
+                inp.x, inp.logits = inp.x[:n].contiguous(), inp.logits[:n].contiguous()
                 out = ep.forward(inp.x, inp.logits)
                 w, ids = ftb.fused_topk(inp.x, inp.logits, K, True)
                 ref = ftb.moe_decode(inp.x, full, w, ids, shared=shared)

@@ -124,6 +124,15 @@ __device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap* map, int
       : "memory");
 }
 
+__device__ __forceinline__ void tma_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z,
+                                       uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
+}
+
 struct Sync {
   uint64_t* full;
   uint64_t* empty;
@@ -225,12 +234,10 @@ __device__ void producer(const DecodeParams& P, const GemvMaps& M, const Layout&
         const CUtensorMap* sm = sh ? &M.ss : &M.s;
         const int ebase = sh ? 0 : e * rows_e;
         if (MODE == kGateUp) {
-          const int h = L.RT / 2;
-          const int y0 = ebase + h * p, y1 = ebase + P.I + h * p;
-          tma_2d(smem_u32(st), wm, kc * 128, y0, bar);
-          tma_2d(smem_u32(st + h * 128), wm, kc * 128, y1, bar);
-          tma_2d(smem_u32(st + L.s_off), sm, kc * 16, y0, bar);
-          tma_2d(smem_u32(st + L.s_off + h * 16), sm, kc * 16, y1, bar);
+          // rows h p .. h p + h of the gate half (z = 2e) and of the up half (z = 2e + 1)
+          const int h = L.RT / 2, z = sh ? 0 : 2 * e;
+          tma_3d(smem_u32(st), wm, kc * 128, h * p, z, bar);
+          tma_3d(smem_u32(st + L.s_off), sm, kc * 16, h * p, z, bar);
         } else {
           const int y = ebase + L.RT * p;
           tma_2d(smem_u32(st), wm, kc * 128, y, bar);
@@ -718,6 +725,17 @@ int get_map(CUtensorMap* out, const void* base, uint64_t inner, uint64_t rows,
                     box_rows, swizzle128);
 }
 
+// A gate_up bank (packed rows or scales) of `experts` experts viewed as [2 experts halves][I
+// rows][kb bytes]: box {kb_box, box_rows, 2} = box_rows gate rows and the same up rows, landing
+// as [2][box_rows][kb_box] (the layout the two 2D boxes of each half would give).
+int gu_map_3d(CUtensorMap* out, const void* base, uint64_t I, uint64_t kb, uint32_t kb_box,
+              uint32_t box_rows, uint64_t experts, bool swizzle128) {
+  const uint64_t dims[3] = {kb, I, 2 * experts};
+  const uint64_t strides[2] = {kb, I * kb};
+  const uint32_t box[3] = {kb_box, box_rows, 2};
+  return get_map_3d(out, base, CU_TENSOR_MAP_DATA_TYPE_UINT8, dims, strides, box, swizzle128);
+}
+
 // xbox: the launch may load activations by boxes (its layout has room; gate_up: P.xs holds the
 // gathered rows).
 template <int MODE>
@@ -726,13 +744,26 @@ int make_maps(const DecodeParams& P, int RT, bool xbox, GemvMaps* M) {
   const uint64_t K = MODE == kGateUp ? P.H : P.I;
   const uint64_t rows_e = MODE == kGateUp ? 2 * (uint64_t)P.I : (uint64_t)P.H;
   const uint32_t box_rows = MODE == kGateUp ? RT / 2 : RT;
-  int st = get_map(&M->w, b.packed, K / 2, rows_e * P.E, 128, box_rows, true);
-  if (!st) st = get_map(&M->s, b.scale, K / 16, rows_e * P.E, 16, box_rows, false);
-  if (st) return st;
-  if (P.has_shared) {
-    st = get_map(&M->sw, b.s_packed, K / 2, rows_e, 128, box_rows, true);
-    if (!st) st = get_map(&M->ss, b.s_scale, K / 16, rows_e, 16, box_rows, false);
+  int st;
+  if (MODE == kGateUp) {
+    // [2E halves][I rows][bytes]: one box = a tile's RT/2 gate rows and the matching up rows
+    // (one TMA issue instead of two, for the packed rows and for the scales)
+    st = gu_map_3d(&M->w, b.packed, P.I, K / 2, 128, box_rows, P.E, true);
+    if (!st) st = gu_map_3d(&M->s, b.scale, P.I, K / 16, 16, box_rows, P.E, false);
+    if (!st && P.has_shared) {
+      st = gu_map_3d(&M->sw, b.s_packed, P.I, K / 2, 128, box_rows, 1, true);
+      if (!st) st = gu_map_3d(&M->ss, b.s_scale, P.I, K / 16, 16, box_rows, 1, false);
+    }
   } else {
+    st = get_map(&M->w, b.packed, K / 2, rows_e * P.E, 128, box_rows, true);
+    if (!st) st = get_map(&M->s, b.scale, K / 16, rows_e * P.E, 16, box_rows, false);
+    if (!st && P.has_shared) {
+      st = get_map(&M->sw, b.s_packed, K / 2, rows_e, 128, box_rows, true);
+      if (!st) st = get_map(&M->ss, b.s_scale, K / 16, rows_e, 16, box_rows, false);
+    }
+  }
+  if (st) return st;
+  if (!P.has_shared) {
     M->sw = M->w;
     M->ss = M->s;
   }

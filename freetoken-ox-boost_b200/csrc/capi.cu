@@ -34,8 +34,6 @@ struct DecodeWs {
   uint16_t* ic3;
   uint16_t* ic3s;
   __half* xs;  // prefill, and decode when decode_gathers_x
-  int32_t* seg_done;  // decode: readiness counters of the fused small-T launch
-  int64_t n_ctl;      // words cleared per call from status on
   uint8_t *q4x, *q4x_sf, *q4h, *q4h_sf;  // FP4 prefill only
   float *q4x_g, *q4h_g;
   size_t bytes;
@@ -48,20 +46,15 @@ DecodeWs carve_decode(void* ws, int64_t T, int H, int I, int64_t E, int top_k, i
   const int64_t Rs = R + (has_shared ? T : 0);
   Carver c(ws);
   DecodeWs w;
-  // control words (kCtl*), then hshift [Rs], then (decode) the per-segment readiness counters
-  // of the fused small-T launch, all cleared by the front at each call
-  const int64_t S = max_segments(R, E, T, has_shared, cap);
-  const int64_t nseg_words = cap == kSegRoutes ? S : 0;
-  w.status = c.take<int32_t>(kCtlWords + Rs + nseg_words);
+  w.status = c.take<int32_t>(kCtlWords + Rs);  // control words (kCtl*), then hshift
   w.hshift = w.status ? w.status + kCtlWords : nullptr;
-  w.seg_done = nseg_words && w.status ? w.hshift + Rs : nullptr;
-  w.n_ctl = kCtlWords + Rs + nseg_words;
   w.hlist = c.take<int32_t>(Rs);
   w.hb = c.take<uint16_t>(Rs * I);
   w.x16 = c.take<__half>(T * H);
   w.xscale = c.take<float>(T);
   w.offsets = c.take<int32_t>(E + 1);
   w.sorted = c.take<int32_t>(Rs);
+  const int64_t S = max_segments(R, E, T, has_shared, cap);
   w.seg_expert = c.take<int32_t>(S);
   w.seg_off = c.take<int32_t>(S);
   w.seg_cnt = c.take<int32_t>(S);
@@ -210,8 +203,8 @@ static int layer_impl(const ftb_moe_args& a, cudaStream_t stream) {
   const int64_t Rs = R + (has_shared ? T : 0);
 
   SortParams sp{};
-  sp.zero_words = w.status;  // control words, the per-row h shifts, the segment counters
-  sp.n_zero = w.n_ctl;
+  sp.zero_words = w.status;  // control words and the per-row h shifts
+  sp.n_zero = kCtlWords + Rs;
   sp.ids = a.topk_ids;
   sp.route_mask = a.route_mask;
   sp.R = R;
@@ -251,10 +244,6 @@ static int layer_impl(const ftb_moe_args& a, cudaStream_t stream) {
   dp.act = ActSpec{a.activation, a.act_alpha, a.act_limit};
   dp.w_on_input = a.weight_on_input ? 1 : 0;
   dp.h_quant = a.h_quant;
-  // a few routes: gate_up and down in one launch (not with the FP8 round trip of h, which
-  // runs between them)
-  dp.fused = sp.route_major && !a.h_quant && w.seg_done ? 1 : 0;
-  dp.seg_done = w.seg_done;
   dp.topk_w = a.topk_w;
   dp.topk_ids = a.topk_ids;
   dp.sorted = w.sorted;

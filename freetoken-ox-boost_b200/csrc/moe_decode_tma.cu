@@ -589,270 +589,6 @@ __global__ void __launch_bounds__((NW + 1) * kWarp, CPS)
 }
 
 // ---------------------------------------------------------------------------------------
-// Fused small-T decode. At a few tokens (the route-major front: one route per segment) each
-// GEMV launch is one latency-bound wave of tiles, and the down launch starts only after the
-// whole gate_up launch has drained. Here one persistent launch claims the gate_up tiles and then
-// the down tiles from one counter. A down tile streams its weight stages at once and issues its
-// activation (h) copies once its segment's h is final: every consumer warp counts its finished
-// gate_up tiles into seg_done[segment], and the warp that completes a segment rewrites the
-// segment's h rows beyond the f16 range (as finish_gate_up does for a whole launch) and marks
-// it ready. A down tile is claimed only after every gate_up tile has been claimed, and a
-// producer issues all stages of a claimed tile before claiming the next, so every wait ends;
-// each is bounded all the same. gate_up and down tiles share one stage layout (128 rows).
-
-constexpr int32_t kSegReady = 1 << 30;
-
-struct FusedMaps {
-  GemvMaps gu, dn;
-};
-
-__device__ __forceinline__ int32_t ld_acquire_gpu(const int32_t* p) {
-  int32_t v;
-  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-// Generic-proxy writes (h, by the gate_up epilogues) before async-proxy reads (bulk copies).
-__device__ __forceinline__ void fence_proxy_async() {
-  asm volatile("fence.proxy.async.global;" ::: "memory");
-}
-
-// Lane 0: wait (bounded) until segment a's h is final.
-__device__ bool wait_segment(const DecodeParams& P, const Sync& sy, int a) {
-  for (uint32_t it = 0; it < kSpinLimit; ++it) {
-    if (*sy.abort) return false;
-    if (ld_acquire_gpu(P.seg_done + a) >= kSegReady) return true;
-    if (it > 16) __nanosleep(64);
-  }
-  *sy.abort = 1;
-  atomicOr(sy.status, kStatusTimeout);
-  return false;
-}
-
-// One consumer warp after its share of gate_up tile (segment a): count it; the warp that
-// completes the segment (all warps of all its tiles, `target` arrivals) rewrites the segment's
-// listed rows of h (f16(h 2^-c) from the bf16 copy where f16 overflowed) and marks it ready.
-__device__ void gate_up_arrive(const DecodeParams& P, int a, int off, int cnt, int target,
-                               int lane) {
-  fence_proxy_async();
-  __threadfence();
-  __syncwarp();
-  int last = 0;
-  if (lane == 0) last = atomicAdd(P.seg_done + a, 1) == target - 1;
-  if (!__shfl_sync(0xffffffffu, last, 0)) return;
-  __threadfence();
-  const int n = *reinterpret_cast<volatile int*>(P.hcount);
-  for (int i = 0; i < n; ++i) {
-    const int64_t sp = __ldcg(P.hlist + i);
-    if (sp < off || sp >= off + cnt) continue;
-    const float f = pow2i(-__ldcg(P.hshift + sp));
-    __half* row = P.h16 + sp * P.I;
-    const uint16_t* brow = P.hb + sp * P.I;
-    for (int k = lane; k < P.I; k += 32) {
-      const unsigned short u = __ldcg(reinterpret_cast<const unsigned short*>(row + k));
-      const float v = (u & 0x7FFFu) == 0x7C00u ? bf16_bits_to_f32(__ldcg(brow + k))
-                                               : __half2float(__ushort_as_half(u));
-      row[k] = __float2half_rn(v * f);
-    }
-  }
-  fence_proxy_async();
-  __threadfence();
-  __syncwarp();
-  if (lane == 0) atomicAdd(P.seg_done + a, kSegReady);
-}
-
-// The fused launch's producer warp (the ring protocol of producer()). A down tile's activation
-// copies wait for its segment; until then its stages hold weights only, and a slot whose
-// consumers are such a pending stage is reused only after the copies went out.
-template <int XR>
-__device__ void producer_fused(const DecodeParams& P, const FusedMaps& M, const Layout& L,
-                               uint8_t* stages, const Sync& sy, int64_t ngu, int64_t ntiles,
-                               int tpe_gu, int tpe_dn) {
-  const int lane = threadIdx.x & 31;
-  int64_t i = 0;
-  bool aborted = false;
-  for (;;) {
-    int64_t t = 0;
-    if (lane == 0) {
-      t = atomicAdd(P.work_counter, 1);
-      if (t >= ntiles) t = -1;
-    }
-    t = __shfl_sync(0xffffffffu, t, 0);
-    const bool gu = t >= 0 && t < ngu;
-    int cnt = 0, e = 0, p = 0, off = 0, a = 0;
-    bool sh = false;
-    const uint16_t* xsrc = nullptr;
-    if (t >= 0) {
-      a = (int)(gu ? t / tpe_gu : (t - ngu) / tpe_dn);
-      p = (int)(gu ? t % tpe_gu : (t - ngu) % tpe_dn);
-      e = P.seg_expert[a];
-      off = P.seg_off[a];
-      cnt = P.seg_cnt[a];
-      if (cnt == 0) continue;
-      sh = (e == P.E);
-      if (lane < cnt) {
-        if (gu) {
-          const int r = P.sorted[off + lane];
-          const int64_t tok = sh ? (int64_t)r - P.R : (int64_t)r / P.top_k;
-          xsrc = reinterpret_cast<const uint16_t*>(P.x16) + tok * P.H;
-        } else {
-          xsrc = reinterpret_cast<const uint16_t*>(P.h16) + (int64_t)(off + lane) * P.I;
-        }
-      }
-    }
-    const int K = gu ? P.H : P.I;
-    const int nstage = t >= 0 ? K / kStageK : 1;
-    const uint32_t xbytes = kStageK * 2;
-    bool ready = gu;     // gate_up reads x, staged before this launch
-    int npend = 0;       // stages issued without their activation copies: ring positions
-    int64_t pend_i = 0;  // pend_i .., k chunks pend_kc ..
-    int pend_kc = 0;
-    auto flush = [&]() {
-      if (!gu) fence_proxy_async();  // h was written in this launch
-      for (int j = 0; j < npend; ++j) {
-        const int s2 = (int)((pend_i + j) % L.stages);
-        if (lane < cnt)
-          bulk_g2s(stages + (size_t)s2 * L.stage_bytes + L.x_off + lane * kXPitch,
-                   xsrc + (int64_t)(pend_kc + j) * kStageK, xbytes, &sy.full[s2]);
-      }
-      npend = 0;
-    };
-    for (int kc = 0; kc < nstage; ++kc, ++i) {
-      const int s = (int)(i % L.stages);
-      const int64_t round = i / L.stages;
-      if (npend > 0 && i - L.stages >= pend_i) {  // the slot's consumers are pending ones
-        int ok = 1;
-        if (!ready && lane == 0) ok = wait_segment(P, sy, a);
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) {
-          aborted = true;
-          break;
-        }
-        ready = true;
-        flush();
-      }
-      int go = 1;
-      if (lane == 0) {
-        if (round > 0 && !sy.wait(&sy.empty[s], (uint32_t)(round - 1) & 1u)) {
-          go = -1;
-        } else {
-          sy.tile_of[s] = t;
-          if (t < 0)
-            mbar_arrive(&sy.full[s]);
-          else
-            mbar_arrive_expect_tx(&sy.full[s], (uint32_t)(L.wbytes + L.sbytes + cnt * xbytes));
-        }
-      }
-      go = __shfl_sync(0xffffffffu, go, 0);
-      if (go < 0) {
-        aborted = true;
-        break;
-      }
-      if (t < 0) continue;
-      uint8_t* st = stages + (size_t)s * L.stage_bytes;
-      const uint32_t bar = smem_u32(&sy.full[s]);
-      if (lane == 0) {
-        if (gu) {
-          const int h = L.RT / 2, z = sh ? 0 : 2 * e;
-          tma_3d(smem_u32(st), sh ? &M.gu.sw : &M.gu.w, kc * 128, h * p, z, bar);
-          tma_3d(smem_u32(st + L.s_off), sh ? &M.gu.ss : &M.gu.s, kc * 16, h * p, z, bar);
-        } else {
-          const int y = (sh ? 0 : e * P.H) + L.RT * p;
-          tma_2d(smem_u32(st), sh ? &M.dn.sw : &M.dn.w, kc * 128, y, bar);
-          tma_2d(smem_u32(st + L.s_off), sh ? &M.dn.ss : &M.dn.s, kc * 16, y, bar);
-        }
-      }
-      if (!ready) {  // a cheap look: is the segment's h final already?
-        int r = 0;
-        if (lane == 0) r = ld_acquire_gpu(P.seg_done + a) >= kSegReady;
-        ready = __shfl_sync(0xffffffffu, r, 0) != 0;
-      }
-      if (npend == 0) {
-        pend_i = i;
-        pend_kc = kc;
-      }
-      ++npend;
-      if (ready) flush();
-    }
-    if (!aborted && t >= 0 && npend > 0) {
-      int ok = 1;
-      if (!ready && lane == 0) ok = wait_segment(P, sy, a);
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (ok)
-        flush();
-      else
-        aborted = true;
-    }
-    if (aborted || t < 0) break;
-  }
-  // after an abort: copies still in flight must land before the CTA exits
-  if (lane != 0 || (!aborted && !*sy.abort)) return;
-  const int64_t issued = i;
-  for (int64_t j = issued - L.stages > 0 ? issued - L.stages : 0; j < issued; ++j) {
-    const int s = (int)(j % L.stages);
-    for (uint32_t it = 0; it < kSpinLimit; ++it) {
-      if (mbar_try_wait(&sy.full[s], (uint32_t)(j / L.stages) & 1u)) break;
-      __nanosleep(64);
-    }
-  }
-}
-
-template <int XR>
-__global__ void __launch_bounds__(9 * kWarp, 2)
-    k_gemv_fused(const __grid_constant__ DecodeParams P, const __grid_constant__ FusedMaps M) {
-  constexpr int NW = 8;
-  extern __shared__ __align__(1024) uint8_t smem[];
-  constexpr Layout L = make_layout(1, NW, XR, 2);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* empty = full + kMaxStages;
-  int64_t* tile_of = reinterpret_cast<int64_t*>(empty + kMaxStages);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tile_of + kMaxStages);
-  uint8_t* stages = smem + kHeader;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  pdl_launch_dependents();
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < L.stages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], NW);
-    }
-    *abort_flag = 0;
-    fence_mbar_init();
-  }
-  __syncthreads();
-  pdl_wait();  // the segment table, activations and work counter come from earlier launches
-  if (P.trace && threadIdx.x == 0) trace_start(P.trace);
-  const Sync sy{full, empty, tile_of, abort_flag, P.status};
-  const int tpe_gu = 2 * P.I / L.RT, tpe_dn = P.H / L.RT;
-  const int64_t nseg = *P.n_seg;
-  const int64_t ngu = nseg * tpe_gu, ntiles = ngu + nseg * tpe_dn;
-  if (warp == NW) {
-    producer_fused<XR>(P, M, L, stages, sy, ngu, ntiles, tpe_gu, tpe_dn);
-    return;
-  }
-  int64_t i = 0;
-  for (;;) {
-    const int s = (int)(i % L.stages);
-    if (!sy.wait(&full[s], (uint32_t)(i / L.stages) & 1u)) break;
-    const int64_t tile = tile_of[s];
-    if (tile < 0) break;  // sentinel
-    const bool gu = tile < ngu;
-    const int a = (int)(gu ? tile / tpe_gu : (tile - ngu) / tpe_dn);
-    const int p = (int)(gu ? tile % tpe_gu : (tile - ngu) % tpe_dn);
-    const int e = P.seg_expert[a], off = P.seg_off[a], cnt = P.seg_cnt[a];
-    if (gu) {
-      i = warp_tile<kGateUp, 1, NW, 1, false>(P, L, stages, sy, i, P.H / kStageK, P.H, warp,
-                                              lane, p, e, off, cnt);
-      if (i < 0) break;
-      gate_up_arrive(P, a, off, cnt, NW * tpe_gu, lane);
-    } else {
-      i = warp_tile<kDown, 1, NW, 1, false>(P, L, stages, sy, i, P.I / kStageK, P.I, warp, lane,
-                                            p, e, off, cnt);
-      if (i < 0) break;
-    }
-  }
-}
-
-// ---------------------------------------------------------------------------------------
 // host: tensor maps (cached by address and shape) and launches
 
 PFN_cuTensorMapEncodeTiled encode_fn() {
@@ -1122,11 +858,7 @@ DecodePlan decode_tile_plan(int64_t R, int64_t E, int64_t Ts, int has_shared, in
   // (with several tiles per SM anyway, the wider tiles' lower per-byte overhead wins)
   const bool few = est_seg * (2 * (int64_t)I / 256) < 4 * (int64_t)sms;
   DecodePlan p;
-  // the route-major front's sizes run gate_up and down in one launch, 128-row tiles for both
-  p.fused = R <= kRouteMajorMaxRoutes && R <= E ? 1 : 0;
-  p.gate_up_rows = !p.fused && few && (2 * I) % 96 == 0 && span(2 * I, 96) < span(2 * I, 128)
-                       ? 96
-                       : 128;
+  p.gate_up_rows = few && (2 * I) % 96 == 0 && span(2 * I, 96) < span(2 * I, 128) ? 96 : 128;
   p.down_rows = 128;
   p.gather_x = decode_gathers_x(R, E) && p.gate_up_rows == 128 ? 1 : 0;  // 96-row: no boxes
   p.down_box = decode_routes_per_expert_at_least(R, E, 4) ? 1 : 0;
@@ -1139,24 +871,6 @@ int launch_decode_gemvs_tma(const DecodeParams& P, cudaStream_t stream) {
   const int64_t max_seg = max_segments(P.R, P.E, P.Ts, P.has_shared);
   const DecodePlan plan = decode_tile_plan(P.R_plan > 0 ? P.R_plan : P.R, P.E, P.Ts,
                                            P.has_shared, P.H, P.I, sm_count());
-  if (P.fused && plan.fused) {  // a few routes: gate_up and down in one launch
-    FusedMaps M;
-    int st = make_maps<kGateUp>(P, 128, false, &M.gu);
-    if (!st) st = make_maps<kDown>(P, 128, false, &M.dn);
-    if (st) return st;
-    constexpr Layout L = make_layout(1, 8, 8, 2);
-    cudaError_t err = cudaFuncSetAttribute(k_gemv_fused<8>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, L.total);
-    if (err != cudaSuccess) return cuda_status(err);
-    const int64_t tiles = max_seg * (2 * (int64_t)P.I + P.H) / 128;
-    int64_t grid = 2 * (int64_t)sm_count();
-    if (tiles < grid) grid = tiles;
-    prof_mark(FTB_KERNEL_GATE_UP, true, stream);
-    err = launch_pdl(k_gemv_fused<8>, dim3((unsigned)grid), dim3(9 * kWarp), (size_t)L.total,
-                     stream, P, M);
-    prof_mark(FTB_KERNEL_GATE_UP, false, stream);
-    return cuda_status(err);
-  }
   const bool gather = plan.gather_x && P.xs;
   if (gather) {
     const int st = cuda_status(launch_pdl(k_gather_x, dim3((unsigned)max_seg), dim3(256), 0,

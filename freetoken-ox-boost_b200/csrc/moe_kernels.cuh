@@ -195,11 +195,6 @@ struct DecodeParams {
   int32_t* hcount;         // entries of hlist (zeroed per call)
   int32_t* gu_done;        // gate_up CTAs finished (zeroed per call)
   unsigned long long* trace;  // or null: [0] gate_up, [1] down start (min over CTAs, ns)
-  // fused small-T decode (route-major calls): one launch runs the gate_up tiles, then the down
-  // tiles; seg_done[a] counts segment a's finished gate_up warps (zeroed per call) and reaches
-  // kSegReady once its h is final
-  int fused;
-  int32_t* seg_done;
   // expert parallelism: the down GEMV stores route r's output at
   // ic3_home[r / ic3_block] + (r % ic3_block) H (the home rank's buffer, peer memory); 0 = P.ic3
   int ic3_block;
@@ -372,7 +367,6 @@ inline BankView view_dn(const ftb_nvfp4_bank* b, const ftb_nvfp4_bank* s) {
 struct DecodePlan {
   int gate_up_rows;
   int down_rows;
-  int fused;     // a few routes (the route-major front): gate_up and down in one launch
   int gather_x;  // gate_up reads x rows gathered into segment order (xs), by TMA boxes
   int down_box;  // down reads its h rows (already in segment order) by TMA boxes
 };

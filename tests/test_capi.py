@@ -106,7 +106,7 @@ def test_smoke_shape_is_accepted_by_the_library():
     assert plan[0] in (96, 128) and plan[1] == 128
 
 
-@pytest.mark.parametrize("T,want", [(1, (128, 128)), (4, (128, 128)), (16, (128, 128)),
+@pytest.mark.parametrize("T,want", [(1, (96, 128)), (4, (128, 128)), (16, (128, 128)),
                                     (64, (128, 128))])
 def test_decode_plan_config1(T, want):
     """Tile rows of the config-1 decode (H4096 I1536 E256 top-8 + shared) on 148 SMs: the
@@ -115,10 +115,8 @@ def test_decode_plan_config1(T, want):
     assert st == _lib.FTB_OK and plan == want
 
 
-@pytest.mark.parametrize("T", [5, 9])
-def test_decode_plan_config0_few_tiles_use_96_row_tiles(T):
-    """Past the fused small-T launch (more than 32 routes), few tiles: 96-row gate_up tiles."""
-    st, plan = _plan(T, 2048, 768, 64, 8, False)
+def test_decode_plan_config0_t1_uses_96_row_tiles():
+    st, plan = _plan(1, 2048, 768, 64, 8, False)
     assert st == _lib.FTB_OK and plan == (96, 128)
 
 

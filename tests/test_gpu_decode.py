@@ -65,15 +65,13 @@ def test_decode_cfg0_full_router_gemv():
     assert m.max_abs_rel(to_f32(out), f64) <= TOL
 
 
-@pytest.mark.parametrize("T", [5, 9])
-def test_decode_cfg0_96_row_tiles(T):
-    """Config 0 at T=5 and T=9 (40 / 72 routes of 64 experts, 2I = 1536, few tiles): the
-    gate_up GEMV runs its 96-row work tiles (k_gemv_tma<0,1,6,8> / <0,1,6,16>); every
-    intermediate against the oracle."""
+def test_decode_cfg0_t1_96_row_tiles():
+    """Config 0 at T=1 (8 routes of 64 experts, 2I = 1536): the gate_up GEMV runs its 96-row
+    work tiles (k_gemv_tma<0,1,6>); every intermediate against the oracle."""
     from ftb.fused_nvfp4 import decode_plan
 
-    assert decode_plan(T, 2048, 768, 64, 8, False) == (96, 128)
-    case = build_case(64, 2048, 768, T, 8, seed=5, shared=False)
+    assert decode_plan(1, 2048, 768, 64, 8, False) == (96, 128)
+    case = build_case(64, 2048, 768, 1, 8, seed=5, shared=False)
     ref = oracle_layer(case)
     out, it = run_gpu(case)
     torch.cuda.synchronize()

@@ -1,9 +1,8 @@
 """GPU parity at the BASELINE config-1 shape (H=4096, I=1536, 256 experts, top-8, shared
 expert) at every config-1 token count, T in {1, 4, 16, 64}. Each T asserts the decode GEMVs'
 work-tile plan, so every tile variant the library can launch at this shape is checked here:
-the fused small-T launch (gate_up and down tiles in one kernel, 128-row tiles, 8 activation
-rows per stage) at T=1 and T=4, 128-row tiles (16 rows per stage) at T=16 and 64, with segments
-of one and of two n-tiles of routes at T=64.
+96-row gate_up tiles at T=1, 128-row tiles (8 activation rows per stage) at T=4, 128-row tiles
+(16 rows per stage) at T=16 and 64, with segments of one and of two n-tiles of routes at T=64.
 Activation boxes (segments of >= 6 routes, gathered x rows) are covered by
 test_gpu_decode_boxes.py.
 
@@ -86,7 +85,7 @@ def layer():
     return bank, shared
 
 
-PLANS = {1: (128, 128), 4: (128, 128), 16: (128, 128), 64: (128, 128)}
+PLANS = {1: (96, 128), 4: (128, 128), 16: (128, 128), 64: (128, 128)}
 
 
 @pytest.mark.parametrize("T", [1, 4, 16, 64])

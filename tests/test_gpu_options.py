@@ -65,8 +65,8 @@ def test_router_weight_on_input(path):
     assert compare(to_f32(it["ic1"]), plain["ic1"])[0] > 0.05
 
 
-def _big_token_case(T, hot, scale, seed, shared=True, E=8):
-    case = build_case(E, 256, 256, T, 2, seed=seed, shared=shared)
+def _big_token_case(T, hot, scale, seed, shared=True):
+    case = build_case(8, 256, 256, T, 2, seed=seed, shared=shared)
     x = case["inp"].x.clone()
     x[hot] = (x[hot].float() * scale).to(torch.bfloat16)  # power of two: exact in bf16
     case["inp"] = synth.Inputs(x, case["inp"].logits)
@@ -83,22 +83,6 @@ def test_h_beyond_f16_range_one_token(path):
     _check(out, it, ref, ("ic1", "h", "ic3", "shared_h", "shared_out"))
     # the other tokens' outputs are unaffected (compare them on their own scale)
     keep = [t for t in range(9) if t != 4]
-    rel, _ = compare(to_f32(out)[keep], ref["out"][keep])
-    assert rel <= TOL, rel
-
-
-def test_h_beyond_f16_range_fused_small_t():
-    """At a few tokens (8 routes over 16 experts: one route per segment) gate_up and down run in
-    one launch; a segment's rescaled h rows are rewritten before its down tiles read them."""
-    from ftb.fused_nvfp4 import decode_plan
-
-    case = _big_token_case(4, [1], 4096.0, 64, E=16)
-    ref = oracle_layer(case)
-    assert np.abs(ref["h"][1]).max() > 1e5 and np.abs(ref["shared_h"][1]).max() > 1e5
-    assert decode_plan(4, 256, 256, 16, 2, True) == (128, 128)
-    out, it = _run("decode", case)
-    _check(out, it, ref, ("ic1", "h", "ic3", "shared_h", "shared_out"))
-    keep = [t for t in range(4) if t != 1]
     rel, _ = compare(to_f32(out)[keep], ref["out"][keep])
     assert rel <= TOL, rel
 

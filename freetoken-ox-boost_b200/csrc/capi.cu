@@ -246,6 +246,11 @@ static int layer_impl(const ftb_moe_args& a, cudaStream_t stream) {
   dp.h_quant = a.h_quant;
   dp.topk_w = a.topk_w;
   dp.topk_ids = a.topk_ids;
+  if (sp.route_major) {  // the segment table route_major_block writes
+    dp.rm_segments = R + (run_shared ? ceil_div(T, (int64_t)kSegRoutes) : 0);
+    dp.rm_ts = run_shared ? T : 0;
+    dp.route_mask = a.route_mask;
+  }
   dp.sorted = w.sorted;
   dp.seg_expert = w.seg_expert;
   dp.seg_off = w.seg_off;

@@ -14,11 +14,13 @@
 //   activations  XR x 512 B   the segment's f16 rows for these 256 k (per-row bulk copies,
 //                             pitch 576 B; XR = 8 when T <= 8, else 16), in the
 //                             round-interleaved layout below.
-// One producer warp claims tiles from a launch-wide counter and fills an S-stage ring
-// (mbarrier full/empty, bounded waits). Eight consumer warps all read every stage: warp w
-// owns G m16 tiles (16G rows) of the tile for the whole K and keeps their fp32 accumulators
-// in registers, so a tile needs no cross-warp reduction; its epilogue runs straight from
-// registers after the last stage (which the warp has already released to the producer).
+// One producer warp claims tiles from a launch-wide counter (route-major launches: a fixed
+// order, and the first tile's weights are requested before the dependency wait) and fills
+// an S-stage ring (mbarrier full/empty, bounded waits). Eight consumer warps all read every
+// stage: warp w owns G m16 tiles (16G rows) of the tile for the whole K and keeps their fp32
+// accumulators in registers, so a tile needs no cross-warp reduction; its epilogue runs
+// straight from registers after the last stage (which the warp has already released to the
+// producer).
 //
 // Inner loop, per warp and 128-k round: the activation fragments (B of mma.m16n8k16, f16,
 // 8 routes per n-tile) are loaded once and reused for the warp's G m16 tiles; per m16 tile a
@@ -158,6 +160,46 @@ __device__ __forceinline__ int tile_rows_total(const DecodeParams& P) {
   return MODE == kGateUp ? 2 * P.I : P.H;
 }
 
+// Route-major launches (DecodeParams::rm_segments > 0): segment a's expert, first sorted
+// position and route count, computed from the top-k ids as route_major_block computes them
+// (L2 loads: this runs before the dependency wait too).
+struct Seg {
+  int e, off, cnt;
+};
+__device__ __forceinline__ Seg rm_segment(const DecodeParams& P, int a) {
+  if (a < P.R) {
+    const int e = __ldcg(P.topk_ids + a);
+    const bool on =
+        !P.route_mask || __ldcg(reinterpret_cast<const signed char*>(P.route_mask) + a) != 0;
+    const bool ok = on && e >= 0 && e < P.E;
+    return Seg{ok ? e : 0, a, ok ? 1 : 0};
+  }
+  const int64_t j = a - P.R;
+  return Seg{P.E, (int)(P.R + j * kSegRoutes),
+             (int)min((int64_t)kSegRoutes, P.rm_ts - j * kSegRoutes)};
+}
+
+// The weight and scale boxes of stage kc of row block p of expert e (e == P.E: the shared
+// expert), completing on `full`.
+template <int MODE>
+__device__ __forceinline__ void issue_weights(const DecodeParams& P, const GemvMaps& M,
+                                              const Layout& L, uint8_t* st, uint64_t* full,
+                                              int e, int p, int kc) {
+  const uint32_t bar = smem_u32(full);
+  const bool sh = e == P.E;
+  const CUtensorMap* wm = sh ? &M.sw : &M.w;
+  const CUtensorMap* sm = sh ? &M.ss : &M.s;
+  if (MODE == kGateUp) {
+    const int h = L.RT / 2, z = sh ? 0 : 2 * e;
+    tma_3d(smem_u32(st), wm, kc * 128, h * p, z, bar);
+    tma_3d(smem_u32(st + L.s_off), sm, kc * 16, h * p, z, bar);
+  } else {
+    const int y = (sh ? 0 : e * tile_rows_total<MODE>(P)) + L.RT * p;
+    tma_2d(smem_u32(st), wm, kc * 128, y, bar);
+    tma_2d(smem_u32(st + L.s_off), sm, kc * 16, y, bar);
+  }
+}
+
 // Producer warp: claims tiles, and for each stage of a tile waits for the slot to be free,
 // arms the full barrier with the stage's byte count, publishes the tile id and issues the
 // copies (lane 0: the TMA boxes; lanes j < cnt: activation row j, or lane 0 the activation
@@ -261,6 +303,101 @@ __device__ void producer(const DecodeParams& P, const GemvMaps& M, const Layout&
   // must land before the CTA exits. (Without an abort every issued stage was consumed.)
   if (lane != 0 || (!aborted && !*sy.abort)) return;
   const int64_t issued = i;
+  for (int64_t j = issued - L.stages > 0 ? issued - L.stages : 0; j < issued; ++j) {
+    const int s = (int)(j % L.stages);
+    for (uint32_t it = 0; it < kSpinLimit; ++it) {
+      if (mbar_try_wait(&sy.full[s], (uint32_t)(j / L.stages) & 1u)) break;
+      __nanosleep(64);
+    }
+  }
+}
+
+// Producer warp of a route-major launch (per-route activation copies; every tile costs the
+// same, one route): tiles in the fixed order blockIdx.x, + gridDim.x, ..., and the first
+// tile's weight copies (up to L.stages stages) issued before the dependency wait, so they
+// stream while the front finishes (gate_up) or while gate_up's last CTAs finish (down). The
+// stage protocol is producer()'s; an early stage's full barrier gets its weight bytes by
+// expect_tx first and the activation bytes with the arrival.
+template <int MODE>
+__device__ void producer_rm(const DecodeParams& P, const GemvMaps& M, const Layout& L,
+                            uint8_t* stages, const Sync& sy, int tpe, int nk) {
+  const int lane = threadIdx.x & 31;
+  const int K = MODE == kGateUp ? P.H : P.I;
+  const int64_t ntiles = P.rm_segments * tpe;
+  int early = 0;  // stages of the first tile whose weights are already in flight
+  if ((int64_t)blockIdx.x < ntiles) {
+    const int64_t t = blockIdx.x;
+    const Seg g = rm_segment(P, (int)(t / tpe));
+    if (g.cnt > 0) {
+      early = nk < L.stages ? nk : L.stages;
+      if (lane == 0)
+        for (int kc = 0; kc < early; ++kc) {
+          mbar_expect_tx(&sy.full[kc], (uint32_t)(L.wbytes + L.sbytes));
+          issue_weights<MODE>(P, M, L, stages + (size_t)kc * L.stage_bytes, &sy.full[kc], g.e,
+                              (int)(t % tpe), kc);
+        }
+    }
+  }
+  pdl_wait();  // activations (x16 / h16) come from earlier launches
+  int64_t i = 0;
+  bool aborted = false;
+  for (int64_t j = 0;; ++j) {
+    int64_t t = (int64_t)blockIdx.x + j * gridDim.x;
+    if (t >= ntiles) t = -1;
+    int cnt = 0, e = 0, p = 0;
+    const uint16_t* xsrc = nullptr;  // lane j's activation row (j < cnt)
+    if (t >= 0) {
+      p = (int)(t % tpe);
+      const Seg g = rm_segment(P, (int)(t / tpe));
+      e = g.e;
+      cnt = g.cnt;
+      if (cnt == 0) continue;  // a skipped route
+      if (lane < cnt) {
+        if (MODE == kGateUp) {
+          const int r = P.sorted[g.off + lane];
+          const int64_t tok = e == P.E ? (int64_t)r - P.R : (int64_t)r / P.top_k;
+          xsrc = reinterpret_cast<const uint16_t*>(P.x16) + tok * P.H;
+        } else {
+          xsrc = reinterpret_cast<const uint16_t*>(P.h16) + (int64_t)(g.off + lane) * P.I;
+        }
+      }
+    }
+    const int nstage = t >= 0 ? nk : 1;
+    for (int kc = 0; kc < nstage; ++kc, ++i) {
+      const int s = (int)(i % L.stages);
+      const int64_t round = i / L.stages;
+      const int kk = K - kc * kStageK < kStageK ? K - kc * kStageK : kStageK;
+      const int xbytes = kk * 2;
+      const bool pre = j == 0 && kc < early;  // weights issued before the wait
+      int go = 1;
+      if (lane == 0) {
+        if (round > 0 && !sy.wait(&sy.empty[s], (uint32_t)(round - 1) & 1u)) {
+          go = -1;
+        } else {
+          sy.tile_of[s] = t;
+          if (t < 0)
+            mbar_arrive(&sy.full[s]);  // sentinel: no bytes
+          else
+            mbar_arrive_expect_tx(&sy.full[s],
+                                  (uint32_t)((pre ? 0 : L.wbytes + L.sbytes) + cnt * xbytes));
+        }
+      }
+      go = __shfl_sync(0xffffffffu, go, 0);
+      if (go < 0) {
+        aborted = true;
+        break;
+      }
+      if (t < 0) continue;
+      uint8_t* st = stages + (size_t)s * L.stage_bytes;
+      if (lane == 0 && !pre) issue_weights<MODE>(P, M, L, st, &sy.full[s], e, p, kc);
+      if (lane < cnt)
+        bulk_g2s(st + L.x_off + lane * kXPitch, xsrc + (int64_t)kc * kStageK, xbytes,
+                 &sy.full[s]);
+    }
+    if (aborted || t < 0) break;
+  }
+  if (lane != 0 || (!aborted && !*sy.abort)) return;
+  const int64_t issued = i;  // drain, as producer()
   for (int64_t j = issued - L.stages > 0 ? issued - L.stages : 0; j < issued; ++j) {
     const int s = (int)(j % L.stages);
     for (uint32_t it = 0; it < kSpinLimit; ++it) {
@@ -532,7 +669,7 @@ __host__ __device__ constexpr bool box_ok(const Layout& L, int XR) {
   return XR == kSegRoutes && L.x_off % 1024 == 0 && XR * kXPitch >= kXBoxStageBytes;
 }
 
-template <int MODE, int MT, int NW, int XR, int CPS, bool BOX>
+template <int MODE, int MT, int NW, int XR, int CPS, bool BOX, bool RM>
 __global__ void __launch_bounds__((NW + 1) * kWarp, CPS)
     k_gemv_tma(const __grid_constant__ DecodeParams P, const __grid_constant__ GemvMaps M) {
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -559,15 +696,21 @@ __global__ void __launch_bounds__((NW + 1) * kWarp, CPS)
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&M.s)) : "memory");
   }
   __syncthreads();
-  pdl_wait();  // the segment table, activations and work counter come from earlier launches
+  // the segment table, activations and work counter come from earlier launches (a route-major
+  // producer waits itself, after its first weight copies)
+  if (!RM || warp != NW) pdl_wait();
   if (P.trace && threadIdx.x == 0) trace_start(P.trace + MODE);
   const Sync sy{full, empty, tile_of, abort_flag, P.status};
   const int K = MODE == kGateUp ? P.H : P.I;
   const int nk = (K + kStageK - 1) / kStageK;
   const int tpe = tile_rows_total<MODE>(P) / L.RT;
-  const int64_t ntiles = (int64_t)(*P.n_seg) * tpe;
   if (warp == NW) {
-    producer<MODE, BOX>(P, M, L, stages, sy, ntiles, tpe, nk, P.work_counter + MODE);
+    if constexpr (RM) {
+      producer_rm<MODE>(P, M, L, stages, sy, tpe, nk);
+    } else {
+      const int64_t ntiles = (int64_t)(*P.n_seg) * tpe;
+      producer<MODE, BOX>(P, M, L, stages, sy, ntiles, tpe, nk, P.work_counter + MODE);
+    }
     return;
   }
   int64_t i = 0;
@@ -778,20 +921,20 @@ int make_maps(const DecodeParams& P, int RT, bool xbox, GemvMaps* M) {
   return st;
 }
 
-template <int MODE, int MT, int NW, int XR, int CPS, bool BOX>
+template <int MODE, int MT, int NW, int XR, int CPS, bool BOX, bool RM = false>
 int launch_one(const DecodeParams& P, int64_t est_tiles, cudaStream_t stream) {
   constexpr Layout L = make_layout(MT, NW, XR, CPS);
   static_assert(L.stages >= 2, "at least two stages per CTA");
   GemvMaps M;
   int st = make_maps<MODE>(P, L.RT, BOX, &M);
   if (st) return st;
-  cudaError_t err = cudaFuncSetAttribute(k_gemv_tma<MODE, MT, NW, XR, CPS, BOX>,
+  cudaError_t err = cudaFuncSetAttribute(k_gemv_tma<MODE, MT, NW, XR, CPS, BOX, RM>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, L.total);
   if (err != cudaSuccess) return cuda_status(err);
   int64_t grid = (int64_t)CPS * sm_count();
   if (est_tiles < grid) grid = est_tiles;
   if (grid < 1) grid = 1;
-  return cuda_status(launch_pdl(k_gemv_tma<MODE, MT, NW, XR, CPS, BOX>, dim3((unsigned)grid),
+  return cuda_status(launch_pdl(k_gemv_tma<MODE, MT, NW, XR, CPS, BOX, RM>, dim3((unsigned)grid),
                                 dim3((NW + 1) * kWarp), (size_t)L.total, stream, P, M));
 }
 
@@ -800,25 +943,41 @@ int launch_one(const DecodeParams& P, int64_t est_tiles, cudaStream_t stream) {
 // measured 4-5% faster than one 256-row CTA per SM at 2.25 to 16 routes per expert); 8
 // activation rows per stage when T <= 8 (no segment holds more routes).
 // box: activation boxes (128-row tiles with kSegRoutes rows per stage only).
+template <int MODE, bool RM>
+int launch_rows_t(const DecodeParams& P, int rows, int64_t tiles, bool box, cudaStream_t stream) {
+  const bool x8 = P.T <= 8;
+  switch (rows) {
+    case 128:
+      if constexpr (!RM)
+        if (box) return launch_one<MODE, 1, 8, kSegRoutes, 2, true>(P, tiles, stream);
+      return x8 ? launch_one<MODE, 1, 8, 8, 2, false, RM>(P, tiles, stream)
+                : launch_one<MODE, 1, 8, kSegRoutes, 2, false, RM>(P, tiles, stream);
+    case 96:
+      if constexpr (MODE == kGateUp)
+        if (!box)
+          return x8 ? launch_one<MODE, 1, 6, 8, 2, false, RM>(P, tiles, stream)
+                    : launch_one<MODE, 1, 6, kSegRoutes, 2, false, RM>(P, tiles, stream);
+      return FTB_ERR_SHAPE;
+    default: return FTB_ERR_SHAPE;
+  }
+}
+
+// One launch of the chosen tile rows: 128-row tiles (8 consumer warps) or, for gate_up at
+// small T, 96-row tiles; two CTAs per SM (twice the copies in flight per SM; 128-row tiles
+// measured 4-5% faster than one 256-row CTA per SM at 2.25 to 16 routes per expert); 8
+// activation rows per stage when T <= 8 (no segment holds more routes).
+// box: activation boxes (128-row tiles with kSegRoutes rows per stage only; never with a
+// route-major front, whose segments hold one route each).
 template <int MODE>
 int launch_rows(const DecodeParams& P, int rows, int64_t max_seg, bool box,
                 cudaStream_t stream) {
   const int64_t per_e = MODE == kGateUp ? 2 * (int64_t)P.I : P.H;
   const int64_t tiles = max_seg * (per_e / rows);
-  const bool x8 = P.T <= 8;
-  switch (rows) {
-    case 128:
-      if (box) return launch_one<MODE, 1, 8, kSegRoutes, 2, true>(P, tiles, stream);
-      return x8 ? launch_one<MODE, 1, 8, 8, 2, false>(P, tiles, stream)
-                : launch_one<MODE, 1, 8, kSegRoutes, 2, false>(P, tiles, stream);
-    case 96:
-      if constexpr (MODE == kGateUp)
-        if (!box)
-          return x8 ? launch_one<MODE, 1, 6, 8, 2, false>(P, tiles, stream)
-                    : launch_one<MODE, 1, 6, kSegRoutes, 2, false>(P, tiles, stream);
-      return FTB_ERR_SHAPE;
-    default: return FTB_ERR_SHAPE;
+  if (P.rm_segments > 0) {
+    if (box) return FTB_ERR_SHAPE;
+    return launch_rows_t<MODE, true>(P, rows, tiles, false, stream);
   }
+  return launch_rows_t<MODE, false>(P, rows, tiles, box, stream);
 }
 
 // x rows into segment order for the gate_up's activation boxes: block a copies the rows of

@@ -171,6 +171,15 @@ struct DecodeParams {
                            // fp32 activation in h16 / hb for launch_h_fp8)
   const float* topk_w;     // [R]
   const int32_t* topk_ids; // [R]
+  // Route-major front (rm_segments > 0): segment a < R is route a (expert topk_ids[a], one
+  // route; none when route_mask[a] == 0 or the id is out of range), segments R.. hold the
+  // shared expert's rm_ts tokens, kSegRoutes each. The GEMV producers derive a tile's expert
+  // from this, not from the segment table, and issue its first stages' weight copies before
+  // the dependency wait: the front triggers its dependents only after its own wait, so the
+  // ids are complete by the time a GEMV launches.
+  int64_t rm_segments;
+  int64_t rm_ts;
+  const int8_t* route_mask;
   // sort results
   const int32_t* sorted;
   const int32_t* seg_expert;

@@ -363,8 +363,11 @@ __device__ void ep_front(const SortParams& P, int* hist) {
 
 __global__ void __launch_bounds__(kSortThreads) k_sort_stage(SortParams P) {
   extern __shared__ int hist[];
-  pdl_launch_dependents();
+  // A route-major front triggers its dependents only once its predecessors (the router) are
+  // complete: the GEMVs then read the top-k ids before their own wait (DecodeParams::rm_*).
+  if (!P.route_major) pdl_launch_dependents();
   pdl_wait();
+  if (P.route_major) pdl_launch_dependents();
   if (P.ep.world > 0) {
     ep_front(P, hist);
   } else if (blockIdx.x == 0) {

@@ -24,11 +24,14 @@
 //              from shared to tensor memory in the layout the MMA reads (row 32g + r of a
 //              32-row group g at lane r of every quarter, column g, byte = k block), then
 //              arrive on the stage's scale barrier;
-//   warps 6-13 epilogue, two per lane quarter on alternate 16-column chunks (the items' route
-//              metadata loaded into shared memory before the accumulator wait): tcgen05.ld, then the decode
-//              path's arithmetic with the activation globals in place of the power-of-two x
-//              scales (gate_up -> bf16 ic1, activation -> f16 h in sorted order; down ->
-//              bf16(acc x gh x global x routed weight) per route).
+//   warps 6-13 epilogue, two per lane quarter on alternate 16-column chunks: before the
+//              accumulator wait each warp loads a 20-column slice of the item's route
+//              metadata into the accumulator buffer's shared copy (one round of loads, not
+//              eight warps each loading all 160 columns: the down GEMM was bound by that), then
+//              tcgen05.ld and the decode path's arithmetic with the activation globals in
+//              place of the power-of-two x scales (gate_up -> bf16 ic1, activation -> f16 h in
+//              sorted order; down -> bf16(acc x gh x global x routed weight) per route, the
+//              chunk's 16 columns of metadata read into registers first).
 // Every wait is bounded; a timeout raises the CTA abort flag and kStatusTimeout; the MMA warp
 // waits for its MMAs and the producer for its copies before the CTA leaves.
 #include <cuda.h>
@@ -53,7 +56,8 @@ constexpr int kF4Rows = 128;           // MMA M (one CTA)
 constexpr int kF4StgK = 256;           // k per stage: 128 bytes of codes per row
 constexpr int kF4MmaK = 64;            // k per MMA
 constexpr int kF4MaxN = kPrefillSegRoutes;  // 160
-constexpr int kF4Stages = 4;
+constexpr int kF4Stages = 4;    // shared-memory stages
+constexpr int kF4SfSlots = 4;   // tensor-memory scale slots (stage i uses slot i % kF4SfSlots)
 constexpr int kF4ABytes = kF4Rows * 128;             // 16384
 constexpr int kF4SfaBytes = kF4Rows * 16;            // 2048
 constexpr int kF4BBytes = kF4MaxN * 128;             // 20480
@@ -67,7 +71,7 @@ constexpr int kF4Header = 16384;
 constexpr int kF4Smem = kF4Header + kF4Stages * kF4StageBytes;
 static_assert(kF4BOff % 1024 == 0 && kF4StageBytes % 1024 == 0, "1024-B swizzle atoms");
 static_assert(kF4Smem <= 227 * 1024, "shared memory");
-// tensor memory: two accumulators of kF4MaxN fp32 columns, then per stage a scale slot of
+// tensor memory: two accumulators of kF4MaxN fp32 columns, then kF4SfSlots scale slots of
 // 16 SFA columns (4 MMAs x 4 row groups) and 4 SFB regions of 8 columns (up to 5 row groups of
 // 32 routes used). Every tcgen05 access starts at a column that is a multiple of its width:
 // slots at multiples of 16, SFB regions at multiples of 8.
@@ -77,7 +81,9 @@ constexpr int kF4SfSlot = 16 + 4 * kF4SfbStride;    // 48
 constexpr int kF4TmemSf = 2 * kF4MaxN;              // 320
 static_assert(kF4SfbGroups <= kF4SfbStride && kF4TmemSf % 16 == 0 && kF4SfSlot % 16 == 0,
               "aligned scale regions");
-static_assert(kF4TmemSf + kF4Stages * kF4SfSlot <= 512, "tensor memory budget");
+static_assert(kF4TmemSf + kF4SfSlots * kF4SfSlot <= 512, "tensor memory budget");
+static_assert(kF4SfSlots <= kF4Stages, "a slot is free once the MMAs of stage i - kF4SfSlots "
+              "are complete");
 constexpr int kF4EpiWarps = 8;  // two per tensor-memory lane quarter, alternate 16-column chunks
 constexpr int kF4Warps = 6 + kF4EpiWarps;
 constexpr int kF4WarpTma = 0, kF4WarpMma = 1, kF4WarpSf = 2, kF4WarpEpi = 6;
@@ -87,16 +93,17 @@ enum { kGateUp = 0, kDown = 1 };
 struct F4Shared {
   uint64_t full[kF4Stages], empty[kF4Stages], sf_full[kF4Stages];
   uint64_t full_d[2], empty_d[2];
+  uint64_t meta_full[2];  // the epilogue warps' slices of an item's column metadata written
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
   int last;
-  // per epilogue warp, the current item's columns: route id (-1 past the segment), the
-  // activation global (times the routed weight where it applies) and, for gate_up with the
-  // weight on the input, the routed weight
-  int col_r[kF4EpiWarps][kF4MaxN];
-  float col_f[kF4EpiWarps][kF4MaxN];
-  float col_w[kF4EpiWarps][kF4MaxN];
+  // the columns of the item in accumulator buffer b: route id (-1 past the segment), the
+  // activation global and the routed weight where it applies (1 elsewhere); written by the
+  // eight epilogue warps, a slice each, read by all of them
+  alignas(16) int col_r[2][kF4MaxN];
+  alignas(16) float col_f[2][kF4MaxN];
+  alignas(16) float col_w[2][kF4MaxN];
 };
 static_assert(sizeof(F4Shared) <= kF4Header, "header");
 
@@ -205,6 +212,25 @@ __device__ __forceinline__ void f4_tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 16 consecutive int / float values from shared memory (16-byte aligned), for the epilogue's
+// column metadata: one broadcast load per four columns.
+__device__ __forceinline__ void lds16_i(const int* p, int (&v)[16]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v[4 * i]), "=r"(v[4 * i + 1]), "=r"(v[4 * i + 2]), "=r"(v[4 * i + 3])
+                 : "r"(smem_u32(p + 4 * i))
+                 : "memory");
+}
+__device__ __forceinline__ void lds16_f(const float* p, float (&v)[16]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v[4 * i]), "=f"(v[4 * i + 1]), "=f"(v[4 * i + 2]), "=f"(v[4 * i + 3])
+                 : "r"(smem_u32(p + 4 * i))
+                 : "memory");
+}
+
 struct F4Item {
   int e, off, cnt, mt, n;  // expert (E = shared), segment start / size, weight tile, MMA N
   bool sh;
@@ -285,25 +311,39 @@ __device__ void f4_sf_warp(uint8_t* smem, const F4Sync& sy, int64_t n_items, int
   for (int64_t i = 0; i < nstages; ++i) {
     const int s = (int)(i % kF4Stages);
     if (!sy.wait(&sh->full[s], (uint32_t)(i / kF4Stages) & 1u)) return;
+    // the scale slot of stage i was last read by the MMAs of stage i - kF4SfSlots: wait for
+    // their completion (the commit on that stage's empty barrier; its next phase needs this
+    // warp's stage i + 1, so the parity cannot alias)
+    if (i >= kF4SfSlots) {
+      const int64_t j = i - kF4SfSlots;
+      if (!sy.wait(&sh->empty[j % kF4Stages], (uint32_t)(j / kF4Stages) & 1u)) return;
+    }
     const uint8_t* st = smem + kF4Header + (size_t)s * kF4StageBytes;
-    const uint32_t col = sh->tmem_base + (q << 21) + (uint32_t)(kF4TmemSf + s * kF4SfSlot);
+    const uint32_t col =
+        sh->tmem_base + (q << 21) + (uint32_t)(kF4TmemSf + (i % kF4SfSlots) * kF4SfSlot);
+    // one 16-byte read per row (its 16 k-block scales of the stage: word m = MMA step m)
     uint32_t a[16];
 #pragma unroll
-    for (int m = 0; m < 4; ++m)
-#pragma unroll
-      for (int g = 0; g < 4; ++g)
-        a[4 * m + g] =
-            *reinterpret_cast<const uint32_t*>(st + kF4SfaOff + (32 * g + lane) * 16 + 4 * m);
+    for (int g = 0; g < 4; ++g) {
+      const uint4 v = *reinterpret_cast<const uint4*>(st + kF4SfaOff + (32 * g + lane) * 16);
+      a[g] = v.x;
+      a[4 + g] = v.y;
+      a[8 + g] = v.z;
+      a[12 + g] = v.w;
+    }
     f4_tmem_st16(col, a);
+    uint4 bv[kF4SfbGroups];
+#pragma unroll
+    for (int g = 0; g < kF4SfbGroups; ++g)
+      bv[g] = *reinterpret_cast<const uint4*>(st + kF4SfbOff + (32 * g + lane) * 16);
 #pragma unroll
     for (int m = 0; m < 4; ++m) {
       uint32_t b[4];
 #pragma unroll
       for (int g = 0; g < 4; ++g)
-        b[g] = *reinterpret_cast<const uint32_t*>(st + kF4SfbOff + (32 * g + lane) * 16 + 4 * m);
+        b[g] = m == 0 ? bv[g].x : m == 1 ? bv[g].y : m == 2 ? bv[g].z : bv[g].w;
       f4_tmem_st4(col + 16 + (uint32_t)(kF4SfbStride * m), b);
-      const uint32_t b4 =
-          *reinterpret_cast<const uint32_t*>(st + kF4SfbOff + (32 * 4 + lane) * 16 + 4 * m);
+      const uint32_t b4 = m == 0 ? bv[4].x : m == 1 ? bv[4].y : m == 2 ? bv[4].z : bv[4].w;
       asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(
                        col + 16 + (uint32_t)(kF4SfbStride * m + 4)),
                    "r"(b4)
@@ -341,7 +381,7 @@ __device__ void f4_mma_warp(const DecodeParams& P, uint8_t* smem, const F4Sync& 
       f4_fence_after();
       const uint64_t a0 = desc0 + (uint64_t)((s * kF4StageBytes) >> 4);
       const uint64_t b0 = desc0 + (uint64_t)((s * kF4StageBytes + kF4BOff) >> 4);
-      const uint32_t sf = tbase + (uint32_t)(kF4TmemSf + s * kF4SfSlot);
+      const uint32_t sf = tbase + (uint32_t)(kF4TmemSf + (i % kF4SfSlots) * kF4SfSlot);
 #pragma unroll
       for (int m = 0; m < kF4StgK / kF4MmaK; ++m)
         f4_mma(d, a0 + (uint64_t)(m * 2), b0 + (uint64_t)(m * 2), idesc, sf + (uint32_t)(4 * m),
@@ -370,17 +410,20 @@ __device__ void f4_epilogue(const DecodeParams& P, const F4Sync& sy, int64_t n_i
   const int q = warp & 3;                  // tensor-memory lane quarter
   const int ew = warp - kF4WarpEpi;        // this warp's metadata slice
   const int half = ew >> 2;                // its 16-column chunks: 16 half + 32 i
-  int* col_r = sh->col_r[ew];
-  float* col_f = sh->col_f[ew];
-  float* col_w = sh->col_w[ew];
+  constexpr int kSlice = kF4MaxN / kF4EpiWarps;
+  static_assert(kF4MaxN % kF4EpiWarps == 0 && kSlice <= kWarp, "one column per lane");
   const uint32_t tbase = sh->tmem_base + ((uint32_t)(32 * q) << 16);
   uint32_t di = 0;
   for (int64_t it = blockIdx.x; it < n_items; it += gridDim.x) {
     const F4Item im = f4_item<MODE>(P, it, mtiles);
-    // the item's column metadata, loaded while its MMAs run
-#pragma unroll
-    for (int k = 0; k < kF4MaxN / kWarp; ++k) {
-      const int n = lane + kWarp * k;
+    const int buf = (int)(di & 1);
+    const uint32_t par = (di >> 1) & 1u;
+    // The item's column metadata, loaded while its MMAs run: this warp's slice into the
+    // buffer's shared copy, once every epilogue warp is done with the item that used the
+    // buffer before (its arrival on empty_d), then wait for the other slices.
+    if (di >= 2 && !sy.wait(&sh->empty_d[buf], par ^ 1u)) return;
+    if (lane < kSlice) {
+      const int n = kSlice * ew + lane;
       int r = -1;
       float f = 1.f, wr = 1.f;
       if (n < im.cnt) {
@@ -393,14 +436,18 @@ __device__ void f4_epilogue(const DecodeParams& P, const F4Sync& sy, int64_t n_i
           if (!im.sh && !P.w_on_input) wr = P.topk_w[r];
         }
       }
-      col_r[n] = r;
-      col_f[n] = f;
-      col_w[n] = wr;
+      sh->col_r[buf][n] = r;
+      sh->col_f[buf][n] = f;
+      sh->col_w[buf][n] = wr;
     }
     __syncwarp();
-    const int buf = (int)(di & 1);
-    if (!sy.wait(&sh->full_d[buf], (di >> 1) & 1u)) return;
+    if (lane == 0) mbar_arrive(&sh->meta_full[buf]);
+    if (!sy.wait(&sh->meta_full[buf], par)) return;
+    if (!sy.wait(&sh->full_d[buf], par)) return;
     f4_fence_after();
+    const int* col_r = sh->col_r[buf];
+    const float* col_f = sh->col_f[buf];
+    const float* col_w = sh->col_w[buf];
     const uint32_t taddr = tbase + (uint32_t)(buf * kF4MaxN);
     if (MODE == kGateUp) {
       const int I = P.I;
@@ -412,6 +459,8 @@ __device__ void f4_epilogue(const DecodeParams& P, const F4Sync& sy, int64_t n_i
       const bool dbg = P.dbg_ic1 || P.dbg_h || P.dbg_sic1 || P.dbg_sh;
       if (P.act.kind == kActSilu && !P.w_on_input && !dbg) {  // the common case, branch-free
         for (int c0 = 16 * half; c0 < im.n; c0 += 32) {
+          // (the column metadata read per pair here: preloading the chunk's 16 columns into
+          // registers, as the other loops do, made this loop 9 % slower)
           float v[16];
           f4_tmem_ld16(taddr + (uint32_t)c0, v);
 #pragma unroll
@@ -430,7 +479,11 @@ __device__ void f4_epilogue(const DecodeParams& P, const F4Sync& sy, int64_t n_i
         }
       } else
       for (int c0 = 16 * half; c0 < im.n; c0 += 32) {
-        float v[16];
+        int rr[16];
+        float ff[16], ww[16], v[16];
+        lds16_i(col_r + c0, rr);
+        lds16_f(col_f + c0, ff);
+        lds16_f(col_w + c0, ww);
         f4_tmem_ld16(taddr + (uint32_t)c0, v);
 #pragma unroll
         for (int p2 = 0; p2 < 8; ++p2) {
@@ -439,14 +492,15 @@ __device__ void f4_epilogue(const DecodeParams& P, const F4Sync& sy, int64_t n_i
           const float own = upper ? v[2 * p2 + 1] : v[2 * p2];
           const float g = upper ? recv : own, u = upper ? own : recv;
           const int n = c0 + 2 * p2 + (upper ? 1 : 0);
-          const int r = col_r[n];
+          const int r = upper ? rr[2 * p2 + 1] : rr[2 * p2];
           if (r < 0) continue;
-          const float gx = col_f[n];
+          const float gx = upper ? ff[2 * p2 + 1] : ff[2 * p2];
           float gv = (g * gx) * glg;
           float uv = (u * gx) * glu;
           if (P.w_on_input) {
-            gv *= col_w[n];
-            uv *= col_w[n];
+            const float wn = upper ? ww[2 * p2 + 1] : ww[2 * p2];
+            gv *= wn;
+            uv *= wn;
           }
           gv = bf16_round(gv);
           uv = bf16_round(uv);
@@ -478,14 +532,16 @@ __device__ void f4_epilogue(const DecodeParams& P, const F4Sync& sy, int64_t n_i
       uint16_t* dst = (im.sh ? P.ic3s : P.ic3) + row;
       const int64_t r0 = im.sh ? P.R : 0;  // shared-expert routes R + t are rows t of ic3s
       for (int c0 = 16 * half; c0 < im.n; c0 += 32) {
-        float v[16];
+        int rr[16];
+        float ff[16], ww[16], v[16];
+        lds16_i(col_r + c0, rr);
+        lds16_f(col_f + c0, ff);
+        lds16_f(col_w + c0, ww);
         f4_tmem_ld16(taddr + (uint32_t)c0, v);
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
-          const int n = c0 + k;
-          const int r = col_r[n];
-          if (r < 0) continue;
-          dst[((int64_t)r - r0) * H] = f32_to_bf16_bits(((v[k] * col_f[n]) * gl) * col_w[n]);
+          if (rr[k] < 0) continue;
+          dst[((int64_t)rr[k] - r0) * H] = f32_to_bf16_bits(((v[k] * ff[k]) * gl) * ww[k]);
         }
       }
     }
@@ -512,6 +568,7 @@ __global__ void __launch_bounds__(kF4Warps * kWarp, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sh->full_d[b], 1);
       mbar_init(&sh->empty_d[b], kF4EpiWarps);
+      mbar_init(&sh->meta_full[b], kF4EpiWarps);
     }
     mbar_init(&sh->drain, 1);
     sh->abort = 0;

@@ -103,18 +103,21 @@ def test_fp4_prefill_vs_emulation(E, T, K, shared):
     assert err < 0.35
 
 
-def test_fp4_prefill_config2_shape_close_to_parity_path():
-    """BASELINE config-2 shape (H=4096, I=1536, 256 experts, top-8, shared expert; 16 and 6 k
-    stages, all 4D tile coordinates of a 256-expert bank): the FP4 path stays within the NVFP4
-    activation error of the parity path, with status 0."""
+@pytest.mark.parametrize("E", [256, 32])
+def test_fp4_prefill_config2_shape_close_to_parity_path(E):
+    """BASELINE config-2 shape (H=4096, I=1536, top-8, shared expert; 16 and 6 k stages): with
+    256 experts all 4D tile coordinates of a full bank; with 32 experts the segments of config 2
+    at T=4096 (128 routes per expert) on a bank of 340 MB. The FP4 path stays within the NVFP4
+    activation error of the parity path, with status 0 (the first call is a warm-up)."""
     from ftb import synth
 
-    E, H, I, K, T = 256, 4096, 1536, 8, 512
+    H, I, K, T = 4096, 1536, 8, 512
     bank = synth.make_bank(E, H, I, seed=33, device=DEV)
     shared = synth.make_shared(H, I, seed=33, device=DEV)
     inp = synth.make_inputs(T, H, E, seed=33, device=DEV)
     w, ids = ftb.fused_topk(inp.x, inp.logits, K, True)
     ref = ftb.moe_prefill(inp.x, bank, w, ids, shared=shared)
+    ftb.moe_prefill_fp4(inp.x, bank, w, ids, shared=shared)
     got, it = ftb.moe_prefill_fp4(inp.x, bank, w, ids, shared=shared, debug=True)
     torch.cuda.synchronize()
     assert it["status"] == 0

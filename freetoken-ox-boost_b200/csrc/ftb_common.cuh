@@ -181,6 +181,25 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// 16 consecutive int / float values from shared memory (16-byte aligned), for the GEMM
+// epilogues' column metadata: one broadcast load per four columns.
+__device__ __forceinline__ void lds16_i(const int* p, int (&v)[16]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v[4 * i]), "=r"(v[4 * i + 1]), "=r"(v[4 * i + 2]), "=r"(v[4 * i + 3])
+                 : "r"(smem_u32(p + 4 * i))
+                 : "memory");
+}
+__device__ __forceinline__ void lds16_f(const float* p, float (&v)[16]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v[4 * i]), "=f"(v[4 * i + 1]), "=f"(v[4 * i + 2]), "=f"(v[4 * i + 3])
+                 : "r"(smem_u32(p + 4 * i))
+                 : "memory");
+}
+
 // Named barrier over `count` threads (ids 1..15; 0 is __syncthreads).
 __device__ __forceinline__ void named_bar(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");

@@ -130,8 +130,8 @@ struct PfShared {
   int abort;
   int last;  // gate_up: this CTA is the launch's last to finish its epilogue
   // epilogue warp w (0..3): route id and factor of each column of its current item
-  int col_r[kEpiWarps][kPrefillSegRoutes];
-  float col_f[kEpiWarps][kPrefillSegRoutes];
+  alignas(16) int col_r[kEpiWarps][kPrefillSegRoutes];  // 16-byte aligned: read 4 at a time
+  alignas(16) float col_f[kEpiWarps][kPrefillSegRoutes];
 };
 static_assert(sizeof(PfShared) <= kPfHeader, "header");
 
@@ -749,15 +749,18 @@ __device__ void pf_epilogue(const DecodeParams& P, const PfSync& sy, int64_t n_i
       uint16_t* out = (im.sh ? P.ic3s : P.ic3) + row;
       const int64_t r0 = im.sh ? P.R : 0;  // shared-expert routes R + t are rows t of ic3s
       for (int c0 = 16 * half; c0 < im.n; c0 += 32) {
-        float v[16];
+        // the chunk's 16 columns of metadata into registers first (one broadcast load per
+        // four columns, not a dependent shared read per element)
+        int rr[16];
+        float ff[16], v[16];
+        lds16_i(col_r + c0, rr);
+        lds16_f(col_f + c0, ff);
         tmem_ld16(taddr + (uint32_t)c0, v);
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const int n = c0 + i;
-          const int r = col_r[n];
-          if (r < 0) continue;
+          if (rr[i] < 0) continue;
           // col_f = routed weight x 2^hshift (shared expert: 2^hshift); x 1.0 is exact
-          out[((int64_t)r - r0) * H] = f32_to_bf16_bits((v[i] * gl) * col_f[n]);
+          out[((int64_t)rr[i] - r0) * H] = f32_to_bf16_bits((v[i] * gl) * ff[i]);
         }
       }
     }

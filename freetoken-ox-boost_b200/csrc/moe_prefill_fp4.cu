@@ -212,25 +212,6 @@ __device__ __forceinline__ void f4_tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// 16 consecutive int / float values from shared memory (16-byte aligned), for the epilogue's
-// column metadata: one broadcast load per four columns.
-__device__ __forceinline__ void lds16_i(const int* p, int (&v)[16]) {
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-    asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(v[4 * i]), "=r"(v[4 * i + 1]), "=r"(v[4 * i + 2]), "=r"(v[4 * i + 3])
-                 : "r"(smem_u32(p + 4 * i))
-                 : "memory");
-}
-__device__ __forceinline__ void lds16_f(const float* p, float (&v)[16]) {
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-    asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
-                 : "=f"(v[4 * i]), "=f"(v[4 * i + 1]), "=f"(v[4 * i + 2]), "=f"(v[4 * i + 3])
-                 : "r"(smem_u32(p + 4 * i))
-                 : "memory");
-}
-
 struct F4Item {
   int e, off, cnt, mt, n;  // expert (E = shared), segment start / size, weight tile, MMA N
   bool sh;
